@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""Benchmark of the differentiable beam search hot path on B200.
+
+Workload (one "step"): the PyTorch `final_scores` autograd path on a batch of
+B=64 examples, T=32 steps, K=8 beams, V=32000 fp32 log-probs (2.1 GB per GPU,
+larger than L2), options eos_token=2, length_penalty_alpha=0.2,
+selected_temperature=0.7: y = final_scores(x); y.sum().backward().
+Logits are 2*N(0,1) plus a Zipf rank bias -1.1*ln(v+1), log_softmax over V,
+generated on the device per example with seed 1_000_003*seed + example.
+
+Metric: log-prob elements per second, B*T*K*V / (forward + backward time).
+
+  * value  -- device-resident inputs, timed with CUDA events, max over ranks.
+  * e2e    -- the same call with the inputs copied from pinned host memory
+              every step and the loss read back.
+  * roofline -- the row scan kernel (the pass that streams every log-prob
+              once) timed live with CUDA events around its launches; its
+              algorithmic bytes are 4*B*T*K*V per launch.
+  * cpu_baseline -- the reference's CPU library (compiled from its source into
+              oracle/_ref) on the same workload, all host threads.
+
+`--impl reference` times only the reference CPU arm (rank 0).
+Multi-GPU (torchrun): every rank runs its own batch (weak scaling, no
+collective on the data path); value = all ranks' elements / max rank time.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "differentiable-beam-search-cuda_b200")
+sys.path.insert(0, os.path.join(PKG, "python"))
+
+METRIC = "log-prob elems/s (B·T·K·V) fwd+sparse bwd; % B200 HBM BW; 1/2/4/8 GPU"
+WORKLOAD = dict(B=64, T=32, K=8, V=32000)
+OPTIONS = dict(beam_size=8, eos_token=2, length_penalty_alpha=0.2, selected_temperature=0.7)
+SEED = 0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic_per_launch():
+    """DRAM bytes per row-scan launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "row_scan_config2.md")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+    return float(m.group(1)) if m else None
+
+
+def make_inputs(torch, B, T, K, V, first_example, device):
+    x = torch.empty((B, T, K, V), dtype=torch.float32, device=device)
+    bias = -1.1 * torch.log(torch.arange(V, dtype=torch.float32, device=device) + 1.0)
+    g = torch.Generator(device=device)
+    for b in range(B):
+        g.manual_seed(SEED * 1_000_003 + first_example + b)
+        x[b].normal_(generator=g)
+        x[b].mul_(2.0).add_(bias)
+        x[b] = torch.log_softmax(x[b], dim=-1)
+    return x
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.uuid, f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_cpu_run(x_host, steps_budget_s=20.0):
+    """Time the reference CPU library on the workload (all host threads).
+
+    Mirrors the reference's CPU path for final_scores forward + backward:
+    dbs_decode_batch over the batch, then per example the sparse backward of
+    grad_final = ones and the scatter into a zero dense gradient
+    (python/torch_extension.cpp:128-188). Returns (elems/s, cores, kind, sample).
+    """
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import dbs_ctypes as dc
+    from oracle import reference_library_path
+    path = reference_library_path()
+    cores = os.cpu_count() or 1
+    B, T, K, V = x_host.shape
+    x = np.ascontiguousarray(x_host)
+    if path is None:
+        return None
+    lib = dc.load_library(path, device_api=False)
+    dec = dc.Decoder(lib, dc.Options(**OPTIONS))
+    gf = np.ones(K, dtype=np.float32)
+    elems = 0
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        br = dec.decode_batch(x, B, T, V, cores)
+        grad = np.zeros((B, T * K * V), dtype=np.float32)
+        for b in range(B):
+            r = lib.dbs_batch_result_at(br, b)
+            bw = dec.backward(r, None, None, gf, mode="default")
+            out = dc.read_backward(lib, bw, K=K)
+            grad[b, out["indices"]] += out["values"]
+            lib.dbs_free_backward(bw)
+        lib.dbs_free_batch_result(br)
+        del grad
+        elems += B * T * K * V
+        reps += 1
+        if time.perf_counter() - t0 >= min(steps_budget_s, 2.0) or reps >= 50:
+            break
+    dt = time.perf_counter() - t0
+    dec.close()
+    sample = (f"{reps} x full batch B={B},T={T},K={K},V={V} via dbs_decode_batch({cores} threads) + per-example "
+              f"dbs_backward + dense scatter; kernel={lib.dbs_selected_kernel_name().decode()}")
+    return elems / dt, cores, "reference", sample
+
+
+def run_reference_arm(args, rank, world):
+    import numpy as np
+    if rank != 0:
+        return
+    B, T, K, V = (WORKLOAD[k] for k in "BTKV")
+    # inputs generated exactly as on the GPU arm, on the CPU generator
+    import torch
+    x = make_inputs(torch, B, T, K, V, 0, "cpu").numpy()
+    vals = []
+    res = None
+    for i in range(args.warmup + args.steps):
+        res = reference_cpu_run(x, steps_budget_s=2.0)
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdbs_ref.so was not built"}))
+            return
+        if i >= args.warmup:
+            vals.append(res[0])
+        if i >= args.warmup and len(vals) >= args.steps:
+            break
+    value = statistics.median(vals)
+    elems = B * T * K * V
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "elem/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * elems / value, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "final_scores fwd+bwd B=64 T=32 K=8 V=32000 eos=2 alpha=0.2 sel_temp=0.7 (host CPU)"},
+        "cpu_baseline": {"value": value, "unit": "elem/s", "cores": res[1], "kind": res[2], "sample": res[3]},
+        "e2e": {"value": value, "unit": "elem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import torch_dbs_extension as ext
+    import dbs_ctypes
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    B, T, K, V = (WORKLOAD[k] for k in "BTKV")
+    elems = B * T * K * V
+    opts = ext.DBSOptions(**OPTIONS)
+    lib = ext._library()
+
+    x = make_inputs(torch, B, T, K, V, rank * B, device)
+    x.requires_grad_(True)
+
+    def step():
+        x.grad = None
+        y = ext.final_scores(x, opts)
+        y.sum().backward()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    sampler.start()
+    time.sleep(0.3)
+    lib.dbs_device_profile(-1)
+    lib.dbs_device_profile(1)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    lib.dbs_device_profile(0)
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end)
+    kern = {}
+    launches = 0
+    for i, name in enumerate(dbs_ctypes.PROFILED_KERNELS):
+        tot = ctypes.c_double()
+        n = ctypes.c_int64()
+        lib.dbs_device_profile_read(i, ctypes.byref(tot), ctypes.byref(n))
+        kern[name] = {"total_ms": tot.value, "launches": n.value}
+        launches += n.value
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    value = world * elems / (ms_per_step / 1e3)
+
+    # live roofline of the row scan
+    rs = kern["row_scan"]
+    peak, peak_kind = measured_peaks()
+    rs_ms = rs["total_ms"] / max(1, rs["launches"])
+    alg_bytes = 4.0 * elems
+    achieved = alg_bytes / (rs_ms / 1e3) / 1e9 if rs_ms > 0 else None
+    traffic = ncu_traffic_per_launch()
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": (achieved / peak) if achieved else None, "traffic": traffic,
+                "peak_kind": peak_kind, "kernel": "row_scan_kernel",
+                "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": rs_ms}
+    step_bytes = 8.0 * elems  # log-prob read + dense gradient write
+    whole = {"achieved_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
+             "frac": step_bytes / (ms_per_step / 1e3) / 1e9 / peak}
+
+    # end to end from pinned host memory
+    x_host = x.detach().cpu().pin_memory()
+    xd = torch.empty_like(x.detach()).requires_grad_(True)
+
+    def e2e_step():
+        with torch.no_grad():
+            xd.copy_(x_host, non_blocking=True)
+        xd.grad = None
+        y = ext.final_scores(xd, opts)
+        loss = y.sum()
+        loss.backward()
+        return loss.item()
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item()) / args.e2e_steps
+    e2e = {"value": world * elems / (e2e_ms / 1e3), "unit": "elem/s", "h2d_bytes_per_step": 4 * elems,
+           "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = reference_cpu_run(x_host.numpy(), steps_budget_s=10.0)
+        if r is not None:
+            cpu = {"value": r[0], "unit": "elem/s", "cores": r[1], "kind": r[2], "sample": r[3]}
+    rescans = (ctypes.c_int64(), ctypes.c_int64())
+    lib.dbs_device_last_rescan_counts(ext._handle(opts), ctypes.byref(rescans[0]), ctypes.byref(rescans[1]))
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "elem/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: 2*N(0,1) logits + Zipf bias -1.1*ln(v+1), log_softmax over V, seeded per example",
+        "config": {"workload": "torch final_scores fwd + y.sum().backward(), B=64 T=32 K=8 V=32000, eos_token=2, "
+                               "length_penalty_alpha=0.2, selected_temperature=0.7 (per GPU)",
+                   "global_batch": B * world, "seq_len": T, "beam_size": K, "vocab": V,
+                   "parallelism": f"batch-sharded x{world}, no data-path collective",
+                   "l2": "inputs larger than L2 (2.1 GB per GPU); no flush needed"},
+        "roofline": roofline,
+        "step_hbm": whole,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": launches,
+        "kernels": kern,
+        "rescans": {"row_scan": rescans[0].value, "step_merge": rescans[1].value},
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,1164 @@
+// sm_100a kernels of the differentiable beam search engine (see dbs_engine.h
+// for the decomposition). Arithmetic that decides selection or gradient
+// values uses explicitly rounded intrinsics (__fadd_rn, __fmul_rn,
+// __fdiv_rn) so nothing is contracted into an FMA: the reference performs
+// those operations as separately rounded float ops
+// (src/differentiable_beam.cpp:501-506, :1536-1537, :1666, :2108-2111).
+#include "dbs_engine.h"
+
+#include <cfloat>
+#include <cmath>
+#include <cstdint>
+
+namespace dbs_dev {
+
+// ---------------------------------------------------------------------------
+// Helpers
+// ---------------------------------------------------------------------------
+
+// Monotone float -> u32 map; -0 is canonicalised to +0 first so that keys
+// compare equal exactly when the floats do (candidate_better uses `!=`).
+__device__ __forceinline__ uint32_t ord_f32(float f) {
+    uint32_t u = __float_as_uint(__fadd_rn(f, 0.0f));
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float unord_f32(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    return __uint_as_float(u);
+}
+
+// Row list entry: larger key = better (lp desc, token asc).
+__device__ __forceinline__ uint64_t list_key(float lp, int token) {
+    return (static_cast<uint64_t>(ord_f32(lp)) << 32) |
+           static_cast<uint64_t>(0xFFFFFFFFu - static_cast<uint32_t>(token));
+}
+__device__ __forceinline__ float list_lp(uint64_t key) { return unord_f32(static_cast<uint32_t>(key >> 32)); }
+__device__ __forceinline__ int list_token(uint64_t key) {
+    return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key));
+}
+
+// Streaming 128-bit load: bypass L1, prefetch the surrounding 256 B into L2.
+__device__ __forceinline__ float4 ldg_stream(const float4* p) {
+    float4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
+__device__ __forceinline__ int warp_isum(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// Descending sort of n single-word keys in shared memory with the
+// "flip" formulation of bitonic sort: every sorted run has the same
+// direction, so out-of-range positions behave as -inf pads that never move and
+// n need not be a power of two. Must be called by all threads of the block.
+__device__ void block_sort_desc_u64(uint64_t* a, int n) {
+    if (n <= 1) { __syncthreads(); return; }
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    const int half = n2 >> 1;
+    for (int size = 2; size <= n2; size <<= 1) {
+        const int hs = size >> 1;
+        for (int pid = threadIdx.x; pid < half; pid += blockDim.x) {
+            const int x = pid & (hs - 1);
+            const int blk = (pid - x) << 1;
+            const int i = blk + x;
+            const int j = blk + size - 1 - x;
+            if (j < n) {
+                uint64_t ai = a[i], aj = a[j];
+                if (ai < aj) { a[i] = aj; a[j] = ai; }
+            }
+        }
+        __syncthreads();
+        for (int st = size >> 2; st > 0; st >>= 1) {
+            for (int pid = threadIdx.x; pid < half; pid += blockDim.x) {
+                const int i = ((pid & ~(st - 1)) << 1) | (pid & (st - 1));
+                const int j = i + st;
+                if (j < n) {
+                    uint64_t ai = a[i], aj = a[j];
+                    if (ai < aj) { a[i] = aj; a[j] = ai; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// Same network over two-word keys (hi, lo) compared lexicographically.
+__device__ __forceinline__ bool key2_less(uint64_t ah, uint64_t al, uint64_t bh, uint64_t bl) {
+    return ah < bh || (ah == bh && al < bl);
+}
+
+__device__ void block_sort_desc_u128(uint64_t* hi, uint64_t* lo, int n) {
+    if (n <= 1) { __syncthreads(); return; }
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    const int half = n2 >> 1;
+    for (int size = 2; size <= n2; size <<= 1) {
+        const int hs = size >> 1;
+        for (int pid = threadIdx.x; pid < half; pid += blockDim.x) {
+            const int x = pid & (hs - 1);
+            const int blk = (pid - x) << 1;
+            const int i = blk + x;
+            const int j = blk + size - 1 - x;
+            if (j < n) {
+                uint64_t ih = hi[i], il = lo[i], jh = hi[j], jl = lo[j];
+                if (key2_less(ih, il, jh, jl)) { hi[i] = jh; lo[i] = jl; hi[j] = ih; lo[j] = il; }
+            }
+        }
+        __syncthreads();
+        for (int st = size >> 2; st > 0; st >>= 1) {
+            for (int pid = threadIdx.x; pid < half; pid += blockDim.x) {
+                const int i = ((pid & ~(st - 1)) << 1) | (pid & (st - 1));
+                const int j = i + st;
+                if (j < n) {
+                    uint64_t ih = hi[i], il = lo[i], jh = hi[j], jl = lo[j];
+                    if (key2_less(ih, il, jh, jl)) { hi[i] = jh; lo[i] = jl; hi[j] = ih; lo[j] = il; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ int find_example(const int64_t* prefix, int B, int64_t row) {
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= row) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// ---------------------------------------------------------------------------
+// 0. Sampled input validation (validate_logprob_tensor,
+//    src/differentiable_beam.cpp:385-402): indices 0, s, 2s, ... of the
+//    example's tight [T,K,V] tensor, s = count/1000 when count > 1000.
+// ---------------------------------------------------------------------------
+__global__ void validate_kernel(DecodeParams p) {
+    const int e = blockIdx.x;
+    const ExampleDesc d = p.desc[e];
+    const int64_t V = p.V;
+    const int64_t count = static_cast<int64_t>(d.T) * d.K * V;
+    const int64_t stride = count > 1000 ? count / 1000 : 1;
+    int bad = 0;
+    for (int64_t s = threadIdx.x; s * stride < count; s += blockDim.x) {
+        const int64_t i = s * stride;
+        const int64_t kv = static_cast<int64_t>(d.K) * V;
+        const int64_t t = i / kv;
+        const int64_t rem = i - t * kv;
+        const int64_t k = rem / V;
+        const int64_t v = rem - k * V;
+        const float x = p.x[d.x_offset + (t * d.k_stride + k) * V + v];
+        if (isnan(x) || x == INFINITY) bad = 1;
+    }
+    bad = __syncthreads_or(bad);
+    if (threadIdx.x == 0) p.status[e] = bad ? 1 : 0;
+}
+
+// ---------------------------------------------------------------------------
+// 1. Row scan: best C entries of every log-prob row.
+//
+// Each CTA owns a contiguous range of rows. A row is streamed with 128-bit
+// loads; an element survives when lp >= T_pass, everything else only feeds a
+// running max (the bound on what was dropped). Survivors that are finite and
+// statically allowed (banned / EOS-before-min-length) are appended to a
+// shared buffer; when the buffer nears capacity it is sorted and cut back to C
+// entries, and T_pass rises to just above the C-th kept value (every later
+// element has a larger token, so an equal value can no longer win).
+//
+// T_pass starts from a guess: the (1.5C)-th best value of the previous row of
+// this CTA. If fewer than C entries survive a guessed threshold the row is
+// rescanned with no threshold, so the list is always the exact top-C.
+// ---------------------------------------------------------------------------
+template <int NT, int U>
+struct RowScanShared {
+    int cnt;
+    float tpass;
+    float evict;
+    float guess;
+    int guess_c;
+    float red[NT / 32];
+};
+
+template <int NT, int U>
+__device__ bool scan_one_row(const float* __restrict__ row, int V, int C, float thr,
+                             const uint8_t* __restrict__ banned, int eos, bool eos_blocked,
+                             uint64_t* __restrict__ buf, int cap, RowScanShared<NT, U>& sh,
+                             uint64_t* __restrict__ out, int32_t* out_count, float* out_bound,
+                             bool write_guess) {
+    const int tid = threadIdx.x;
+    constexpr int kIter = NT * U * 4;
+    __syncthreads();
+    if (tid == 0) {
+        sh.cnt = 0;
+        sh.tpass = fmaxf(thr, -FLT_MAX);
+        sh.evict = -INFINITY;
+    }
+    __syncthreads();
+    float tp = sh.tpass;
+    float rej = -INFINITY;
+
+    auto consider = [&](int v, float lp) {
+        if (lp >= tp) {
+            if (lp != INFINITY && !(banned && banned[v]) && !(eos_blocked && v == eos)) {
+                const int pos = atomicAdd(&sh.cnt, 1);
+                buf[pos] = list_key(lp, v);
+            }
+        } else {
+            rej = fmaxf(rej, lp);
+        }
+    };
+    auto compact = [&]() {
+        // all threads
+        const int n = sh.cnt;
+        block_sort_desc_u64(buf, n);
+        if (tid == 0 && n > C) {
+            sh.evict = fmaxf(sh.evict, list_lp(buf[C]));
+            sh.tpass = fmaxf(sh.tpass, nextafterf(list_lp(buf[C - 1]), INFINITY));
+            sh.cnt = C;
+        }
+        __syncthreads();
+    };
+
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
+    int h = static_cast<int>(((16u - (addr & 15u)) & 15u) >> 2);
+    if (h > V) h = V;
+    if (tid < h) consider(tid, row[tid]);
+    const int nv = (V - h) >> 2;
+    const float4* p4 = reinterpret_cast<const float4*>(row + h);
+    for (int base = 0; base < nv; base += NT * U) {
+        float4 vals[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = base + u * NT + tid;
+            if (idx < nv) vals[u] = ldg_stream(p4 + idx);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int idx = base + u * NT + tid;
+            if (idx < nv) {
+                const int v0 = h + 4 * idx;
+                consider(v0 + 0, vals[u].x);
+                consider(v0 + 1, vals[u].y);
+                consider(v0 + 2, vals[u].z);
+                consider(v0 + 3, vals[u].w);
+            }
+        }
+        __syncthreads();
+        if (sh.cnt > cap - kIter) compact();
+        tp = sh.tpass;
+    }
+    const int tail0 = h + 4 * nv;
+    if (tid < V - tail0) consider(tail0 + tid, row[tail0 + tid]);
+    __syncthreads();
+
+    const int n = sh.cnt;
+    if (thr > -INFINITY && n < C) return false;  // guess too high: caller rescans
+    block_sort_desc_u64(buf, n);
+    // bound = max over everything dropped
+    float r = warp_max(rej);
+    if ((tid & 31) == 0) sh.red[tid >> 5] = r;
+    __syncthreads();
+    const int keep = n < C ? n : C;
+    for (int i = tid; i < keep; i += NT) out[i] = buf[i];
+    if (tid == 0) {
+        float b = sh.red[0];
+        for (int w = 1; w < NT / 32; ++w) b = fmaxf(b, sh.red[w]);
+        b = fmaxf(b, sh.evict);
+        if (n > C) b = fmaxf(b, list_lp(buf[C]));
+        *out_count = keep;
+        *out_bound = b;
+        if (write_guess) {
+            int gi = C + (C >> 1) + 2;
+            if (gi > n) gi = n;
+            sh.guess = gi > 0 ? list_lp(buf[gi - 1]) : -INFINITY;
+            sh.guess_c = C;
+        }
+    }
+    return true;
+}
+
+template <int NT, int U>
+__global__ void __launch_bounds__(NT) row_scan_kernel(DecodeParams p, int cap, int64_t rows_per_cta) {
+    extern __shared__ __align__(16) uint64_t buf[];
+    __shared__ RowScanShared<NT, U> sh;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
+    int64_t r1 = r0 + rows_per_cta;
+    if (r1 > p.total_rows) r1 = p.total_rows;
+    if (r0 >= r1) return;
+    if (threadIdx.x == 0) {
+        sh.guess = -INFINITY;
+        sh.guess_c = -1;
+    }
+    int e = find_example(p.row_prefix, p.B, r0);
+    const int V = p.V;
+    for (int64_t r = r0; r < r1; ++r) {
+        while (r >= p.row_prefix[e + 1]) ++e;
+        const ExampleDesc& d = p.desc[e];
+        const int64_t lr = r - d.row_begin;
+        const int t = static_cast<int>(lr / d.K);
+        const int k = static_cast<int>(lr - static_cast<int64_t>(t) * d.K);
+        const float* row = p.x + d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
+        uint64_t* out = p.lists + d.list_offset + lr * d.C;
+        const int forced = d.forced ? d.forced[t] : -1;
+        const bool eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
+        if (forced >= 0) {
+            // Forced step: only the forced token is a candidate of this row.
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                const float lp = row[forced];
+                const bool ok = isfinite(lp) && !(d.banned && d.banned[forced]) &&
+                                !(eos_blocked && forced == d.eos);
+                if (ok) out[0] = list_key(lp, forced);
+                p.list_count[r] = ok ? 1 : 0;
+                p.list_bound[r] = -INFINITY;
+            }
+            continue;
+        }
+        __syncthreads();
+        const float thr = (sh.guess_c == d.C) ? sh.guess : -INFINITY;
+        bool ok = scan_one_row<NT, U>(row, V, d.C, thr, d.banned, d.eos, eos_blocked, buf, cap, sh,
+                                      out, p.list_count + r, p.list_bound + r, true);
+        if (!ok) {
+            if (threadIdx.x == 0 && p.counters) atomicAdd(p.counters + 0, 1ull);
+            scan_one_row<NT, U>(row, V, d.C, -INFINITY, d.banned, d.eos, eos_blocked, buf, cap, sh,
+                                out, p.list_count + r, p.list_bound + r, true);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2. Step merge: one CTA per example, T sequential steps.
+// ---------------------------------------------------------------------------
+struct MergeState {
+    float* prev_raw;
+    float* next_raw;
+    int* prev_len;
+    int* next_len;
+    int* ended;
+    int* ended_next;
+    int* row_cnt;
+    float* row_bound;
+    int* unsafe;
+    int* blocked_n;   // [K] count of n-gram blocked tokens (constraints only)
+};
+
+// Candidate key (hi, lo), larger = better under candidate_better
+// (src/differentiable_beam.cpp:291-298): score desc, raw desc, parent asc,
+// token asc. Length and from_logprob never decide because (parent, token) is
+// unique among a step's candidates (a parent either scans or carries).
+__device__ __forceinline__ uint64_t cand_hi(float rank, float raw) {
+    return (static_cast<uint64_t>(ord_f32(rank)) << 32) | ord_f32(raw);
+}
+__device__ __forceinline__ uint64_t cand_lo(int parent, int token) {
+    return (static_cast<uint64_t>(0x7FFFFFFFu - static_cast<uint32_t>(parent)) << 32) |
+           static_cast<uint64_t>(0x7FFFFFFFu - static_cast<uint32_t>(token));
+}
+__device__ __forceinline__ int cand_parent(uint64_t lo) {
+    return static_cast<int>(0x7FFFFFFFu - static_cast<uint32_t>(lo >> 32));
+}
+__device__ __forceinline__ int cand_token(uint64_t lo) {
+    return static_cast<int>(0x7FFFFFFFu - static_cast<uint32_t>(lo));
+}
+__device__ __forceinline__ float cand_rank(uint64_t hi) { return unord_f32(static_cast<uint32_t>(hi >> 32)); }
+__device__ __forceinline__ float cand_raw(uint64_t hi) { return unord_f32(static_cast<uint32_t>(hi)); }
+
+// would_repeat_ngram (src/differentiable_beam.cpp:305-325) for n >= 2 turned
+// into the set of tokens it rejects for one prefix.
+__device__ int ngram_blocked_set(const int32_t* pre, int plen, int n, int32_t* out) {
+    int cnt = 0;
+    if (plen + 1 < n) return 0;
+    const int suffix = plen - (n - 1);
+    for (int i = 0; i + n <= plen; ++i) {
+        bool same = true;
+        for (int j = 0; j < n - 1; ++j) {
+            if (pre[i + j] != pre[suffix + j]) { same = false; break; }
+        }
+        if (same) out[cnt++] = pre[i + n - 1];
+    }
+    return cnt;
+}
+
+__device__ __forceinline__ bool in_list(const int32_t* a, int n, int v) {
+    for (int i = 0; i < n; ++i)
+        if (a[i] == v) return true;
+    return false;
+}
+
+__global__ void __launch_bounds__(kMergeThreads) step_merge_kernel(DecodeParams p, int cand_cap,
+                                                                   int seq_T) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int e = blockIdx.x;
+    const ExampleDesc d = p.desc[e];
+    const int K = d.K, C = d.C, N = d.N, T = d.T, P = d.P;
+    const int V = p.V;
+    const int tid = threadIdx.x;
+    const int NT = blockDim.x;
+
+    uint64_t* chi = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* clo = chi + cand_cap;
+    float* f_base = reinterpret_cast<float*>(clo + cand_cap);
+    MergeState s;
+    s.prev_raw = f_base;
+    s.next_raw = s.prev_raw + K;
+    s.row_bound = s.next_raw + K;
+    int* i_base = reinterpret_cast<int*>(s.row_bound + K);
+    s.prev_len = i_base;
+    s.next_len = s.prev_len + K;
+    s.ended = s.next_len + K;
+    s.ended_next = s.ended + K;
+    s.row_cnt = s.ended_next + K;
+    s.unsafe = s.row_cnt + K;
+    s.blocked_n = s.unsafe + K;
+    __shared__ int sh_any_unsafe;
+    __shared__ int sh_stage;
+
+    const bool use_rep = p.repetition_penalty > 1.0f;
+    const bool use_ngram = p.no_repeat_ngram > 0;
+    const bool need_seq = use_rep || use_ngram;
+    // Beam prefixes (only with repetition penalty / n-gram constraints):
+    // [2][K][seq_T] in global scratch, plus n-gram blocked sets [K][seq_T].
+    int32_t* seq_a = need_seq ? p.seq_scratch + static_cast<int64_t>(e) * 3 * K * seq_T : nullptr;
+    int32_t* seq_b = need_seq ? seq_a + static_cast<int64_t>(K) * seq_T : nullptr;
+    int32_t* blk = need_seq ? seq_b + static_cast<int64_t>(K) * seq_T : nullptr;
+    __shared__ int seq_len_a[1024];
+    __shared__ int seq_len_b[1024];
+    int* sl_prev = seq_len_a;
+    int* sl_next = seq_len_b;
+
+    for (int k = tid; k < K; k += NT) {
+        s.prev_raw[k] = (k == 0) ? 0.0f : -INFINITY;
+        s.prev_len[k] = 0;
+        s.ended[k] = 0;
+        if (need_seq) sl_prev[k] = 0;
+    }
+    __syncthreads();
+
+    for (int t = 0; t < T; ++t) {
+        const int64_t row0 = d.row_begin + static_cast<int64_t>(t) * K;
+        const int forced = d.forced ? d.forced[t] : -1;
+        const bool eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
+        for (int k = tid; k < K; k += NT) {
+            s.row_cnt[k] = p.list_count[row0 + k];
+            s.row_bound[k] = p.list_bound[row0 + k];
+            s.unsafe[k] = 0;
+            if (use_ngram && p.no_repeat_ngram >= 2 && isfinite(s.prev_raw[k]) &&
+                !(d.eos >= 0 && s.ended[k])) {
+                s.blocked_n[k] = ngram_blocked_set(seq_a + static_cast<int64_t>(k) * seq_T, sl_prev[k],
+                                                   p.no_repeat_ngram, blk + static_cast<int64_t>(k) * seq_T);
+            } else if (k < K) {
+                s.blocked_n[k] = 0;
+            }
+        }
+        if (tid == 0) { sh_any_unsafe = 0; sh_stage = 0; }
+        __syncthreads();
+
+        // Candidate generation: slot k*C + i holds entry i of row k; an
+        // ended parent's carry candidate takes slot k*C.
+        const int M = K * C;
+        for (int idx = tid; idx < M; idx += NT) {
+            const int k = idx / C;
+            const int i = idx - k * C;
+            uint64_t h = 0, l = 0;
+            const float pr = s.prev_raw[k];
+            if (isfinite(pr)) {
+                if (d.eos >= 0 && s.ended[k]) {
+                    if (i == 0) {
+                        const int len = s.prev_len[k] < 1 ? 1 : s.prev_len[k];
+                        const float rank = __fdiv_rn(pr, p.pen[len]);
+                        h = cand_hi(rank, pr);
+                        l = cand_lo(k, d.eos);
+                    }
+                } else if (i < s.row_cnt[k]) {
+                    const uint64_t key = p.lists[d.list_offset + (row0 - d.row_begin + k) * C + i];
+                    float lp = list_lp(key);
+                    const int v = list_token(key);
+                    bool ok = true;
+                    if (need_seq) {
+                        const int32_t* pre = seq_a + static_cast<int64_t>(k) * seq_T;
+                        const int plen = sl_prev[k];
+                        if (use_ngram) {
+                            if (p.no_repeat_ngram == 1) ok = !in_list(pre, plen, v);
+                            else ok = !in_list(blk + static_cast<int64_t>(k) * seq_T, s.blocked_n[k], v);
+                        }
+                        if (ok && use_rep && in_list(pre, plen, v))
+                            lp = __fsub_rn(lp, p.log_repetition_penalty);
+                    }
+                    if (ok) {
+                        const float raw = __fadd_rn(pr, lp);
+                        if (raw != -INFINITY) {
+                            const float rank = __fmul_rn(raw, p.inv_pen[s.prev_len[k] + 1]);
+                            h = cand_hi(rank, raw);
+                            l = cand_lo(k, v);
+                        }
+                    }
+                }
+            }
+            chi[idx] = h;
+            clo[idx] = l;
+        }
+        __syncthreads();
+        block_sort_desc_u128(chi, clo, M);
+
+        // Exactness proof per truncated row: every entry the scan dropped has
+        // lp <= bound, so its candidate is at most U = (rank(bound),
+        // raw(bound)); if the current N-th candidate G beats U, no dropped
+        // entry can enter the top-N.
+        for (int k = tid; k < K; k += NT) {
+            const float pr = s.prev_raw[k];
+            if (!isfinite(pr) || (d.eos >= 0 && s.ended[k])) continue;
+            const float bnd = s.row_bound[k];
+            if (!(bnd > -INFINITY)) continue;  // nothing dropped
+            const float raw_u = __fadd_rn(pr, bnd);
+            if (raw_u == -INFINITY) continue;   // dropped entries can never be selected
+            const float rank_u = __fmul_rn(raw_u, p.inv_pen[s.prev_len[k] + 1]);
+            bool safe = false;
+            if (N - 1 < M && chi[N - 1] != 0) {
+                const uint64_t uh = cand_hi(rank_u, raw_u);
+                const uint64_t gh = chi[N - 1];
+                safe = gh > uh || (gh == uh && cand_parent(clo[N - 1]) < k);
+            }
+            if (!safe) {
+                s.unsafe[k] = 1;
+                atomicOr(&sh_any_unsafe, 1);
+            }
+        }
+        __syncthreads();
+
+        if (sh_any_unsafe) {
+            // Rescan the unproven rows from HBM and merge in every dropped
+            // candidate that beats the current N-th (rare path).
+            constexpr int kChunk = 2048;
+            for (int k = 0; k < K; ++k) {
+                if (!s.unsafe[k]) continue;
+                if (tid == 0 && p.counters) atomicAdd(p.counters + 1, 1ull);
+                const float pr = s.prev_raw[k];
+                const float inv = p.inv_pen[s.prev_len[k] + 1];
+                const float* row = p.x + d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
+                const int cnt = s.row_cnt[k];
+                const uint64_t last = p.lists[d.list_offset + (row0 - d.row_begin + k) * C + (cnt - 1)];
+                const float m_lp = list_lp(last);
+                const int m_tok = list_token(last);
+                const int32_t* pre = need_seq ? seq_a + static_cast<int64_t>(k) * seq_T : nullptr;
+                const int plen = need_seq ? sl_prev[k] : 0;
+                for (int base = 0; base < V; base += kChunk) {
+                    // G is re-read each chunk; it only improves.
+                    const uint64_t gh = (N - 1 < M) ? chi[N - 1] : 0;
+                    const uint64_t gl = (N - 1 < M) ? clo[N - 1] : 0;
+                    for (int v = base + tid; v < base + kChunk && v < V; v += NT) {
+                        if (forced >= 0 && v != forced) continue;
+                        if (d.banned && d.banned[v]) continue;
+                        if (eos_blocked && v == d.eos) continue;
+                        float lp = row[v];
+                        if (!isfinite(lp)) continue;
+                        const float lpc = __fadd_rn(lp, 0.0f);
+                        if (lpc > m_lp || (lpc == m_lp && v <= m_tok)) continue;  // already listed
+                        if (need_seq) {
+                            if (use_ngram) {
+                                const bool bl = (p.no_repeat_ngram == 1)
+                                                    ? in_list(pre, plen, v)
+                                                    : in_list(blk + static_cast<int64_t>(k) * seq_T, s.blocked_n[k], v);
+                                if (bl) continue;
+                            }
+                            if (use_rep && in_list(pre, plen, v)) lp = __fsub_rn(lp, p.log_repetition_penalty);
+                        }
+                        const float raw = __fadd_rn(pr, lp);
+                        if (raw == -INFINITY) continue;
+                        const float rank = __fmul_rn(raw, inv);
+                        const uint64_t h = cand_hi(rank, raw);
+                        const uint64_t l = cand_lo(k, v);
+                        if (key2_less(gh, gl, h, l)) {
+                            const int pos = atomicAdd(&sh_stage, 1);
+                            chi[N + pos] = h;
+                            clo[N + pos] = l;
+                        }
+                    }
+                    __syncthreads();
+                    const int staged = sh_stage;
+                    if (staged > 0) {
+                        block_sort_desc_u128(chi, clo, N + staged);
+                        for (int i = N + tid; i < N + staged; i += NT) { chi[i] = 0; clo[i] = 0; }
+                        __syncthreads();
+                        if (tid == 0) sh_stage = 0;
+                        __syncthreads();
+                    }
+                }
+            }
+        }
+
+        // Outputs of step t and beam state update.
+        const bool want_pool = p.pool_scores != nullptr;
+        for (int j = tid; j < N; j += NT) {
+            const uint64_t h = (j < M) ? chi[j] : 0;
+            const uint64_t l = (j < M) ? clo[j] : 0;
+            int parent = -1, token = -1, len = 0, flp = 0;
+            float rank = -INFINITY, raw = -INFINITY;
+            if (h != 0) {
+                parent = cand_parent(l);
+                token = cand_token(l);
+                rank = cand_rank(h);
+                raw = cand_raw(h);
+                const bool carry = d.eos >= 0 && s.ended[parent];
+                len = carry ? (s.prev_len[parent] < 1 ? 1 : s.prev_len[parent]) : s.prev_len[parent] + 1;
+                flp = carry ? 0 : 1;
+            }
+            if (want_pool && j < P) {
+                const int64_t o = d.pool_offset + static_cast<int64_t>(t) * d.pool_t_stride + j;
+                p.pool_parents[o] = parent;
+                p.pool_tokens[o] = token;
+                p.pool_lengths[o] = len;
+                p.pool_raw_scores[o] = raw;
+                p.pool_scores[o] = rank;
+                if (p.pool_from_logprob) p.pool_from_logprob[o] = static_cast<uint8_t>(flp);
+            }
+            if (j < K) {
+                const int64_t o = d.sel_offset + static_cast<int64_t>(t) * d.sel_t_stride + j;
+                p.parents[o] = parent;
+                p.tokens[o] = token;
+                p.lengths[o] = len;
+                if (p.raw_scores) p.raw_scores[o] = raw;
+                if (p.scores) p.scores[o] = rank;
+                p.from_logprob[o] = static_cast<uint8_t>(flp);
+                s.next_raw[j] = raw;
+                s.next_len[j] = len;
+                s.ended_next[j] = (parent >= 0) ? ((s.ended[parent] != 0) || (d.eos >= 0 && token == d.eos)) : 0;
+            }
+        }
+        __syncthreads();
+        if (need_seq) {
+            // prefix[j] = prefix[parent_j] ++ token_j (when from a log-prob)
+            for (int j = tid; j < K; j += NT) {
+                const uint64_t l = (j < M) ? clo[j] : 0;
+                const uint64_t h = (j < M) ? chi[j] : 0;
+                int len = 0;
+                if (h != 0) {
+                    const int parent = cand_parent(l);
+                    len = sl_prev[parent];
+                    const bool carry = d.eos >= 0 && s.ended[parent];
+                    if (!carry) len += 1;
+                }
+                sl_next[j] = len;
+            }
+            for (int idx = tid; idx < K * seq_T; idx += NT) {
+                const int j = idx / seq_T;
+                const int i = idx - j * seq_T;
+                const uint64_t h = (j < M) ? chi[j] : 0;
+                if (h == 0) continue;
+                const uint64_t l = clo[j];
+                const int parent = cand_parent(l);
+                const int plen = sl_prev[parent];
+                if (i < plen) seq_b[static_cast<int64_t>(j) * seq_T + i] = seq_a[static_cast<int64_t>(parent) * seq_T + i];
+                else if (i == plen && !(d.eos >= 0 && s.ended[parent]))
+                    seq_b[static_cast<int64_t>(j) * seq_T + i] = cand_token(l);
+            }
+        }
+        __syncthreads();
+        for (int k = tid; k < K; k += NT) {
+            s.prev_raw[k] = s.next_raw[k];
+            s.prev_len[k] = s.next_len[k];
+            s.ended[k] = s.ended_next[k];
+        }
+        if (need_seq) {
+            int32_t* tmp = seq_a; seq_a = seq_b; seq_b = tmp;
+            int* tl = sl_prev; sl_prev = sl_next; sl_next = tl;
+        }
+        __syncthreads();
+    }
+    // Finalisation (src/differentiable_beam.cpp:1661-1667): a division, not
+    // a multiply by the reciprocal.
+    for (int k = tid; k < K; k += NT) {
+        const int len = s.prev_len[k] < 1 ? 1 : s.prev_len[k];
+        const int64_t o = d.final_offset + k;
+        if (p.final_raw_scores) p.final_raw_scores[o] = s.prev_raw[k];
+        if (p.final_scores) p.final_scores[o] = __fdiv_rn(s.prev_raw[k], p.pen[len]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 3. Weights: selected softmax (softmax_selected_scalar, :410-442) and relaxed
+//    pool weights (soft_topk_inclusion, :1333-1386). One warp per step.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float safe_exp_dev(float x) {
+    const float hi = 88.3762626647949f;
+    x = (-hi < x) ? x : -hi;
+    x = (x < hi) ? x : hi;
+    return expf(x);
+}
+__device__ __forceinline__ float sigmoid_dev(float x) {
+    if (x >= 0.0f) {
+        const float e = safe_exp_dev(-x);
+        return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+    }
+    const float e = safe_exp_dev(x);
+    return __fdiv_rn(e, __fadd_rn(1.0f, e));
+}
+
+template <int MAXP>
+__global__ void weights_kernel(DecodeParams p, int max_T) {
+    constexpr int kPer = (MAXP + 31) / 32;
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int e = warp / max_T;
+    const int t = warp - e * max_T;
+    if (e >= p.B) return;
+    const ExampleDesc d = p.desc[e];
+    if (t >= d.T) return;
+    const float guard = -1.0e30f;
+    if (p.weights && p.scores) {
+        const int K = d.K;
+        const int64_t o = d.sel_offset + static_cast<int64_t>(t) * d.sel_t_stride;
+        const float temp = p.selected_temperature;
+        float mx = -INFINITY;
+        for (int i = lane; i < K; i += 32) {
+            const float sc = p.scores[o + i];
+            if (sc > guard) mx = fmaxf(mx, __fdiv_rn(sc, temp));
+        }
+        mx = warp_max(mx);
+        if (!isfinite(mx)) {
+            for (int i = lane; i < K; i += 32) p.weights[o + i] = 0.0f;
+        } else {
+            float sum = 0.0f;
+            for (int i = lane; i < K; i += 32) {
+                const float sc = p.scores[o + i];
+                if (sc > guard) sum = __fadd_rn(sum, safe_exp_dev(__fsub_rn(__fdiv_rn(sc, temp), mx)));
+            }
+            sum = warp_sum(sum);
+            if (!(sum > 0.0f) || !isfinite(sum)) {
+                for (int i = lane; i < K; i += 32) p.weights[o + i] = 0.0f;
+            } else {
+                const float inv = __fdiv_rn(1.0f, sum);
+                for (int i = lane; i < K; i += 32) {
+                    const float sc = p.scores[o + i];
+                    float w = 0.0f;
+                    if (sc > guard) w = __fmul_rn(safe_exp_dev(__fsub_rn(__fdiv_rn(sc, temp), mx)), inv);
+                    p.weights[o + i] = w;
+                }
+            }
+        }
+    }
+    if (p.relaxed_weights && p.pool_scores) {
+        const int P = d.P;
+        const int target = d.K;
+        const int64_t o = d.pool_offset + static_cast<int64_t>(t) * d.pool_t_stride;
+        const float temp = p.soft_topk_temperature;
+        const float tol = p.soft_topk_tolerance;
+        float sv[kPer];
+        int active = 0;
+        float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int i = lane + 32 * j;
+            sv[j] = (i < P) ? p.pool_scores[o + i] : -INFINITY;
+            if (sv[j] > guard) {
+                ++active;
+                mn = fminf(mn, sv[j]);
+                mx = fmaxf(mx, sv[j]);
+            }
+        }
+        active = warp_isum(active);
+        mn = warp_min(mn);
+        mx = warp_max(mx);
+        float out[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) out[j] = 0.0f;
+        if (active > 0 && target > 0) {
+            if (target >= active) {
+#pragma unroll
+                for (int j = 0; j < kPer; ++j) out[j] = (sv[j] > guard) ? 1.0f : 0.0f;
+            } else {
+                float lo = __fsub_rn(mn, __fmul_rn(80.0f, temp));
+                float hi = __fadd_rn(mx, __fmul_rn(80.0f, temp));
+                for (int it = 0; it < p.soft_topk_max_iters; ++it) {
+                    const float mid = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+                    float sum = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j)
+                        if (sv[j] > guard) sum = __fadd_rn(sum, sigmoid_dev(__fdiv_rn(__fsub_rn(sv[j], mid), temp)));
+                    sum = warp_sum(sum);
+                    const float err = __fsub_rn(sum, static_cast<float>(target));
+                    const float amid = fabsf(mid);
+                    if (fabsf(err) <= tol || fabsf(__fsub_rn(hi, lo)) <= __fmul_rn(tol, fmaxf(1.0f, amid))) {
+                        lo = hi = mid;
+                        break;
+                    }
+                    if (err > 0.0f) lo = mid; else hi = mid;
+                }
+                const float theta = __fmul_rn(0.5f, __fadd_rn(lo, hi));
+#pragma unroll
+                for (int j = 0; j < kPer; ++j)
+                    out[j] = (sv[j] > guard) ? sigmoid_dev(__fdiv_rn(__fsub_rn(sv[j], theta), temp)) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int i = lane + 32 * j;
+            if (i < P) p.relaxed_weights[o + i] = out[j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 4. Surrogate backward (backward_sparse / backward, :1674-1791). One CTA per
+//    example walks t = T-1 .. 0. prev_raw_grad is accumulated per parent in
+//    the reference's order (selected k ascending, then pool p ascending).
+// ---------------------------------------------------------------------------
+__global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max_P) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int e = blockIdx.x;
+    const ExampleDesc d = p.desc[e];
+    const int K = d.K, T = d.T, P = d.P;
+    const int64_t V = p.V;
+    const int tid = threadIdx.x;
+    const int NT = blockDim.x;
+    float* next_g = reinterpret_cast<float*>(smem);
+    float* prev_g = next_g + max_K;
+    float* sel_draw = prev_g + max_K;
+    float* pool_draw = sel_draw + max_K;
+    int* sel_parent = reinterpret_cast<int*>(pool_draw + max_P);
+    int* pool_parent = sel_parent + max_K;
+    uint64_t* ent_key = reinterpret_cast<uint64_t*>(pool_parent + max_P);
+    float* ent_val = reinterpret_cast<float*>(ent_key + (max_K + max_P));
+    __shared__ float sh_dot;
+    __shared__ float sh_center;
+    __shared__ int sh_relax;
+    __shared__ int sh_n;
+
+    for (int k = tid; k < K; k += NT) next_g[k] = 0.0f;
+    __syncthreads();
+    const float inv_temp_soft = __fdiv_rn(1.0f, p.soft_topk_temperature);
+    for (int t = T - 1; t >= 0; --t) {
+        const int64_t so = d.sel_offset + static_cast<int64_t>(t) * d.sel_t_stride;
+        const int64_t po = d.pool_offset + static_cast<int64_t>(t) * d.pool_t_stride;
+        if (tid == 0) {
+            sh_n = 0;
+            float dot = 0.0f;
+            if (p.grad_selected) {
+                for (int k = 0; k < K; ++k)
+                    dot = __fadd_rn(dot, __fmul_rn(p.weights[so + k], p.grad_selected[so + k]));
+            }
+            sh_dot = dot;
+            sh_relax = 0;
+            if (p.grad_relaxed) {
+                float denom = 0.0f, numer = 0.0f;
+                for (int q = 0; q < P; ++q) {
+                    const float w = p.relaxed_weights[po + q];
+                    const float a = __fmul_rn(w, __fsub_rn(1.0f, w));
+                    denom = __fadd_rn(denom, a);
+                    numer = __fadd_rn(numer, __fmul_rn(p.grad_relaxed[po + q], a));
+                }
+                if (denom > 1.0e-12f) {
+                    sh_relax = 1;
+                    sh_center = __fdiv_rn(numer, denom);
+                }
+            }
+        }
+        __syncthreads();
+        // selected slots
+        for (int k = tid; k < K; k += NT) {
+            const int parent = p.parents[so + k];
+            float draw = 0.0f;
+            if (parent >= 0) {
+                float drank = 0.0f;
+                if (p.grad_selected) {
+                    const float w = p.weights[so + k];
+                    drank = __fadd_rn(drank, __fdiv_rn(__fmul_rn(w, __fsub_rn(p.grad_selected[so + k], sh_dot)),
+                                                       p.selected_temperature));
+                }
+                if (p.grad_final && t == T - 1) drank = __fadd_rn(drank, p.grad_final[d.final_offset + k]);
+                const int len = p.lengths[so + k] < 1 ? 1 : p.lengths[so + k];
+                draw = __fadd_rn(next_g[k], __fmul_rn(drank, p.inv_pen[len]));
+                const int token = p.tokens[so + k];
+                if (draw != 0.0f && p.from_logprob[so + k] && token >= 0) {
+                    const int64_t gi = (static_cast<int64_t>(t) * K + parent) * V + token;
+                    if (sparse) {
+                        const int pos = atomicAdd(&sh_n, 1);
+                        ent_key[pos] = ~((static_cast<uint64_t>(gi) << 12) | static_cast<uint64_t>(pos));
+                        ent_val[pos] = draw;
+                    } else {
+                        p.grad_dense[d.grad_offset + gi] = draw;
+                    }
+                }
+            }
+            sel_parent[k] = (parent >= 0 && draw != 0.0f) ? parent : -1;
+            sel_draw[k] = draw;
+        }
+        __syncthreads();
+        // relaxed pool
+        if (sh_relax) {
+            const float center = sh_center;
+            for (int q = tid; q < P; q += NT) {
+                const int parent = p.pool_parents[po + q];
+                float draw = 0.0f;
+                if (parent >= 0) {
+                    const float w = p.relaxed_weights[po + q];
+                    const float a = __fmul_rn(w, __fsub_rn(1.0f, w));
+                    const float drank = __fmul_rn(__fmul_rn(a, inv_temp_soft), __fsub_rn(p.grad_relaxed[po + q], center));
+                    if (drank != 0.0f) {
+                        const int len = p.pool_lengths[po + q] < 1 ? 1 : p.pool_lengths[po + q];
+                        draw = __fmul_rn(drank, p.inv_pen[len]);
+                        const int token = p.pool_tokens[po + q];
+                        if (draw != 0.0f && p.pool_from_logprob[po + q] && token >= 0) {
+                            const int64_t gi = (static_cast<int64_t>(t) * K + parent) * V + token;
+                            if (sparse) {
+                                const int pos = atomicAdd(&sh_n, 1);
+                                ent_key[pos] = ~((static_cast<uint64_t>(gi) << 12) | static_cast<uint64_t>(pos));
+                                ent_val[pos] = draw;
+                            } else {
+                                atomicAdd(p.grad_dense + d.grad_offset + gi, draw);
+                            }
+                        }
+                    }
+                }
+                pool_parent[q] = (parent >= 0 && draw != 0.0f) ? parent : -1;
+                pool_draw[q] = draw;
+            }
+        }
+        __syncthreads();
+        // prev_raw_grad in the reference's accumulation order
+        for (int j = tid; j < K; j += NT) {
+            float acc = 0.0f;
+            for (int k = 0; k < K; ++k)
+                if (sel_parent[k] == j) acc = __fadd_rn(acc, sel_draw[k]);
+            if (sh_relax)
+                for (int q = 0; q < P; ++q)
+                    if (pool_parent[q] == j) acc = __fadd_rn(acc, pool_draw[q]);
+            prev_g[j] = acc;
+        }
+        if (sparse) {
+            // Sort this step's entries by index (keys hold ~(index << 12 | slot)
+            // so a descending sort yields ascending indices) and merge the at
+            // most two entries of one index (finalize_sparse_entries,
+            // src/differentiable_beam.cpp:1908-1941).
+            __syncthreads();
+            const int n = sh_n;
+            block_sort_desc_u64(ent_key, n);
+            if (tid == 0) {
+                const int64_t seg = d.sparse_offset + static_cast<int64_t>(t) * (K + P);
+                int m = 0;
+                for (int a = 0; a < n;) {
+                    const uint64_t ka = ~ent_key[a];
+                    const int64_t gi = static_cast<int64_t>(ka >> 12);
+                    float sum = 0.0f;
+                    int b = a;
+                    while (b < n && static_cast<int64_t>((~ent_key[b]) >> 12) == gi) {
+                        sum = __fadd_rn(sum, ent_val[(~ent_key[b]) & 0xFFFu]);
+                        ++b;
+                    }
+                    p.sparse_indices[seg + m] = gi;
+                    p.sparse_values[seg + m] = sum;
+                    ++m;
+                    a = b;
+                }
+                p.step_counts[static_cast<int64_t>(e) * p.max_T + t] = m;
+            }
+        }
+        __syncthreads();
+        for (int k = tid; k < K; k += NT) next_g[k] = prev_g[k];
+        __syncthreads();
+    }
+    for (int k = tid; k < K; k += NT)
+        if (p.grad_initial) p.grad_initial[d.final_offset + k] = next_g[k];
+    if (sparse) {
+        // compact the per-step segments (t ascending == index ascending)
+        __syncthreads();
+        int64_t off = 0;
+        for (int t = 0; t < T; ++t) {
+            const int m = p.step_counts[static_cast<int64_t>(e) * p.max_T + t];
+            const int64_t src = d.sparse_offset + static_cast<int64_t>(t) * (K + P);
+            const int64_t dst = d.sparse_offset + off;
+            if (dst != src) {
+                // read all, then write (ranges may overlap; dst < src)
+                int64_t* tmp_idx = reinterpret_cast<int64_t*>(ent_key);
+                for (int a = tid; a < m; a += NT) {
+                    tmp_idx[a] = p.sparse_indices[src + a];
+                    ent_val[a] = p.sparse_values[src + a];
+                }
+                __syncthreads();
+                for (int a = tid; a < m; a += NT) {
+                    p.sparse_indices[dst + a] = tmp_idx[a];
+                    p.sparse_values[dst + a] = ent_val[a];
+                }
+                __syncthreads();
+            }
+            off += m;
+        }
+        if (tid == 0) p.sparse_counts[e] = off;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 5. Zero fill with 128-bit stores (dense gradient).
+// ---------------------------------------------------------------------------
+__global__ void fill_zero_kernel(float* __restrict__ dst, int64_t count) {
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(dst);
+    int64_t h = static_cast<int64_t>(((16u - (addr & 15u)) & 15u) >> 2);
+    if (h > count) h = count;
+    const int64_t gtid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t gsz = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    if (gtid < h) dst[gtid] = 0.0f;
+    const int64_t nv = (count - h) >> 2;
+    float4* d4 = reinterpret_cast<float4*>(dst + h);
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t i = gtid; i < nv; i += gsz) __stcs(d4 + i, z);
+    const int64_t tail0 = h + 4 * nv;
+    if (gtid < count - tail0) dst[tail0 + gtid] = 0.0f;
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream) {
+    validate_kernel<<<p.B, 1024, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+static int row_scan_cap(int max_C) {
+    constexpr int kIter = kRowScanThreads * 4 * 4;
+    return kIter + max_C + 8;
+}
+
+cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream) {
+    if (p.total_rows <= 0) return cudaSuccess;
+    const int cap = row_scan_cap(max_C);
+    const size_t smem = static_cast<size_t>(cap) * sizeof(uint64_t);
+    auto kern = row_scan_kernel<kRowScanThreads, 4>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+    int per_sm = 0;
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowScanThreads, smem);
+    if (err != cudaSuccess) return err;
+    if (per_sm < 1) per_sm = 1;
+    int64_t ctas = static_cast<int64_t>(num_sms) * per_sm;
+    if (ctas > p.total_rows) ctas = p.total_rows;
+    const int64_t rows_per_cta = (p.total_rows + ctas - 1) / ctas;
+    ctas = (p.total_rows + rows_per_cta - 1) / rows_per_cta;
+    kern<<<static_cast<unsigned>(ctas), kRowScanThreads, smem, stream>>>(p, cap, rows_per_cta);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T, int max_N,
+                              bool need_sequences, cudaStream_t stream) {
+    const int M = max_K * max_C;
+    int cand_cap = M;
+    if (cand_cap < max_N + 2048) cand_cap = max_N + 2048;
+    const size_t smem = static_cast<size_t>(cand_cap) * 2 * sizeof(uint64_t) +
+                        static_cast<size_t>(max_K) * 3 * sizeof(float) +
+                        static_cast<size_t>(max_K) * 7 * sizeof(int) + 64;
+    int threads = 64;
+    while (threads < kMergeThreads && threads * 2 <= (M + 1) / 2) threads <<= 1;
+    if (threads < 128 && max_K > 64) threads = 128;
+    cudaError_t err = cudaFuncSetAttribute(step_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+    (void)need_sequences;
+    step_merge_kernel<<<p.B, threads, smem, stream>>>(p, cand_cap, max_T);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_P, cudaStream_t stream) {
+    (void)max_K;
+    const int64_t warps = static_cast<int64_t>(p.B) * max_T;
+    const int threads = 256;
+    const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    if (max_P <= 32) weights_kernel<32><<<blocks, threads, 0, stream>>>(p, max_T);
+    else if (max_P <= 128) weights_kernel<128><<<blocks, threads, 0, stream>>>(p, max_T);
+    else if (max_P <= 512) weights_kernel<512><<<blocks, threads, 0, stream>>>(p, max_T);
+    else if (max_P <= 1024) weights_kernel<1024><<<blocks, threads, 0, stream>>>(p, max_T);
+    else if (max_P <= 4096) weights_kernel<4096><<<blocks, threads, 0, stream>>>(p, max_T);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool sparse, cudaStream_t stream) {
+    const size_t smem = static_cast<size_t>(max_K) * 3 * sizeof(float) + static_cast<size_t>(max_P) * sizeof(float) +
+                        static_cast<size_t>(max_K + max_P) * sizeof(int) + 16 +
+                        static_cast<size_t>(max_K + max_P) * (sizeof(int64_t) + sizeof(float));
+    cudaError_t err = cudaFuncSetAttribute(backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+    int threads = 128;
+    if (max_P > 512) threads = 256;
+    backward_kernel<<<p.B, threads, smem, stream>>>(p, sparse ? 1 : 0, max_K, max_P);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_t stream) {
+    if (count <= 0) return cudaSuccess;
+    const int threads = 512;
+    int64_t blocks = (count / 4 + threads - 1) / threads;
+    const int64_t max_blocks = static_cast<int64_t>(num_sms) * 4;
+    if (blocks > max_blocks) blocks = max_blocks;
+    if (blocks < 1) blocks = 1;
+    fill_zero_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(dst, count);
+    return cudaGetLastError();
+}
+
+}  // namespace dbs_dev
+
+namespace dbs_dev {
+
+// Exact widening of IEEE binary16 / bfloat16 bit patterns to fp32
+// (the reference converts on the host: src/differentiable_beam.cpp:3275-3305).
+__global__ void widen_16_kernel(const uint16_t* __restrict__ src, float* __restrict__ dst, int64_t count,
+                                int is_bf16) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
+        const uint32_t h = src[i];
+        uint32_t out;
+        if (is_bf16) {
+            out = h << 16;
+        } else {
+            const uint32_t sign = (h & 0x8000u) << 16;
+            const uint32_t exp = (h >> 10) & 0x1Fu;
+            const uint32_t mant = h & 0x3FFu;
+            if (exp == 0) {
+                if (mant == 0) {
+                    out = sign;
+                } else {
+                    // subnormal half: value = mant * 2^-24, renormalise
+                    const int shift = __clz(mant) - 21;      // leading zeros within 10 bits
+                    const uint32_t m = (mant << shift) & 0x3FFu;
+                    const uint32_t e = 113u - static_cast<uint32_t>(shift);
+                    out = sign | (e << 23) | (m << 13);
+                }
+            } else if (exp == 31) {
+                out = sign | 0x7F800000u | (mant << 13);
+            } else {
+                out = sign | ((exp + 112u) << 23) | (mant << 13);
+            }
+        }
+        dst[i] = __uint_as_float(out);
+    }
+}
+
+cudaError_t launch_widen_16(const uint16_t* src, float* dst, int64_t count, int is_bf16, cudaStream_t stream) {
+    if (count <= 0) return cudaSuccess;
+    int64_t blocks = (count + 255) / 256;
+    if (blocks > 65535) blocks = 65535;
+    widen_16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, count, is_bf16);
+    return cudaGetLastError();
+}
+
+}  // namespace dbs_dev

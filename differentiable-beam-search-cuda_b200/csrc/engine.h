@@ -1,0 +1,157 @@
+// Host side of the device engine: turns a batch of per-example decode specs
+// into descriptors, sizes and carves the workspace, and launches the kernels
+// of dbs_kernels.cu on one stream.
+#pragma once
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "dbs_engine.h"
+
+namespace dbs_host {
+
+// Decoder options after the reference's default substitution
+// (from_c_options, src/differentiable_beam.cpp:3145-3177).
+struct Options {
+    int beam_size = 8;
+    int eos_token = -1;
+    float selected_temperature = 1.0f;
+    float soft_topk_temperature = 0.25f;
+    int relaxed_pool_multiplier = 8;
+    int vocab_block = 4096;
+    float length_penalty_alpha = 0.0f;
+    float soft_topk_tolerance = 1.0e-4f;
+    int soft_topk_max_iters = 48;
+    int min_length = 0;
+    int validate_inputs = 1;
+    int64_t max_dense_gradient_elements = 100000000LL;
+};
+
+int pool_size(int beam_size, int multiplier);
+
+// One example of a decode call. banned / forced are DEVICE pointers.
+struct ExampleSpec {
+    int T = 0;
+    int K = 0;
+    int k_stride = 0;            // rows per step in the input layout
+    int64_t x_offset = 0;        // element offset of the example in x
+    int eos = -1;
+    int min_length = 0;          // effective EOS min length
+    const uint8_t* banned = nullptr;
+    const int32_t* forced = nullptr;
+};
+
+// Device output arrays. Selected arrays are tight per example ([T_e, K_e]
+// back to back), pool arrays [T_e, P_e] back to back, finals [K_e].
+struct Outputs {
+    int32_t* parents = nullptr;
+    int32_t* tokens = nullptr;
+    int32_t* lengths = nullptr;
+    float* raw_scores = nullptr;
+    float* scores = nullptr;
+    float* weights = nullptr;
+    uint8_t* from_logprob = nullptr;
+    int32_t* pool_parents = nullptr;
+    int32_t* pool_tokens = nullptr;
+    int32_t* pool_lengths = nullptr;
+    float* pool_raw_scores = nullptr;
+    float* pool_scores = nullptr;
+    float* relaxed_weights = nullptr;
+    uint8_t* pool_from_logprob = nullptr;
+    float* final_raw_scores = nullptr;
+    float* final_scores = nullptr;
+};
+
+struct CallConstraints {
+    float repetition_penalty = 1.0f;  // > 1 enables
+    int no_repeat_ngram = 0;          // > 0 enables
+};
+
+// Element counts of the tight per-example output layout.
+struct Layout {
+    std::vector<int64_t> sel_offset;   // [B]
+    std::vector<int64_t> pool_offset;  // [B]
+    std::vector<int64_t> final_offset; // [B]
+    std::vector<int64_t> grad_offset;  // [B]
+    std::vector<int64_t> sparse_offset;// [B]
+    std::vector<int> P;                // [B]
+    int64_t sel_total = 0;
+    int64_t pool_total = 0;
+    int64_t final_total = 0;
+    int64_t grad_total = 0;
+    int64_t sparse_total = 0;
+};
+
+Layout make_layout(const Options& opt, const std::vector<ExampleSpec>& ex, int V);
+
+// Thrown for errors the reference reports as std::invalid_argument.
+struct InvalidArgument : std::invalid_argument {
+    using std::invalid_argument::invalid_argument;
+};
+struct CudaFailure : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+struct LengthError : std::length_error {
+    using std::length_error::length_error;
+};
+
+void check_cuda(cudaError_t err, const char* what);
+
+// Runs the full forward on `stream`. When `pool` is false only the top-K per
+// step is selected (the pool and relaxed weights are not produced); when
+// `weights` is false the selected softmax is skipped. Returns after the
+// stream has finished; throws InvalidArgument when validation failed.
+struct DecodeStats {
+    unsigned long long row_rescans = 0;
+    unsigned long long merge_fallbacks = 0;
+};
+
+void decode(const Options& opt, const float* d_x, int V, const std::vector<ExampleSpec>& ex,
+            const CallConstraints& cons, const Outputs& out, const Layout& layout, bool pool,
+            bool weights, cudaStream_t stream, DecodeStats* stats, bool synchronize = true);
+
+struct BackwardInputs {
+    // trace (device), tight layout from `decode`
+    const int32_t* parents = nullptr;
+    const int32_t* tokens = nullptr;
+    const int32_t* lengths = nullptr;
+    const float* weights = nullptr;
+    const uint8_t* from_logprob = nullptr;
+    const int32_t* pool_parents = nullptr;
+    const int32_t* pool_tokens = nullptr;
+    const int32_t* pool_lengths = nullptr;
+    const float* relaxed_weights = nullptr;
+    const uint8_t* pool_from_logprob = nullptr;
+    const float* grad_selected = nullptr;  // tight [T_e,K_e]
+    const float* grad_relaxed = nullptr;   // tight [T_e,P_e]
+    const float* grad_final = nullptr;     // [K_e]
+};
+
+struct BackwardOutputs {
+    float* grad_dense = nullptr;       // tight [T_e,K_e,V], zero-filled here
+    int64_t* sparse_indices = nullptr; // [sparse_total]
+    float* sparse_values = nullptr;
+    int64_t* sparse_counts = nullptr;  // [B]
+    float* grad_initial = nullptr;     // [final_total]
+};
+
+void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, const Layout& layout,
+              const BackwardInputs& in, const BackwardOutputs& out, cudaStream_t stream,
+              bool zero_dense = true);
+
+int device_sm_count();
+
+// Live kernel timing: when enabled, every engine launch is bracketed by a pair
+// of CUDA events recorded on the launch stream; read() waits for them and
+// returns the summed device time per kernel.
+enum ProfiledKernel { kValidate = 0, kRowScan = 1, kStepMerge = 2, kWeights = 3, kFillZero = 4, kBackward = 5,
+                      kProfiledKernels = 6 };
+void profile_enable(bool on);
+void profile_reset();
+void profile_read(int kernel, double* total_ms, long long* launches);
+
+}  // namespace dbs_host

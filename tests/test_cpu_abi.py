@@ -1,0 +1,137 @@
+"""The drop-in library loads on a machine without a GPU, exports every symbol
+its headers declare under the reference's version node, and serves the
+host-only parts of the ABI (handles, options, errors, stats, utilities)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import dbs_ctypes as dc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("dbs.h", "dbs_device.h")]
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADERS:
+        text = open(h).read()
+        names |= set(re.findall(r"DBS_EXPORT[^;(]*?\b(dbs_\w+)\s*\(", text, flags=re.S))
+    return names
+
+
+def test_library_exports_every_declared_symbol(libdbs):
+    out = subprocess.run(["nm", "-D", "--defined-only", libdbs._name], capture_output=True, text=True, check=True)
+    exported = {m.group(1) for m in re.finditer(r" T (dbs_\w+)", out.stdout)}
+    declared = declared_symbols()
+    assert len(declared) >= 76 + 4
+    assert declared <= exported, sorted(declared - exported)
+    for name in declared:
+        assert hasattr(libdbs, name)
+
+
+def test_reference_abi_symbol_set_and_version_node(libdbs):
+    out = subprocess.run(["objdump", "-T", libdbs._name], capture_output=True, text=True, check=True)
+    versioned = {m.group(1) for m in re.finditer(r"DBS_0\.6\s+(dbs_\w+)", out.stdout)}
+    assert set(dc.ABI_FUNCTIONS) <= versioned
+    assert len(dc.ABI_FUNCTIONS) == 76
+
+
+def test_version_and_stub_entry_points(libdbs):
+    assert libdbs.dbs_abi_version() == 10
+    assert libdbs.dbs_version_string() == b"1.0.0"
+    assert libdbs.dbs_is_deterministic() == 1
+    buf = ctypes.create_string_buffer(256)
+    assert libdbs.dbs_validate_production_gate_manifest(b"{}", buf, 256) != 0
+    assert b"deprecated" in buf.value
+    assert libdbs.dbs_selected_kernel_name() == b"cuda"
+
+
+def test_create_defaults_errors_and_stats(libdbs):
+    opt = dc.DBSOptionsC()  # all zero -> reference defaults
+    h = ctypes.c_void_p()
+    assert libdbs.dbs_create_ex(opt, ctypes.byref(h)) == 0
+    st = dc.DBSStatsC()
+    assert libdbs.dbs_get_stats(h, ctypes.byref(st)) == 0
+    assert st.abi_version == 10 and st.last_kernel == 5
+    js = ctypes.create_string_buffer(2048)
+    assert libdbs.dbs_get_stats_json(h, js, 2048) == 0
+    assert b'"abi_version":10' in js.value and b'"allocator_calls"' in js.value
+    assert libdbs.dbs_set_deterministic_seed(h, 123456789) == 0
+    assert libdbs.dbs_get_deterministic_seed(h) == 123456789
+    libdbs.dbs_reset_stats(h)
+    # null output pointers
+    assert libdbs.dbs_decode(h, None, 1, 1, None) == -1
+    assert libdbs.dbs_create_ex(opt, None) == -1
+    assert libdbs.dbs_last_global_error() == b"out_handle cannot be null"
+    libdbs.dbs_destroy(h)
+
+
+@pytest.mark.parametrize("field,value,msg", [
+    ("length_penalty_alpha", -0.5, None),         # negative alpha falls back to 0 (from_c_options)
+    ("min_length", -3, None),                     # negative min length falls back to 0
+])
+def test_option_default_substitution(libdbs, field, value, msg):
+    opt = dc.Options()
+    setattr(opt, field, value)
+    h = ctypes.c_void_p()
+    assert libdbs.dbs_create_ex(opt.to_c(), ctypes.byref(h)) == 0
+    libdbs.dbs_destroy(h)
+
+
+def test_invalid_arguments_fail_before_touching_the_device(libdbs):
+    h = ctypes.c_void_p()
+    assert libdbs.dbs_create_ex(dc.Options(beam_size=2).to_c(), ctypes.byref(h)) == 0
+    r = ctypes.c_void_p()
+    x = (ctypes.c_float * 8)()
+    assert libdbs.dbs_decode(h, None, 1, 4, ctypes.byref(r)) == -2
+    assert libdbs.dbs_last_error(h) == b"log_probs cannot be null"
+    assert libdbs.dbs_decode(h, x, 0, 4, ctypes.byref(r)) == -2
+    assert libdbs.dbs_last_error(h) == b"steps must be positive"
+    assert libdbs.dbs_decode(h, x, 1, 0, ctypes.byref(r)) == -2
+    assert libdbs.dbs_last_error(h) == b"vocab_size must be positive"
+    br = ctypes.c_void_p()
+    assert libdbs.dbs_decode_batch(h, x, 0, 1, 4, 1, ctypes.byref(br)) == -1
+    st = dc.DBSStatsC()
+    libdbs.dbs_get_stats(h, ctypes.byref(st))
+    assert st.last_error_category == 1
+    libdbs.dbs_destroy(h)
+
+
+def test_eos_outside_vocab_and_forced_outside_vocab(libdbs):
+    h = ctypes.c_void_p()
+    assert libdbs.dbs_create_ex(dc.Options(beam_size=2, eos_token=9).to_c(), ctypes.byref(h)) == 0
+    x = (ctypes.c_float * 16)()
+    r = ctypes.c_void_p()
+    assert libdbs.dbs_decode(h, x, 2, 4, ctypes.byref(r)) == -2
+    assert libdbs.dbs_last_error(h) == b"eos_token is outside vocab"
+    libdbs.dbs_destroy(h)
+    assert libdbs.dbs_create_ex(dc.Options(beam_size=2).to_c(), ctypes.byref(h)) == 0
+    forced = (ctypes.c_int32 * 2)(1, 7)
+    assert libdbs.dbs_decode_constrained(h, x, 2, 4, None, forced, 0, ctypes.byref(r)) == -2
+    assert libdbs.dbs_last_error(h) == b"forced token is outside vocab"
+    libdbs.dbs_destroy(h)
+
+
+def test_workspace_api(libdbs):
+    ws = ctypes.c_void_p()
+    assert libdbs.dbs_workspace_create(ctypes.byref(ws)) == 0
+    assert libdbs.dbs_workspace_reserve(ws, 4096, 128) == 0
+    assert libdbs.dbs_workspace_allocated_bytes(ws) == 4096 * 4 + 128 * 4
+    assert libdbs.dbs_workspace_reserve(ws, -1, 0) == -1
+    libdbs.dbs_workspace_destroy(ws)
+
+
+def test_null_handles_are_safe(libdbs):
+    assert libdbs.dbs_result_steps(None) == 0
+    assert libdbs.dbs_result_tokens(None) is None
+    assert libdbs.dbs_batch_result_size(None) == 0
+    assert libdbs.dbs_batch_result_at(None, 0) is None
+    assert libdbs.dbs_backward_sparse_logprob_count(None) == 0
+    assert libdbs.dbs_get_stats(None, None) == -1
+    libdbs.dbs_free_result(None)
+    libdbs.dbs_free_batch_result(None)
+    libdbs.dbs_free_backward(None)
+    libdbs.dbs_destroy(None)

@@ -1,0 +1,74 @@
+"""The oracle (plain-C restatement) against the reference's own outputs.
+
+Pins the oracle before it is trusted as the checker: every golden case (the
+reference's handcrafted parity cases, its C ABI test inputs, seeded random
+cases and the first-config workload) must match bit-exactly on ints and
+scores, within the reference's tolerances on weights and weight-dependent
+gradients, and bit-exactly on grad_final-only gradients.
+"""
+import numpy as np
+import pytest
+
+from parity import (assert_decode_equal, assert_sparse_close, config1_input, golden_config1, load_golden)
+
+CASES = load_golden()
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_oracle_matches_reference_golden(oracle_lib, case):
+    o = oracle_lib.options(**case["opts"])
+    fwd = oracle_lib.decode(o, case["x"], case["T"], case["V"], **case["cons"])
+    assert_decode_equal(fwd, case["want"], case["name"])
+    K, P = fwd["K"], fwd["P"]
+    T = case["T"]
+    gsel = ((np.arange(T * K) % 7) - 3).astype(np.float32) * 0.125
+    grel = ((np.arange(T * P) % 11) - 5).astype(np.float32) * 0.03125
+    gfin = (np.arange(K) + 1).astype(np.float32) * 0.2
+    bw = oracle_lib.backward_sparse(fwd, gsel, grel, gfin)
+    assert_sparse_close(bw, case["bw_all"], 8e-3, case["name"])
+    bf = oracle_lib.backward_sparse(fwd, None, None, gfin)
+    for k in ("indices", "values", "grad_initial"):
+        assert np.array_equal(bf[k], case["bw_final"][k]), f"{case['name']} grad_final-only {k}"
+
+
+def test_oracle_matches_reference_first_config(oracle_lib):
+    sha, want = golden_config1()
+    x, got_sha = config1_input()
+    assert got_sha == sha, "regenerated first-config input drifted from the fixture"
+    for b in range(4):
+        o = oracle_lib.options(beam_size=4)
+        fwd = oracle_lib.decode(o, x[b], 4, 32000)
+        assert_decode_equal(fwd, want[b][0], f"config1[{b}]")
+        bw = oracle_lib.backward_sparse(fwd, None, None, np.array([1, 0, 0, 0], np.float32))
+        for k in ("indices", "values", "grad_initial"):
+            assert np.array_equal(bw[k], want[b][1][k])
+
+
+def test_reference_debug_unit_tests_pass():
+    """The reference's own C ABI unit tests, built in Debug (asserts live)."""
+    import os
+    import subprocess
+    exe = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                       "dbs_tests_debug")
+    if not os.path.exists(exe):
+        pytest.skip("reference tests not built here (no reference tree)")
+    out = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0 and "dbs_tests passed" in out.stdout
+
+
+def test_oracle_live_against_reference_random(oracle_lib):
+    """Seeded random cases beyond the fixtures, against oracle/_ref directly."""
+    import dbs_ctypes as dc
+    from oracle import reference_library_path
+    from parity import random_case
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+    ref = dc.load_library(path, device_api=False)
+    rng = np.random.default_rng(99)
+    for i in range(150):
+        opts, x, T, V, cons = random_case(rng)
+        o = oracle_lib.options(**opts)
+        want = dc.decode_and_read(ref, dc.Options(**opts), np.ascontiguousarray(x), T, V, **cons)
+        got = oracle_lib.decode(o, x, T, V, **cons)
+        assert_decode_equal(got, want, f"random {i}")

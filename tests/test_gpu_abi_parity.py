@@ -1,0 +1,244 @@
+"""Parity of the device decoder, called through the drop-in C ABI of
+lib/libdbs.so, against the oracle (plain-C restatement of the reference)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import dbs_ctypes as dc
+from parity import (assert_close_rel, assert_decode_equal, assert_sparse_equal, log_softmax_np,
+                    random_case)
+
+pytestmark = pytest.mark.gpu
+
+
+def _oracle_decode(orc, opts, x, T, V, cons):
+    o = orc.options(**opts)
+    return orc.decode(o, x, T, V, **cons)
+
+
+def _product_decode(lib, opts, x, T, V, cons):
+    return dc.decode_and_read(lib, dc.Options(**opts), np.ascontiguousarray(x), T, V, **cons)
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_random_small_cases_bit_exact(libdbs, oracle_lib, seed):
+    rng = np.random.default_rng(1000 + seed)
+    for case in range(40):
+        opts, x, T, V, cons = random_case(rng)
+        want = _oracle_decode(oracle_lib, opts, x, T, V, cons)
+        got = _product_decode(libdbs, opts, x, T, V, cons)
+        assert_decode_equal(got, want, f"seed={seed} case={case} opts={opts} cons={list(cons)}")
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_sparse_backward_matches_oracle(libdbs, oracle_lib, seed):
+    rng = np.random.default_rng(2000 + seed)
+    for case in range(30):
+        opts, x, T, V, cons = random_case(rng, allow_constraints=False)
+        fwd = _oracle_decode(oracle_lib, opts, x, T, V, {})
+        K, P = fwd["K"], fwd["P"]
+        gf = rng.standard_normal(K).astype(np.float32)
+        use_sel = rng.random() < 0.5
+        use_rel = rng.random() < 0.5
+        gs = rng.standard_normal(T * K).astype(np.float32) if use_sel else None
+        gr = rng.standard_normal(T * P).astype(np.float32) if use_rel else None
+        want = oracle_lib.backward_sparse(fwd, gs, gr, gf)
+        dec = dc.Decoder(libdbs, dc.Options(**opts))
+        r = dec.decode(x, T, V)
+        b = dec.backward(r, gs, gr, gf, mode="sparse")
+        got = dc.read_backward(libdbs, b, K=K)
+        libdbs.dbs_free_backward(b)
+        # grad_final-only gradients use the same float ops as the reference;
+        # weight-dependent terms inherit the weights' tolerance.
+        rtol = 1e-5 if not (use_sel or use_rel) else 8e-3
+        assert_sparse_equal(got, want, rtol, f"seed={seed} case={case}")
+        # dense backward carries the same values
+        if T * K * V <= 200000:
+            bd = dec.backward(r, gs, gr, gf, mode="dense")
+            dense = dc.read_backward(libdbs, bd, dense_count=T * K * V, K=K)
+            libdbs.dbs_free_backward(bd)
+            wd = oracle_lib.backward_dense(fwd, gs, gr, gf)
+            assert_close_rel(dense["grad_log_probs"], wd["grad_log_probs"], rtol, "dense")
+        libdbs.dbs_free_result(r)
+        dec.close()
+
+
+def test_grad_final_backward_is_bit_exact(libdbs, oracle_lib):
+    rng = np.random.default_rng(7)
+    for case in range(40):
+        opts, x, T, V, _ = random_case(rng, allow_constraints=False)
+        fwd = _oracle_decode(oracle_lib, opts, x, T, V, {})
+        gf = rng.standard_normal(fwd["K"]).astype(np.float32)
+        want = oracle_lib.backward_sparse(fwd, None, None, gf)
+        out = dc.decode_and_read(libdbs, dc.Options(**opts), x, T, V, grad_final=gf)
+        b = out["backward"]
+        assert np.array_equal(b["indices"], want["indices"])
+        assert np.array_equal(b["values"], want["values"]), f"case {case}"
+        assert np.array_equal(b["grad_initial"], want["grad_initial"])
+
+
+def test_uniform_batch_matches_per_example(libdbs, oracle_lib):
+    rng = np.random.default_rng(11)
+    B, T, K, V = 5, 6, 4, 301
+    x = log_softmax_np(rng.standard_normal((B, T, K, V)).astype(np.float32) * 2)
+    opts = dict(beam_size=K, eos_token=3, length_penalty_alpha=0.2, selected_temperature=0.7)
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    br = dec.decode_batch(np.ascontiguousarray(x), B, T, V, 4)
+    assert libdbs.dbs_batch_result_size(br) == B
+    for b in range(B):
+        r = libdbs.dbs_batch_result_at(br, b)
+        got = dc.read_result(libdbs, r)
+        want = _oracle_decode(oracle_lib, opts, x[b], T, V, {})
+        assert_decode_equal(got, want, f"example {b}")
+    libdbs.dbs_free_batch_result(br)
+    dec.close()
+
+
+def test_variable_batch_matches_per_example(libdbs, oracle_lib):
+    rng = np.random.default_rng(12)
+    B, maxT, maxK, V = 6, 7, 5, 97
+    x = log_softmax_np(rng.standard_normal((B, maxT, maxK, V)).astype(np.float32) * 1.5)
+    steps = rng.integers(1, maxT + 1, B).astype(np.int32)
+    beams = rng.integers(1, maxK + 1, B).astype(np.int32)
+    eos = rng.integers(-1, 6, B).astype(np.int32)
+    minlen = rng.integers(-1, 4, B).astype(np.int32)
+    banned = (rng.random((B, V)) < 0.1).astype(np.uint8)
+    forced = np.where(rng.random((B, maxT)) < 0.2, rng.integers(0, V, (B, maxT)), -1).astype(np.int32)
+    base = dict(beam_size=3, relaxed_pool_multiplier=4, length_penalty_alpha=0.35)
+    dec = dc.Decoder(libdbs, dc.Options(**base))
+    br = dec.decode_batch_variable(np.ascontiguousarray(x), B, maxT, maxK, V, steps, beams, eos, minlen, banned,
+                                   forced)
+    for b in range(B):
+        T, K = int(steps[b]), int(beams[b])
+        opts = dict(base, beam_size=K, eos_token=int(eos[b]), min_length=max(0, int(minlen[b])))
+        cons = dict(banned=banned[b], forced=forced[b, :T].copy(), min_length=int(minlen[b]))
+        want = _oracle_decode(oracle_lib, opts, np.ascontiguousarray(x[b, :T, :K]), T, V, cons)
+        got = dc.read_result(libdbs, libdbs.dbs_batch_result_at(br, b))
+        assert_decode_equal(got, want, f"example {b}")
+    libdbs.dbs_free_batch_result(br)
+    dec.close()
+
+
+@pytest.mark.parametrize("V", [31999, 32000, 32003, 50257])
+def test_vocab_sized_rows_and_alignment(libdbs, oracle_lib, V):
+    rng = np.random.default_rng(V)
+    T, K = 4, 8
+    bias = -1.1 * np.log(np.arange(V, dtype=np.float32) + 1.0)
+    x = log_softmax_np(2.0 * rng.standard_normal((T, K, V)).astype(np.float32) + bias)
+    opts = dict(beam_size=K, eos_token=2, length_penalty_alpha=0.2, selected_temperature=0.7)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, {})
+    got = _product_decode(libdbs, opts, x, T, V, {})
+    assert_decode_equal(got, want, f"V={V}")
+
+
+def test_large_pool(libdbs, oracle_lib):
+    rng = np.random.default_rng(5)
+    T, K, V = 3, 32, 5000   # P = 256
+    x = log_softmax_np(rng.standard_normal((T, K, V)).astype(np.float32))
+    opts = dict(beam_size=K)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, {})
+    got = _product_decode(libdbs, opts, x, T, V, {})
+    assert_decode_equal(got, want, "K=32")
+
+
+def test_dense_ties_force_the_rescan_path(libdbs, oracle_lib):
+    # every row is constant: every list boundary is an exact tie, so the step
+    # merge has to rescan rows to prove the token order
+    T, K, V = 3, 4, 300
+    x = np.full((T, K, V), -1.0, dtype=np.float32)
+    x[:, :, 7] = -0.5
+    x[1, 2, 200:260] = -0.25
+    opts = dict(beam_size=K, relaxed_pool_multiplier=3)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, {})
+    got = _product_decode(libdbs, opts, x, T, V, {})
+    assert_decode_equal(got, want, "ties")
+
+
+def test_nan_and_pos_inf_rejected_negative_inf_accepted(libdbs):
+    T, K, V = 2, 2, 16
+    x = log_softmax_np(np.random.default_rng(0).standard_normal((T, K, V)).astype(np.float32))
+    for bad in (np.nan, np.inf):
+        y = x.copy()
+        y[0, 0, 0] = bad
+        dec = dc.Decoder(libdbs, dc.Options(beam_size=K))
+        with pytest.raises(dc.DBSError, match="NaN or \\+Inf") as ei:
+            dec.decode(y, T, V)
+        assert ei.value.rc == -2
+        st = dec.stats()
+        assert st.last_error_category == 1
+        dec.close()
+    y = x.copy()
+    y[0, 0, 0] = -np.inf
+    out = dc.decode_and_read(libdbs, dc.Options(beam_size=K), y, T, V)
+    assert np.isfinite(out["final_scores"]).all()
+
+
+def test_validation_disabled_skips_pos_inf(libdbs, oracle_lib):
+    T, K, V = 2, 3, 8
+    x = np.full((T, K, V), -4.0, dtype=np.float32)
+    x[:, :, 1] = -0.05
+    x[0, 0, 2] = np.inf
+    x[1, 1, 5] = np.inf
+    opts = dict(beam_size=K, validate_inputs=0, relaxed_pool_multiplier=3)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, {})
+    got = _product_decode(libdbs, opts, x, T, V, {})
+    assert_decode_equal(got, want, "+inf")
+
+
+def test_token_filter_is_rejected(libdbs):
+    T, K, V = 1, 2, 5
+    x = np.full((T, K, V), -1.0, dtype=np.float32)
+    dec = dc.Decoder(libdbs, dc.Options(beam_size=K))
+    cb = dc.TOKEN_FILTER_FN(lambda *a: 1)
+    with pytest.raises(dc.DBSError, match="token_filter"):
+        dec.decode_constrained_ex(x, T, V, token_filter=cb)
+    dec.close()
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_typed_decode_widening(libdbs, oracle_lib, dtype):
+    rng = np.random.default_rng(3)
+    T, K, V = 3, 4, 200
+    x = log_softmax_np(rng.standard_normal((T, K, V)).astype(np.float32))
+    if dtype == "f16":
+        h = x.astype(np.float16)
+        bits = h.view(np.uint16)
+        wide = h.astype(np.float32)
+        code = dc.DBS_DTYPE_F16
+    else:
+        bits = (x.view(np.uint32) >> 16).astype(np.uint16)
+        wide = (bits.astype(np.uint32) << 16).view(np.float32)
+        code = dc.DBS_DTYPE_BF16
+    opts = dict(beam_size=K)
+    want = _oracle_decode(oracle_lib, opts, wide, T, V, {})
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    r = ctypes.c_void_p()
+    rc = libdbs.dbs_decode_typed(dec.h, bits.ctypes.data_as(ctypes.c_void_p), code, T, V, ctypes.byref(r))
+    assert rc == 0, libdbs.dbs_last_error(dec.h)
+    got = dc.read_result(libdbs, r)
+    libdbs.dbs_free_result(r)
+    dec.close()
+    assert_decode_equal(got, want, dtype)
+
+
+def test_model_step_decode(libdbs):
+    # the reference's own model-step case (tests/dbs_tests.cpp:158-209)
+    @dc.MODEL_STEP_FN
+    def step(user, batch, t, prev_tokens, prev_scores, K, V, out):
+        for k in range(K):
+            for v in range(V):
+                out[k * V + v] = -10.0
+            preferred = k if t == 0 else (prev_tokens[k] + 1) % V
+            out[k * V + preferred] = 0.0
+        return 0
+
+    dec = dc.Decoder(libdbs, dc.Options(beam_size=2, relaxed_pool_multiplier=4, vocab_block=64))
+    r = ctypes.c_void_p()
+    assert libdbs.dbs_decode_model_steps(dec.h, step, None, 0, 3, 6, ctypes.byref(r)) == 0
+    assert libdbs.dbs_result_steps(r) == 3
+    tok = dc.read_result(libdbs, r)["tokens"]
+    assert tok[0] == 0
+    assert dec.stats().used_model_step_callback == 1
+    libdbs.dbs_free_result(r)
+    dec.close()
