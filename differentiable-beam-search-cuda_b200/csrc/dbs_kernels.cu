@@ -407,7 +407,7 @@ __device__ __forceinline__ bool in_list(const int32_t* a, int n, int v) {
 }
 
 __global__ void __launch_bounds__(kMergeThreads) step_merge_kernel(DecodeParams p, int cand_cap,
-                                                                   int seq_T) {
+                                                                   int seq_T, int seq_K) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     const ExampleDesc d = p.desc[e];
@@ -439,7 +439,8 @@ __global__ void __launch_bounds__(kMergeThreads) step_merge_kernel(DecodeParams 
     const bool need_seq = use_rep || use_ngram;
     // Beam prefixes (only with repetition penalty / n-gram constraints):
     // [2][K][seq_T] in global scratch, plus n-gram blocked sets [K][seq_T].
-    int32_t* seq_a = need_seq ? p.seq_scratch + static_cast<int64_t>(e) * 3 * K * seq_T : nullptr;
+    // per-example region of 3 * seq_K * seq_T (seq_K = largest K of the call)
+    int32_t* seq_a = need_seq ? p.seq_scratch + static_cast<int64_t>(e) * 3 * seq_K * seq_T : nullptr;
     int32_t* seq_b = need_seq ? seq_a + static_cast<int64_t>(K) * seq_T : nullptr;
     int32_t* blk = need_seq ? seq_b + static_cast<int64_t>(K) * seq_T : nullptr;
     __shared__ int seq_len_a[1024];
@@ -1073,7 +1074,7 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
                                            static_cast<int>(smem));
     if (err != cudaSuccess) return err;
     (void)need_sequences;
-    step_merge_kernel<<<p.B, threads, smem, stream>>>(p, cand_cap, max_T);
+    step_merge_kernel<<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K);
     return cudaGetLastError();
 }
 
