@@ -55,6 +55,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override B (profiling a smaller case only; bench lines use the default 64)")
     return ap.parse_args()
 
 
@@ -245,6 +247,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     B, T, K, V = (WORKLOAD[k] for k in "BTKV")
+    if args.batch:
+        B = args.batch
     elems = B * T * K * V
     opts = ext.DBSOptions(**OPTIONS)
     lib = ext._library()
