@@ -9,6 +9,9 @@
 #include <cfloat>
 #include <cmath>
 #include <cstdint>
+#include <mutex>
+#include <tuple>
+#include <vector>
 
 namespace dbs_dev {
 
@@ -179,172 +182,370 @@ __global__ void validate_kernel(DecodeParams p) {
 // ---------------------------------------------------------------------------
 // 1. Row scan: best C entries of every log-prob row.
 //
-// Each CTA owns a contiguous range of rows. A row is streamed with 128-bit
-// loads; an element survives when lp >= T_pass, everything else only feeds a
-// running max (the bound on what was dropped). Survivors that are finite and
-// statically allowed (banned / EOS-before-min-length) are appended to a
-// shared buffer; when the buffer nears capacity it is sorted and cut back to C
-// entries, and T_pass rises to just above the C-th kept value (every later
-// element has a larger token, so an equal value can no longer win).
+// One warp owns one row at a time; rows are claimed dynamically from a
+// global counter, so the load stays balanced to the last row. Each warp
+// streams its row body (the 16-byte aligned part) through a private ring of
+// kScanStages shared-memory chunks filled by 1-D bulk copies
+// (cp.async.bulk, no multicast) that lane 0 issues ahead of the consumption
+// point; the prefetch runs on into the next claimed row, so the copy engine
+// never waits for the per-row bookkeeping. The unaligned head / tail
+// elements are read directly.
 //
-// T_pass starts from a guess: the (1.5C)-th best value of the previous row of
-// this CTA. If fewer than C entries survive a guessed threshold the row is
-// rescanned with no threshold, so the list is always the exact top-C.
+// Selection is exact and single-pass. An element survives when
+// lp >= threshold; everything else only feeds a running max (the bound on what
+// was dropped). Finite, statically allowed survivors (banned / EOS before
+// min_length) are appended to the warp's buffer with a ballot; a full buffer
+// is sorted and cut back to C entries, after which the threshold is "strictly
+// above the C-th kept value" (later elements have larger tokens, so an equal
+// value can no longer win). The threshold starts at the C-th largest of the
+// 32 lane maxima of the first chunk (each lane maximum is a distinct finite,
+// allowed element, so at least C candidates reach it), which removes most of
+// the first chunk without any guess from other rows.
 // ---------------------------------------------------------------------------
-template <int NT, int U>
-struct RowScanShared {
-    int cnt;
-    float tpass;
-    float evict;
-    float guess;
-    int guess_c;
-    float red[NT / 32];
-};
+constexpr int kScanStages = 4;
+constexpr int kScanChunkF4 = 128;       // 2 KB per chunk: 4 float4 per lane
+constexpr int kScanWarpsPerCta = 4;
+constexpr int kScanAppendsPerChunk = kScanChunkF4 * 4;
 
-template <int NT, int U>
-__device__ bool scan_one_row(const float* __restrict__ row, int V, int C, float thr,
-                             const uint8_t* __restrict__ banned, int eos, bool eos_blocked,
-                             uint64_t* __restrict__ buf, int cap, RowScanShared<NT, U>& sh,
-                             uint64_t* __restrict__ out, int32_t* out_count, float* out_bound,
-                             bool write_guess) {
-    const int tid = threadIdx.x;
-    constexpr int kIter = NT * U * 4;
-    __syncthreads();
-    if (tid == 0) {
-        sh.cnt = 0;
-        sh.tpass = fmaxf(thr, -FLT_MAX);
-        sh.evict = -INFINITY;
-    }
-    __syncthreads();
-    float tp = sh.tpass;
-    float rej = -INFINITY;
-
-    auto consider = [&](int v, float lp) {
-        if (lp >= tp) {
-            if (lp != INFINITY && !(banned && banned[v]) && !(eos_blocked && v == eos)) {
-                const int pos = atomicAdd(&sh.cnt, 1);
-                buf[pos] = list_key(lp, v);
-            }
-        } else {
-            rej = fmaxf(rej, lp);
-        }
-    };
-    auto compact = [&]() {
-        // all threads
-        const int n = sh.cnt;
-        block_sort_desc_u64(buf, n);
-        if (tid == 0 && n > C) {
-            sh.evict = fmaxf(sh.evict, list_lp(buf[C]));
-            sh.tpass = fmaxf(sh.tpass, nextafterf(list_lp(buf[C - 1]), INFINITY));
-            sh.cnt = C;
-        }
-        __syncthreads();
-    };
-
-    const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
-    int h = static_cast<int>(((16u - (addr & 15u)) & 15u) >> 2);
-    if (h > V) h = V;
-    if (tid < h) consider(tid, row[tid]);
-    const int nv = (V - h) >> 2;
-    const float4* p4 = reinterpret_cast<const float4*>(row + h);
-    for (int base = 0; base < nv; base += NT * U) {
-        float4 vals[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int idx = base + u * NT + tid;
-            if (idx < nv) vals[u] = ldg_stream(p4 + idx);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int idx = base + u * NT + tid;
-            if (idx < nv) {
-                const int v0 = h + 4 * idx;
-                consider(v0 + 0, vals[u].x);
-                consider(v0 + 1, vals[u].y);
-                consider(v0 + 2, vals[u].z);
-                consider(v0 + 3, vals[u].w);
+__device__ __forceinline__ void warp_sort_desc_u64(uint64_t* a, int n, int lane) {
+    if (n <= 1) { __syncwarp(); return; }
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    const int half = n2 >> 1;
+    for (int size = 2; size <= n2; size <<= 1) {
+        const int hs = size >> 1;
+        for (int pid = lane; pid < half; pid += 32) {
+            const int x = pid & (hs - 1);
+            const int blk = (pid - x) << 1;
+            const int i = blk + x;
+            const int j = blk + size - 1 - x;
+            if (j < n) {
+                const uint64_t ai = a[i], aj = a[j];
+                if (ai < aj) { a[i] = aj; a[j] = ai; }
             }
         }
-        __syncthreads();
-        if (sh.cnt > cap - kIter) compact();
-        tp = sh.tpass;
-    }
-    const int tail0 = h + 4 * nv;
-    if (tid < V - tail0) consider(tail0 + tid, row[tail0 + tid]);
-    __syncthreads();
-
-    const int n = sh.cnt;
-    if (thr > -INFINITY && n < C) return false;  // guess too high: caller rescans
-    block_sort_desc_u64(buf, n);
-    // bound = max over everything dropped
-    float r = warp_max(rej);
-    if ((tid & 31) == 0) sh.red[tid >> 5] = r;
-    __syncthreads();
-    const int keep = n < C ? n : C;
-    for (int i = tid; i < keep; i += NT) out[i] = buf[i];
-    if (tid == 0) {
-        float b = sh.red[0];
-        for (int w = 1; w < NT / 32; ++w) b = fmaxf(b, sh.red[w]);
-        b = fmaxf(b, sh.evict);
-        if (n > C) b = fmaxf(b, list_lp(buf[C]));
-        *out_count = keep;
-        *out_bound = b;
-        if (write_guess) {
-            int gi = C + (C >> 1) + 2;
-            if (gi > n) gi = n;
-            sh.guess = gi > 0 ? list_lp(buf[gi - 1]) : -INFINITY;
-            sh.guess_c = C;
+        __syncwarp();
+        for (int st = size >> 2; st > 0; st >>= 1) {
+            for (int pid = lane; pid < half; pid += 32) {
+                const int i = ((pid & ~(st - 1)) << 1) | (pid & (st - 1));
+                const int j = i + st;
+                if (j < n) {
+                    const uint64_t ai = a[i], aj = a[j];
+                    if (ai < aj) { a[i] = aj; a[j] = ai; }
+                }
+            }
+            __syncwarp();
         }
     }
-    return true;
 }
 
-template <int NT, int U>
-__global__ void __launch_bounds__(NT) row_scan_kernel(DecodeParams p, int cap, int64_t rows_per_cta) {
-    extern __shared__ __align__(16) uint64_t buf[];
-    __shared__ RowScanShared<NT, U> sh;
-    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
-    int64_t r1 = r0 + rows_per_cta;
-    if (r1 > p.total_rows) r1 = p.total_rows;
-    if (r0 >= r1) return;
-    if (threadIdx.x == 0) {
-        sh.guess = -INFINITY;
-        sh.guess_c = -1;
+// k-th largest (1-based, k <= 32) of one float per lane, broadcast to all lanes.
+__device__ __forceinline__ float warp_kth_largest(float v, int k, int lane) {
+    // bitonic sort descending across the 32 lanes
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int st = size >> 1; st > 0; st >>= 1) {
+            const float o = __shfl_xor_sync(0xFFFFFFFFu, v, st);
+            const bool lower = (lane & st) == 0;
+            const bool desc = (lane & size) == 0;
+            // keep the larger value in the lower lane of a descending run
+            const float hi = fmaxf(v, o), lo = fminf(v, o);
+            v = (lower == desc) ? hi : lo;
+        }
     }
-    int e = find_example(p.row_prefix, p.B, r0);
-    const int V = p.V;
-    for (int64_t r = r0; r < r1; ++r) {
-        while (r >= p.row_prefix[e + 1]) ++e;
-        const ExampleDesc& d = p.desc[e];
-        const int64_t lr = r - d.row_begin;
-        const int t = static_cast<int>(lr / d.K);
-        const int k = static_cast<int>(lr - static_cast<int64_t>(t) * d.K);
-        const float* row = p.x + d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
-        uint64_t* out = p.lists + d.list_offset + lr * d.C;
-        const int forced = d.forced ? d.forced[t] : -1;
-        const bool eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
-        if (forced >= 0) {
-            // Forced step: only the forced token is a candidate of this row.
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                const float lp = row[forced];
-                const bool ok = isfinite(lp) && !(d.banned && d.banned[forced]) &&
-                                !(eos_blocked && forced == d.eos);
-                if (ok) out[0] = list_key(lp, forced);
-                p.list_count[r] = ok ? 1 : 0;
-                p.list_bound[r] = -INFINITY;
+    return __shfl_sync(0xFFFFFFFFu, v, k - 1);
+}
+
+// --- 1-D TMA (cp.async.bulk) + mbarrier helpers ------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Non-multicast bulk copy global -> this CTA's shared memory; completion is
+// reported as transaction bytes on `bar`. dst, src and bytes are multiples
+// of 16 (the row body is 16-byte aligned by construction).
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+// Bounded wait: gives up after 2^22 polls (seconds) and reports the timeout
+// through the error counter instead of hanging.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned long long* err) {
+    for (uint32_t i = 0; i < (1u << 22); ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicExch(err, 1ull);
+    return false;
+}
+
+struct RowJob {
+    const float* row;
+    int64_t r;
+    int64_t list_at;  // first list entry of the row
+    int C;
+    int forced;
+    int eos;
+    bool eos_blocked;
+    const uint8_t* banned;
+    int h;       // unaligned head elements
+    int nv;      // float4 in the aligned body
+    int chunks;
+};
+
+__device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int& e) {
+    while (r >= p.row_prefix[e + 1]) ++e;
+    const ExampleDesc& d = p.desc[e];
+    RowJob j;
+    const int64_t lr = r - d.row_begin;
+    const int t = static_cast<int>(lr / d.K);
+    const int k = static_cast<int>(lr - static_cast<int64_t>(t) * d.K);
+    j.row = p.x + d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * p.V;
+    j.r = r;
+    j.list_at = d.list_offset + lr * d.C;
+    j.C = d.C;
+    j.forced = d.forced ? d.forced[t] : -1;
+    j.eos = d.eos;
+    j.eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
+    j.banned = d.banned;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(j.row);
+    int h = static_cast<int>(((16u - (addr & 15u)) & 15u) >> 2);
+    if (h > p.V) h = p.V;
+    j.h = h;
+    j.nv = (p.V - h) >> 2;
+    j.chunks = j.forced >= 0 ? 0 : (j.nv + kScanChunkF4 - 1) / kScanChunkF4;
+    return j;
+}
+
+__global__ void __launch_bounds__(kScanWarpsPerCta * 32) row_scan_kernel(DecodeParams p, int capw) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    constexpr unsigned FULL = 0xFFFFFFFFu;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // per-warp region: ring | barriers | survivor buffer
+    const size_t ring_bytes = static_cast<size_t>(kScanStages) * kScanChunkF4 * 16;
+    const size_t warp_bytes = ring_bytes + kScanStages * sizeof(uint64_t) + static_cast<size_t>(capw) * sizeof(uint64_t);
+    unsigned char* base = smem_raw + warp * ((warp_bytes + 127) & ~static_cast<size_t>(127));
+    float4* ring = reinterpret_cast<float4*>(base);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + ring_bytes);
+    uint64_t* buf = full + kScanStages;
+    unsigned long long* err = p.counters ? p.counters + 3 : nullptr;
+    unsigned long long* next_row = p.counters + 2;
+    const unsigned lt_mask = (1u << lane) - 1u;
+
+    if (lane == 0) {
+        for (int s = 0; s < kScanStages; ++s) mbar_init(full + s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+
+    auto claim = [&]() -> int64_t {
+        unsigned long long r = 0;
+        if (lane == 0) r = atomicAdd(next_row, 1ull);
+        r = __shfl_sync(FULL, r, 0);
+        return static_cast<int64_t>(r);
+    };
+
+    // two-row window: `cur` is consumed, `nxt` is being prefetched
+    int e_cur = 0, e_nxt = 0;
+    int64_t r_cur = claim();
+    if (r_cur >= p.total_rows) return;
+    e_cur = find_example(p.row_prefix, p.B, r_cur);
+    RowJob cur = make_job(p, r_cur, e_cur);
+    e_nxt = e_cur;
+    RowJob nxt = cur;
+    bool have_nxt = false;
+    // issue cursor
+    bool issue_in_cur = true;  // issuing chunks of cur (else of nxt)
+    int ic = 0;                // next chunk to issue within its row
+    uint32_t n_issued = 0, n_used = 0;
+
+    auto issue_more = [&]() {
+        // lane 0 keeps up to kScanStages chunks in flight, crossing into nxt
+        while (n_issued < n_used + kScanStages) {
+            RowJob* j = issue_in_cur ? &cur : &nxt;
+            if (!issue_in_cur && !have_nxt) break;
+            if (ic >= j->chunks) {
+                if (!issue_in_cur) break;  // at most one row ahead
+                // move the issue cursor to the next claimed row
+                if (!have_nxt) {
+                    const int64_t rn = claim();
+                    if (rn >= p.total_rows) break;
+                    nxt = make_job(p, rn, e_nxt);
+                    have_nxt = true;
+                }
+                issue_in_cur = false;
+                ic = 0;
+                continue;
             }
-            continue;
+            const int s = static_cast<int>(n_issued % kScanStages);
+            const int f0 = ic * kScanChunkF4;
+            const int nf = min(kScanChunkF4, j->nv - f0);
+            if (lane == 0) {
+                const uint32_t bytes = static_cast<uint32_t>(nf) * 16u;
+                mbar_arrive_expect_tx(full + s, bytes);
+                bulk_copy_g2s(ring + static_cast<size_t>(s) * kScanChunkF4,
+                              reinterpret_cast<const float4*>(j->row + j->h) + f0, bytes, full + s);
+            }
+            ++ic;
+            ++n_issued;
         }
-        __syncthreads();
-        const float thr = (sh.guess_c == d.C) ? sh.guess : -INFINITY;
-        bool ok = scan_one_row<NT, U>(row, V, d.C, thr, d.banned, d.eos, eos_blocked, buf, cap, sh,
-                                      out, p.list_count + r, p.list_bound + r, true);
-        if (!ok) {
-            if (threadIdx.x == 0 && p.counters) atomicAdd(p.counters + 0, 1ull);
-            scan_one_row<NT, U>(row, V, d.C, -INFINITY, d.banned, d.eos, eos_blocked, buf, cap, sh,
-                                out, p.list_count + r, p.list_bound + r, true);
+    };
+
+    while (true) {
+        issue_more();
+        const RowJob& j = cur;
+        const int C = j.C;
+        uint64_t* out = p.lists + j.list_at;
+        if (j.forced >= 0) {
+            // Forced step: only the forced token is a candidate of this row.
+            if (lane == 0) {
+                const float lp = j.row[j.forced];
+                const bool ok = isfinite(lp) && !(j.banned && j.banned[j.forced]) &&
+                                !(j.eos_blocked && j.forced == j.eos);
+                if (ok) out[0] = list_key(lp, j.forced);
+                p.list_count[j.r] = ok ? 1 : 0;
+                p.list_bound[j.r] = -INFINITY;
+            }
+        } else {
+            int cnt = 0;
+            float thr = -FLT_MAX;
+            float rej = -INFINITY;
+            float evict = -INFINITY;
+            auto allowed = [&](int v, float lp) {
+                return lp != INFINITY && !(j.banned && j.banned[v]) && !(j.eos_blocked && v == j.eos);
+            };
+            auto consider = [&](bool in, int v, float lp) {
+                const bool pass = in && lp >= thr;
+                if (in && !pass) rej = fmaxf(rej, lp);
+                const bool keep = pass && allowed(v, lp);
+                const unsigned b = __ballot_sync(FULL, keep);
+                if (keep) buf[cnt + __popc(b & lt_mask)] = list_key(lp, v);
+                cnt += __popc(b);
+            };
+            auto compact = [&]() {
+                __syncwarp();
+                warp_sort_desc_u64(buf, cnt, lane);
+                if (cnt > C) {
+                    evict = fmaxf(evict, list_lp(buf[C]));
+                    thr = fmaxf(thr, nextafterf(list_lp(buf[C - 1]), INFINITY));
+                    cnt = C;
+                }
+                __syncwarp();
+            };
+            {  // unaligned head, first in token order
+                const bool in = lane < j.h;
+                const float lp = in ? j.row[lane] : -INFINITY;
+                consider(in, lane, lp);
+            }
+            for (int c = 0; c < j.chunks; ++c) {
+                const int s = static_cast<int>(n_used % kScanStages);
+                const uint32_t parity = (n_used / kScanStages) & 1u;
+                if (!mbar_wait(full + s, parity, err)) return;
+                const int nf = min(kScanChunkF4, j.nv - c * kScanChunkF4);
+                const float4* st = ring + static_cast<size_t>(s) * kScanChunkF4;
+                float4 q[4];
+                bool in[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int idx = u * 32 + lane;
+                    in[u] = idx < nf;
+                    q[u] = in[u] ? st[idx] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                }
+                if (c == 0 && C <= 32) {
+                    // threshold bootstrap: C-th largest lane maximum over
+                    // finite, allowed elements of the first chunk
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        if (!in[u]) continue;
+                        const int v0 = j.h + 4 * (u * 32 + lane);
+                        if (isfinite(q[u].x) && allowed(v0 + 0, q[u].x)) mx = fmaxf(mx, q[u].x);
+                        if (isfinite(q[u].y) && allowed(v0 + 1, q[u].y)) mx = fmaxf(mx, q[u].y);
+                        if (isfinite(q[u].z) && allowed(v0 + 2, q[u].z)) mx = fmaxf(mx, q[u].z);
+                        if (isfinite(q[u].w) && allowed(v0 + 3, q[u].w)) mx = fmaxf(mx, q[u].w);
+                    }
+                    const float kth = warp_kth_largest(mx, C, lane);
+                    if (kth > thr) thr = kth;
+                }
+                // the stage is in registers: let lane 0 refill it
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                ++n_used;
+                issue_more();
+                const int tok0 = j.h + 4 * c * kScanChunkF4;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const bool p0 = q[u].x >= thr, p1 = q[u].y >= thr, p2 = q[u].z >= thr, p3 = q[u].w >= thr;
+                    if (in[u]) {
+                        if (!p0) rej = fmaxf(rej, q[u].x);
+                        if (!p1) rej = fmaxf(rej, q[u].y);
+                        if (!p2) rej = fmaxf(rej, q[u].z);
+                        if (!p3) rej = fmaxf(rej, q[u].w);
+                    }
+                    if (__any_sync(FULL, in[u] && (p0 | p1 | p2 | p3))) {
+                        const int v0 = tok0 + 4 * (u * 32 + lane);
+                        consider(in[u], v0 + 0, q[u].x);
+                        consider(in[u], v0 + 1, q[u].y);
+                        consider(in[u], v0 + 2, q[u].z);
+                        consider(in[u], v0 + 3, q[u].w);
+                    }
+                }
+                if (cnt > capw - kScanAppendsPerChunk - 8) compact();
+            }
+            {  // unaligned tail, last in token order
+                const int t0 = j.h + 4 * j.nv;
+                const bool in = lane < p.V - t0;
+                const float lp = in ? j.row[t0 + lane] : -INFINITY;
+                consider(in, t0 + lane, lp);
+            }
+            __syncwarp();
+            warp_sort_desc_u64(buf, cnt, lane);
+            const int keep = cnt < C ? cnt : C;
+            for (int i = lane; i < keep; i += 32) out[i] = buf[i];
+            rej = warp_max(rej);
+            if (lane == 0) {
+                float b = fmaxf(rej, evict);
+                if (cnt > C) b = fmaxf(b, list_lp(buf[C]));
+                p.list_count[j.r] = keep;
+                p.list_bound[j.r] = b;
+            }
+            __syncwarp();
         }
+        // advance to the next claimed row
+        if (issue_in_cur) {
+            // nothing of the next row was issued yet
+            const int64_t rn = have_nxt ? nxt.r : claim();
+            if (!have_nxt) {
+                if (rn >= p.total_rows) return;
+                nxt = make_job(p, rn, e_nxt);
+            }
+            cur = nxt;
+            have_nxt = false;
+            ic = 0;
+        } else {
+            cur = nxt;
+            have_nxt = false;
+            issue_in_cur = true;
+        }
+        e_cur = e_nxt;
     }
 }
 
@@ -1029,33 +1230,72 @@ __global__ void fill_zero_kernel(float* __restrict__ dst, int64_t count) {
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
+
+// cudaFuncSetAttribute / occupancy results are cached per (kernel, device):
+// the runtime calls cost microseconds and the launchers run on every decode.
+static std::mutex g_attr_mu;
+static std::vector<std::tuple<const void*, int, size_t>> g_smem_set;
+static std::vector<std::tuple<int, size_t, int>> g_row_scan_occ;
+
+static cudaError_t ensure_dynamic_smem(const void* fn, size_t smem) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    for (auto& e : g_smem_set) {
+        if (std::get<0>(e) == fn && std::get<1>(e) == dev) {
+            if (std::get<2>(e) >= smem) return cudaSuccess;
+            err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (err == cudaSuccess) std::get<2>(e) = smem;
+            return err;
+        }
+    }
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err == cudaSuccess) g_smem_set.emplace_back(fn, dev, smem);
+    return err;
+}
+
 cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream) {
     validate_kernel<<<p.B, 1024, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
-static int row_scan_cap(int max_C) {
-    constexpr int kIter = kRowScanThreads * 4 * 4;
-    return kIter + max_C + 8;
+// per-warp survivor buffer: C kept + one chunk of appends + head/tail
+static int row_scan_capw(int max_C) { return max_C + kScanAppendsPerChunk + 16; }
+
+static size_t row_scan_smem(int capw) {
+    const size_t warp_bytes = static_cast<size_t>(kScanStages) * kScanChunkF4 * 16 + kScanStages * sizeof(uint64_t) +
+                              static_cast<size_t>(capw) * sizeof(uint64_t);
+    return static_cast<size_t>(kScanWarpsPerCta) * ((warp_bytes + 127) & ~static_cast<size_t>(127));
 }
 
 cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream) {
     if (p.total_rows <= 0) return cudaSuccess;
-    const int cap = row_scan_cap(max_C);
-    const size_t smem = static_cast<size_t>(cap) * sizeof(uint64_t);
-    auto kern = row_scan_kernel<kRowScanThreads, 4>;
-    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
+    const int capw = row_scan_capw(max_C);
+    const int threads = kScanWarpsPerCta * 32;
+    const size_t smem = row_scan_smem(capw);
+    cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(row_scan_kernel), smem);
     if (err != cudaSuccess) return err;
-    int per_sm = 0;
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowScanThreads, smem);
+    int dev = 0;
+    err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
+    int per_sm = -1;
+    {
+        std::lock_guard<std::mutex> lock(g_attr_mu);
+        for (auto& e : g_row_scan_occ)
+            if (std::get<0>(e) == dev && std::get<1>(e) == smem) per_sm = std::get<2>(e);
+    }
+    if (per_sm < 0) {
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_scan_kernel, threads, smem);
+        if (err != cudaSuccess) return err;
+        std::lock_guard<std::mutex> lock(g_attr_mu);
+        g_row_scan_occ.emplace_back(dev, smem, per_sm);
+    }
     if (per_sm < 1) per_sm = 1;
     int64_t ctas = static_cast<int64_t>(num_sms) * per_sm;
-    if (ctas > p.total_rows) ctas = p.total_rows;
-    const int64_t rows_per_cta = (p.total_rows + ctas - 1) / ctas;
-    ctas = (p.total_rows + rows_per_cta - 1) / rows_per_cta;
-    kern<<<static_cast<unsigned>(ctas), kRowScanThreads, smem, stream>>>(p, cap, rows_per_cta);
+    const int64_t need = (p.total_rows + kScanWarpsPerCta - 1) / kScanWarpsPerCta;
+    if (ctas > need) ctas = need;
+    row_scan_kernel<<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw);
     return cudaGetLastError();
 }
 
@@ -1070,8 +1310,7 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     int threads = 64;
     while (threads < kMergeThreads && threads * 2 <= (M + 1) / 2) threads <<= 1;
     if (threads < 128 && max_K > 64) threads = 128;
-    cudaError_t err = cudaFuncSetAttribute(step_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
+    cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(step_merge_kernel), smem);
     if (err != cudaSuccess) return err;
     (void)need_sequences;
     step_merge_kernel<<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K);
@@ -1087,7 +1326,6 @@ cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_
     else if (max_P <= 128) weights_kernel<128><<<blocks, threads, 0, stream>>>(p, max_T);
     else if (max_P <= 512) weights_kernel<512><<<blocks, threads, 0, stream>>>(p, max_T);
     else if (max_P <= 1024) weights_kernel<1024><<<blocks, threads, 0, stream>>>(p, max_T);
-    else if (max_P <= 4096) weights_kernel<4096><<<blocks, threads, 0, stream>>>(p, max_T);
     else return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
@@ -1096,8 +1334,7 @@ cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool 
     const size_t smem = static_cast<size_t>(max_K) * 3 * sizeof(float) + static_cast<size_t>(max_P) * sizeof(float) +
                         static_cast<size_t>(max_K + max_P) * sizeof(int) + 16 +
                         static_cast<size_t>(max_K + max_P) * (sizeof(int64_t) + sizeof(float));
-    cudaError_t err = cudaFuncSetAttribute(backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
+    cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(backward_kernel), smem);
     if (err != cudaSuccess) return err;
     int threads = 128;
     if (max_P > 512) threads = 256;

@@ -154,17 +154,96 @@ size_t bytes_of(size_t count) {
     return ((count * sizeof(T)) + 255) & ~static_cast<size_t>(255);
 }
 
-struct StreamBuffer {
-    void* ptr = nullptr;
-    cudaStream_t stream = nullptr;
-    StreamBuffer(size_t bytes, cudaStream_t s) : stream(s) {
-        check_cuda(cudaMallocAsync(&ptr, bytes == 0 ? 256 : bytes, s), "cudaMallocAsync(workspace)");
+// Reusable per-device workspace: a device buffer, a pinned host staging buffer
+// (metadata uploads and status read-back go through it, so the copies are
+// truly asynchronous) and an event marking the end of the last call that used
+// it. Slots grow on demand and are never released before process exit, so a
+// steady stream of calls allocates nothing.
+struct Slot {
+    int device = -1;
+    void* dev = nullptr;
+    size_t dev_bytes = 0;
+    char* pinned = nullptr;
+    size_t pinned_bytes = 0;
+    cudaEvent_t done = nullptr;
+    bool in_use = false;
+};
+
+class Arena {
+  public:
+    Slot* acquire(size_t dev_bytes, size_t pinned_bytes) {
+        int device = 0;
+        check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+        Slot* s = nullptr;
+        {
+            std::lock_guard<std::mutex> lock(mu_);
+            // prefer an idle slot whose last use has finished
+            for (Slot* c : slots_) {
+                if (c->device != device || c->in_use) continue;
+                if (cudaEventQuery(c->done) == cudaSuccess) { s = c; break; }
+                cudaGetLastError();
+                if (!s) s = c;
+            }
+            if (!s || (cudaEventQuery(s->done) != cudaSuccess && count_on(device) < kMaxSlots)) {
+                cudaGetLastError();
+                s = new Slot;
+                s->device = device;
+                check_cuda(cudaEventCreateWithFlags(&s->done, cudaEventDisableTiming), "cudaEventCreate");
+                slots_.push_back(s);
+            }
+            s->in_use = true;
+        }
+        // the host writes the staging buffer below: the previous use must be over
+        check_cuda(cudaEventSynchronize(s->done), "workspace reuse");
+        if (s->dev_bytes < dev_bytes) {
+            if (s->dev) check_cuda(cudaFree(s->dev), "cudaFree(workspace)");
+            s->dev = nullptr;
+            s->dev_bytes = 0;
+            const size_t n = std::max(dev_bytes + dev_bytes / 4, static_cast<size_t>(1) << 20);
+            check_cuda(cudaMalloc(&s->dev, n), "cudaMalloc(workspace)");
+            s->dev_bytes = n;
+        }
+        if (s->pinned_bytes < pinned_bytes) {
+            if (s->pinned) check_cuda(cudaFreeHost(s->pinned), "cudaFreeHost(staging)");
+            s->pinned = nullptr;
+            s->pinned_bytes = 0;
+            const size_t n = std::max(pinned_bytes + pinned_bytes / 4, static_cast<size_t>(64) << 10);
+            check_cuda(cudaHostAlloc(reinterpret_cast<void**>(&s->pinned), n, cudaHostAllocDefault),
+                       "cudaHostAlloc(staging)");
+            s->pinned_bytes = n;
+        }
+        return s;
     }
-    ~StreamBuffer() {
-        if (ptr) cudaFreeAsync(ptr, stream);
+    void release(Slot* s, cudaStream_t stream) {
+        cudaEventRecord(s->done, stream);
+        std::lock_guard<std::mutex> lock(mu_);
+        s->in_use = false;
     }
-    StreamBuffer(const StreamBuffer&) = delete;
-    StreamBuffer& operator=(const StreamBuffer&) = delete;
+
+  private:
+    static constexpr int kMaxSlots = 4;
+    int count_on(int device) const {
+        int n = 0;
+        for (const Slot* c : slots_) n += c->device == device;
+        return n;
+    }
+    std::mutex mu_;
+    std::vector<Slot*> slots_;
+};
+
+Arena& arena() {
+    static Arena* a = new Arena;  // intentionally leaked: outlives static destructors
+    return *a;
+}
+
+// RAII lease of a slot for one call on one stream.
+struct Lease {
+    Slot* s;
+    cudaStream_t stream;
+    Lease(size_t dev_bytes, size_t pinned_bytes, cudaStream_t st) : s(arena().acquire(dev_bytes, pinned_bytes)), stream(st) {}
+    ~Lease() { arena().release(s, stream); }
+    Lease(const Lease&) = delete;
+    Lease& operator=(const Lease&) = delete;
 };
 
 }  // namespace
@@ -257,41 +336,46 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     std::vector<float> pen, inv;
     penalty_tables(opt.length_penalty_alpha, lmax, pen, inv);
 
-    size_t ws = 0;
-    ws += bytes_of<dbs_dev::ExampleDesc>(B);
-    ws += bytes_of<int64_t>(B + 1);
-    ws += 2 * bytes_of<float>(lmax + 1);
+    // Workspace layout: [header: desc | row prefix | pen | inv_pen | status |
+    // counters] [lists | counts | bounds | prefixes]. The header is staged in
+    // pinned memory (status and counters zeroed there) and uploaded with one
+    // asynchronous copy.
+    size_t hdr = 0;
+    hdr += bytes_of<dbs_dev::ExampleDesc>(B);
+    hdr += bytes_of<int64_t>(B + 1);
+    hdr += 2 * bytes_of<float>(lmax + 1);
+    hdr += bytes_of<int32_t>(B);
+    hdr += bytes_of<unsigned long long>(4);
+    size_t ws = hdr;
     ws += bytes_of<uint64_t>(static_cast<size_t>(list_entries));
     ws += bytes_of<int32_t>(static_cast<size_t>(rows));
     ws += bytes_of<float>(static_cast<size_t>(rows));
-    ws += bytes_of<int32_t>(B);
-    ws += bytes_of<unsigned long long>(4);
     if (dynamic) ws += bytes_of<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
-    StreamBuffer buf(ws, stream);
-    Carve cv{static_cast<char*>(buf.ptr), 0, ws};
+    Lease lease(ws, hdr, stream);
+    Carve cv{static_cast<char*>(lease.s->dev), 0, ws};
+    Carve hv{lease.s->pinned, 0, hdr};
 
     dbs_dev::DecodeParams p{};
     auto* d_desc = cv.take<dbs_dev::ExampleDesc>(B);
     auto* d_prefix = cv.take<int64_t>(B + 1);
     auto* d_pen = cv.take<float>(lmax + 1);
     auto* d_inv = cv.take<float>(lmax + 1);
+    p.status = cv.take<int32_t>(B);
+    p.counters = cv.take<unsigned long long>(4);
+    std::memcpy(hv.take<dbs_dev::ExampleDesc>(B), desc.data(), sizeof(dbs_dev::ExampleDesc) * B);
+    std::memcpy(hv.take<int64_t>(B + 1), row_prefix.data(), sizeof(int64_t) * (B + 1));
+    std::memcpy(hv.take<float>(lmax + 1), pen.data(), sizeof(float) * (lmax + 1));
+    std::memcpy(hv.take<float>(lmax + 1), inv.data(), sizeof(float) * (lmax + 1));
+    int32_t* h_status = hv.take<int32_t>(B);
+    unsigned long long* h_counters = hv.take<unsigned long long>(4);
+    std::memset(h_status, 0, sizeof(int32_t) * B);
+    std::memset(h_counters, 0, sizeof(unsigned long long) * 4);
+    check_cuda(cudaMemcpyAsync(lease.s->dev, lease.s->pinned, cv.off, cudaMemcpyHostToDevice, stream),
+               "upload decode metadata");
     p.lists = cv.take<uint64_t>(static_cast<size_t>(list_entries));
     p.list_count = cv.take<int32_t>(static_cast<size_t>(rows));
     p.list_bound = cv.take<float>(static_cast<size_t>(rows));
-    p.status = cv.take<int32_t>(B);
-    p.counters = cv.take<unsigned long long>(4);
     p.seq_scratch = dynamic ? cv.take<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T) : nullptr;
-
-    check_cuda(cudaMemcpyAsync(d_desc, desc.data(), sizeof(dbs_dev::ExampleDesc) * B, cudaMemcpyHostToDevice, stream),
-               "upload descriptors");
-    check_cuda(cudaMemcpyAsync(d_prefix, row_prefix.data(), sizeof(int64_t) * (B + 1), cudaMemcpyHostToDevice, stream),
-               "upload row prefix");
-    check_cuda(cudaMemcpyAsync(d_pen, pen.data(), sizeof(float) * (lmax + 1), cudaMemcpyHostToDevice, stream),
-               "upload penalty table");
-    check_cuda(cudaMemcpyAsync(d_inv, inv.data(), sizeof(float) * (lmax + 1), cudaMemcpyHostToDevice, stream),
-               "upload penalty table");
-    check_cuda(cudaMemsetAsync(p.status, 0, sizeof(int32_t) * B, stream), "clear status");
-    check_cuda(cudaMemsetAsync(p.counters, 0, sizeof(unsigned long long) * 4, stream), "clear counters");
 
     p.x = d_x;
     p.V = V;
@@ -348,20 +432,20 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     }
 
     if (synchronize) {
-        std::vector<int32_t> status(B, 0);
-        unsigned long long counters[4] = {0, 0, 0, 0};
-        check_cuda(cudaMemcpyAsync(status.data(), p.status, sizeof(int32_t) * B, cudaMemcpyDeviceToHost, stream),
+        // status and counters are contiguous in the header: one read-back
+        const size_t off = reinterpret_cast<char*>(p.status) - static_cast<char*>(lease.s->dev);
+        const size_t n = reinterpret_cast<char*>(p.counters + 4) - reinterpret_cast<char*>(p.status);
+        check_cuda(cudaMemcpyAsync(lease.s->pinned + off, p.status, n, cudaMemcpyDeviceToHost, stream),
                    "read status");
-        check_cuda(cudaMemcpyAsync(counters, p.counters, sizeof(counters), cudaMemcpyDeviceToHost, stream),
-                   "read counters");
         check_cuda(cudaStreamSynchronize(stream), "decode");
         if (stats) {
-            stats->row_rescans = counters[0];
-            stats->merge_fallbacks = counters[1];
+            stats->row_rescans = h_counters[0];
+            stats->merge_fallbacks = h_counters[1];
         }
+        if (h_counters[3]) throw CudaFailure("row scan: a shared-memory copy did not complete within the wait bound");
         if (opt.validate_inputs) {
             for (int b = 0; b < B; ++b)
-                if (status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
+                if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
         }
     }
 }
@@ -395,17 +479,18 @@ void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, con
     std::vector<float> pen, inv;
     penalty_tables(opt.length_penalty_alpha, lmax, pen, inv);
     const bool sparse = out.sparse_indices != nullptr;
-    size_t ws = bytes_of<dbs_dev::ExampleDesc>(B) + bytes_of<float>(lmax + 1) +
-                bytes_of<int32_t>(static_cast<size_t>(B) * max_T);
-    StreamBuffer buf(ws, stream);
-    Carve cv{static_cast<char*>(buf.ptr), 0, ws};
+    const size_t hdr = bytes_of<dbs_dev::ExampleDesc>(B) + bytes_of<float>(lmax + 1);
+    const size_t ws = hdr + bytes_of<int32_t>(static_cast<size_t>(B) * max_T);
+    Lease lease(ws, hdr, stream);
+    Carve cv{static_cast<char*>(lease.s->dev), 0, ws};
+    Carve hv{lease.s->pinned, 0, hdr};
     auto* d_desc = cv.take<dbs_dev::ExampleDesc>(B);
     auto* d_inv = cv.take<float>(lmax + 1);
+    std::memcpy(hv.take<dbs_dev::ExampleDesc>(B), desc.data(), sizeof(dbs_dev::ExampleDesc) * B);
+    std::memcpy(hv.take<float>(lmax + 1), inv.data(), sizeof(float) * (lmax + 1));
+    check_cuda(cudaMemcpyAsync(lease.s->dev, lease.s->pinned, cv.off, cudaMemcpyHostToDevice, stream),
+               "upload backward metadata");
     auto* d_steps = cv.take<int32_t>(static_cast<size_t>(B) * max_T);
-    check_cuda(cudaMemcpyAsync(d_desc, desc.data(), sizeof(dbs_dev::ExampleDesc) * B, cudaMemcpyHostToDevice, stream),
-               "upload descriptors");
-    check_cuda(cudaMemcpyAsync(d_inv, inv.data(), sizeof(float) * (lmax + 1), cudaMemcpyHostToDevice, stream),
-               "upload penalty table");
     if (!sparse && out.grad_dense && zero_dense) {
         ProfileScope ps(kFillZero, stream);
         check_cuda(dbs_dev::launch_fill_zero(out.grad_dense, layout.grad_total, device_sm_count(), stream),
