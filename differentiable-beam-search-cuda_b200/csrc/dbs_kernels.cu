@@ -205,7 +205,6 @@ __global__ void validate_kernel(DecodeParams p) {
 constexpr int kScanStages = 4;
 constexpr int kScanChunkF4 = 128;       // 2 KB per chunk: 4 float4 per lane
 constexpr int kScanWarpsPerCta = 4;
-constexpr int kScanAppendsPerChunk = kScanChunkF4 * 4;
 
 __device__ __forceinline__ void warp_sort_desc_u64(uint64_t* a, int n, int lane) {
     if (n <= 1) { __syncwarp(); return; }
@@ -335,7 +334,7 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     return j;
 }
 
-__global__ void __launch_bounds__(kScanWarpsPerCta * 32) row_scan_kernel(DecodeParams p, int capw) {
+__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 1) row_scan_kernel(DecodeParams p, int capw) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     constexpr unsigned FULL = 0xFFFFFFFFu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -380,9 +379,9 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32) row_scan_kernel(DecodeP
     auto issue_more = [&]() {
         // lane 0 keeps up to kScanStages chunks in flight, crossing into nxt
         while (n_issued < n_used + kScanStages) {
-            RowJob* j = issue_in_cur ? &cur : &nxt;
             if (!issue_in_cur && !have_nxt) break;
-            if (ic >= j->chunks) {
+            const int jchunks = issue_in_cur ? cur.chunks : nxt.chunks;
+            if (ic >= jchunks) {
                 if (!issue_in_cur) break;  // at most one row ahead
                 // move the issue cursor to the next claimed row
                 if (!have_nxt) {
@@ -397,12 +396,14 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32) row_scan_kernel(DecodeP
             }
             const int s = static_cast<int>(n_issued % kScanStages);
             const int f0 = ic * kScanChunkF4;
-            const int nf = min(kScanChunkF4, j->nv - f0);
+            const int jnv = issue_in_cur ? cur.nv : nxt.nv;
+            const float* jbody = issue_in_cur ? cur.row + cur.h : nxt.row + nxt.h;
+            const int nf = min(kScanChunkF4, jnv - f0);
             if (lane == 0) {
                 const uint32_t bytes = static_cast<uint32_t>(nf) * 16u;
                 mbar_arrive_expect_tx(full + s, bytes);
                 bulk_copy_g2s(ring + static_cast<size_t>(s) * kScanChunkF4,
-                              reinterpret_cast<const float4*>(j->row + j->h) + f0, bytes, full + s);
+                              reinterpret_cast<const float4*>(jbody) + f0, bytes, full + s);
             }
             ++ic;
             ++n_issued;
@@ -491,24 +492,25 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32) row_scan_kernel(DecodeP
                 ++n_used;
                 issue_more();
                 const int tok0 = j.h + 4 * c * kScanChunkF4;
+                // Fast path: one max and one vote for the lane's 16 values;
+                // survivors are rare once the threshold has settled.
+                float m16 = -INFINITY;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const bool p0 = q[u].x >= thr, p1 = q[u].y >= thr, p2 = q[u].z >= thr, p3 = q[u].w >= thr;
-                    if (in[u]) {
-                        if (!p0) rej = fmaxf(rej, q[u].x);
-                        if (!p1) rej = fmaxf(rej, q[u].y);
-                        if (!p2) rej = fmaxf(rej, q[u].z);
-                        if (!p3) rej = fmaxf(rej, q[u].w);
-                    }
-                    if (__any_sync(FULL, in[u] && (p0 | p1 | p2 | p3))) {
+                for (int u = 0; u < 4; ++u)
+                    m16 = fmaxf(m16, fmaxf(fmaxf(q[u].x, q[u].y), fmaxf(q[u].z, q[u].w)));
+                if (!__any_sync(FULL, m16 >= thr)) {
+                    rej = fmaxf(rej, m16);
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
                         const int v0 = tok0 + 4 * (u * 32 + lane);
                         consider(in[u], v0 + 0, q[u].x);
                         consider(in[u], v0 + 1, q[u].y);
                         consider(in[u], v0 + 2, q[u].z);
                         consider(in[u], v0 + 3, q[u].w);
+                        if (cnt > capw - 128 - 8) compact();
                     }
                 }
-                if (cnt > capw - kScanAppendsPerChunk - 8) compact();
             }
             {  // unaligned tail, last in token order
                 const int t0 = j.h + 4 * j.nv;
@@ -1260,8 +1262,8 @@ cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-// per-warp survivor buffer: C kept + one chunk of appends + head/tail
-static int row_scan_capw(int max_C) { return max_C + kScanAppendsPerChunk + 16; }
+// per-warp survivor buffer: C kept + 8 + one 128-value group of appends + head/tail
+static int row_scan_capw(int max_C) { return max_C + 128 + 24; }
 
 static size_t row_scan_smem(int capw) {
     const size_t warp_bytes = static_cast<size_t>(kScanStages) * kScanChunkF4 * 16 + kScanStages * sizeof(uint64_t) +
