@@ -98,24 +98,18 @@ bool is_device_pointer(const void* p) {
     return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
-// One call's stream: the caller's stream for device entry points, a private
-// non-blocking stream otherwise.
+// Stream of one host-pointer ABI call: a private stream created blocking, so
+// it is ordered after pending work on the legacy default stream; the call
+// waits for it before returning. The device entry points never use this:
+// they run on the caller's stream verbatim (NULL = legacy default stream).
 struct CallStream {
     cudaStream_t s = nullptr;
-    bool owned = false;
-    explicit CallStream(void* user) {
-        if (user) {
-            s = static_cast<cudaStream_t>(user);
-        } else {
-            dbs_host::check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "cudaStreamCreate");
-            owned = true;
-        }
+    explicit CallStream(void*) {
+        dbs_host::check_cuda(cudaStreamCreate(&s), "cudaStreamCreate");
     }
     ~CallStream() {
-        if (owned) {
-            cudaStreamSynchronize(s);
-            cudaStreamDestroy(s);
-        }
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
     }
 };
 
@@ -459,7 +453,7 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
         o.final_scores = reinterpret_cast<float*>(take(nfin * 4));
         const float* dx = x_dev ? x : xs.as<float>();
         dbs_host::DecodeStats st;
-        dbs_host::decode(opt, dx, V, spec, cons, o, CL, true, true, s, &st, true);
+        dbs_host::decode(opt, dx, V, spec, cons, o, CL, true, true, s, &st, dbs_host::DecodeControl{});
         if (stats_handle) {
             stats_handle->last_row_rescans.store(static_cast<int64_t>(st.row_rescans));
             stats_handle->last_merge_rescans.store(static_cast<int64_t>(st.merge_fallbacks));
@@ -1340,7 +1334,8 @@ static dbs_host::Outputs to_outputs(const DBSDeviceDecodeOutputs* o) {
 }
 
 static void run_device_decode(DBSDecoderHandle* handle, const float* x, int V, const std::vector<ExampleSpec>& spec,
-                              const CallConstraints& cons, const DBSDeviceDecodeOutputs* outputs, void* stream) {
+                              const CallConstraints& cons, const DBSDeviceDecodeOutputs* outputs, void* stream,
+                              float* zero_fill = nullptr, int64_t zero_fill_count = 0) {
     const Options& opt = handle->options;
     if (!outputs || !outputs->parents || !outputs->tokens || !outputs->lengths || !outputs->from_logprob)
         throw std::invalid_argument("device outputs need parents, tokens, lengths and from_logprob");
@@ -1350,18 +1345,29 @@ static void run_device_decode(DBSDecoderHandle* handle, const float* x, int V, c
         throw std::invalid_argument("device pool outputs are incomplete");
     const Layout L = dbs_host::make_layout(opt, spec, V);
     dbs_host::DecodeStats st;
-    CallStream cs(stream);
-    const bool sync = opt.validate_inputs != 0;
-    dbs_host::decode(opt, x, V, spec, cons, to_outputs(outputs), L, pool, outputs->weights != nullptr, cs.s, &st,
-                     sync);
-    if (sync) {
-        handle->last_row_rescans.store(static_cast<int64_t>(st.row_rescans));
-        handle->last_merge_rescans.store(static_cast<int64_t>(st.merge_fallbacks));
-    }
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL = legacy default stream
+    dbs_host::DecodeControl ctl;
+    ctl.synchronize = false;  // validation is still checked before the decode is queued
+    ctl.zero_fill = zero_fill;
+    ctl.zero_fill_count = zero_fill_count;
+    dbs_host::decode(opt, x, V, spec, cons, to_outputs(outputs), L, pool, outputs->weights != nullptr, s, &st,
+                     ctl);
+    (void)handle;
 }
+
+DBS_EXPORT int dbs_device_decode_batch_ex(DBSDecoderHandle* handle, const float* log_probs, int batch_size,
+                                          int steps, int vocab_size, const DBSDeviceDecodeOutputs* outputs,
+                                          float* zero_fill, int64_t zero_fill_count, void* cuda_stream);
 
 DBS_EXPORT int dbs_device_decode_batch(DBSDecoderHandle* handle, const float* log_probs, int batch_size, int steps,
                                        int vocab_size, const DBSDeviceDecodeOutputs* outputs, void* cuda_stream) {
+    return dbs_device_decode_batch_ex(handle, log_probs, batch_size, steps, vocab_size, outputs, nullptr, 0,
+                                      cuda_stream);
+}
+
+DBS_EXPORT int dbs_device_decode_batch_ex(DBSDecoderHandle* handle, const float* log_probs, int batch_size,
+                                          int steps, int vocab_size, const DBSDeviceDecodeOutputs* outputs,
+                                          float* zero_fill, int64_t zero_fill_count, void* cuda_stream) {
     if (!handle || !outputs) {
         set_error(handle, "invalid decoder or output pointer");
         return -1;
@@ -1381,7 +1387,10 @@ DBS_EXPORT int dbs_device_decode_batch(DBSDecoderHandle* handle, const float* lo
             spec[b].eos = opt.eos_token;
             spec[b].min_length = opt.min_length;
         }
-        run_device_decode(handle, log_probs, vocab_size, spec, CallConstraints{}, outputs, cuda_stream);
+        if (zero_fill_count < 0 || (zero_fill_count > 0 && !zero_fill))
+            throw std::invalid_argument("zero_fill needs a buffer for a positive element count");
+        run_device_decode(handle, log_probs, vocab_size, spec, CallConstraints{}, outputs, cuda_stream, zero_fill,
+                          zero_fill_count);
         ExampleInfo e;
         e.T = steps;
         e.K = opt.beam_size;
@@ -1451,11 +1460,29 @@ DBS_EXPORT int dbs_device_decode_batch_variable_ex(
     });
 }
 
+DBS_EXPORT int dbs_device_backward_batch_ex(DBSDecoderHandle* handle, int batch_size, int steps, int vocab_size,
+                                            const DBSDeviceDecodeOutputs* trace, const float* grad_selected_weights,
+                                            const float* grad_relaxed_weights, const float* grad_final_scores,
+                                            float* grad_log_probs, int64_t* sparse_indices, float* sparse_values,
+                                            int64_t* sparse_counts, float* grad_initial_scores, int flags,
+                                            void* cuda_stream);
+
 DBS_EXPORT int dbs_device_backward_batch(DBSDecoderHandle* handle, int batch_size, int steps, int vocab_size,
                                          const DBSDeviceDecodeOutputs* trace, const float* grad_selected_weights,
                                          const float* grad_relaxed_weights, const float* grad_final_scores,
                                          float* grad_log_probs, int64_t* sparse_indices, float* sparse_values,
                                          int64_t* sparse_counts, float* grad_initial_scores, void* cuda_stream) {
+    return dbs_device_backward_batch_ex(handle, batch_size, steps, vocab_size, trace, grad_selected_weights,
+                                        grad_relaxed_weights, grad_final_scores, grad_log_probs, sparse_indices,
+                                        sparse_values, sparse_counts, grad_initial_scores, 0, cuda_stream);
+}
+
+DBS_EXPORT int dbs_device_backward_batch_ex(DBSDecoderHandle* handle, int batch_size, int steps, int vocab_size,
+                                            const DBSDeviceDecodeOutputs* trace, const float* grad_selected_weights,
+                                            const float* grad_relaxed_weights, const float* grad_final_scores,
+                                            float* grad_log_probs, int64_t* sparse_indices, float* sparse_values,
+                                            int64_t* sparse_counts, float* grad_initial_scores, int flags,
+                                            void* cuda_stream) {
     if (!handle || !trace) {
         set_error(handle, "invalid decoder or trace pointer");
         return -1;
@@ -1500,8 +1527,8 @@ DBS_EXPORT int dbs_device_backward_batch(DBSDecoderHandle* handle, int batch_siz
         bo.sparse_values = sparse_values;
         bo.sparse_counts = sparse_counts;
         bo.grad_initial = grad_initial_scores;
-        CallStream cs(cuda_stream);
-        dbs_host::backward(opt, vocab_size, spec, L, in, bo, cs.s, true);
+        dbs_host::backward(opt, vocab_size, spec, L, in, bo, static_cast<cudaStream_t>(cuda_stream),
+                           (flags & DBS_DEVICE_GRAD_PREZEROED) == 0);
         {
             std::lock_guard<std::mutex> lock(handle->stats_mutex);
             handle->stats.used_sparse_backward = sparse ? 1 : 0;
@@ -1518,8 +1545,17 @@ DBS_EXPORT int dbs_device_profile(int enable) {
         if (enable < 0) {
             dbs_host::profile_reset();
         } else {
-            dbs_host::profile_enable(enable != 0);
+            dbs_host::profile_enable(enable != 0 ? ((1u << dbs_host::kProfiledKernels) - 1u) : 0u);
         }
+        return 0;
+    } catch (...) {
+        return -2;
+    }
+}
+
+DBS_EXPORT int dbs_device_profile_kernels(unsigned mask) {
+    try {
+        dbs_host::profile_enable(mask & ((1u << dbs_host::kProfiledKernels) - 1u));
         return 0;
     } catch (...) {
         return -2;
@@ -1536,8 +1572,10 @@ DBS_EXPORT int dbs_device_profile_read(int kernel, double* total_ms, int64_t* la
 
 DBS_EXPORT int dbs_device_last_rescan_counts(DBSDecoderHandle* handle, int64_t* row_rescans, int64_t* merge_rescans) {
     if (!handle) return -1;
-    if (row_rescans) *row_rescans = handle->last_row_rescans.load();
-    if (merge_rescans) *merge_rescans = handle->last_merge_rescans.load();
+    unsigned long long merge = 0;
+    dbs_host::last_decode_diagnostics(&merge, nullptr);
+    if (row_rescans) *row_rescans = 0;  // the row scan is exact in one pass
+    if (merge_rescans) *merge_rescans = static_cast<int64_t>(merge);
     return 0;
 }
 

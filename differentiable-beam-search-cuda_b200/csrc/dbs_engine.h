@@ -147,7 +147,12 @@ cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_
                            cudaStream_t stream);
 cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool sparse,
                             cudaStream_t stream);
-cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_t stream);
+// blocks_per_sm: 4 fills the GPU; 1 leaves three quarters of every SM's
+// registers and thread slots to a kernel running beside the fill (the merge).
+cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_t stream, int blocks_per_sm = 4);
+// Same result through bulk (TMA) stores from one 32-thread CTA per SM; leaves
+// the SMs' load/store pipes and registers to a kernel running beside it.
+cudaError_t launch_fill_zero_bulk(float* dst, int64_t count, int num_sms, cudaStream_t stream);
 
 // Limits of this implementation.
 constexpr int kMaxMergeCandidates = 8192;   // K * C per step handled by one CTA

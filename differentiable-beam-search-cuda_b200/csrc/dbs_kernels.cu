@@ -800,6 +800,7 @@ __global__ void __launch_bounds__(kMergeThreads) step_merge_kernel(DecodeParams 
                     }
                     __syncthreads();
                     const int staged = sh_stage;
+                    __syncthreads();   // every thread holds the count before the next chunk stages
                     if (staged > 0) {
                         block_sort_desc_u128(chi, clo, N + staged);
                         for (int i = N + tid; i < N + staged; i += NT) { chi[i] = 0; clo[i] = 0; }
@@ -896,6 +897,384 @@ __global__ void __launch_bounds__(kMergeThreads) step_merge_kernel(DecodeParams 
         const int64_t o = d.final_offset + k;
         if (p.final_raw_scores) p.final_raw_scores[o] = s.prev_raw[k];
         if (p.final_scores) p.final_scores[o] = __fdiv_rn(s.prev_raw[k], p.pen[len]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2b. Step merge by ranking (no repetition penalty, no n-gram blocking).
+//
+// For a fixed parent the candidate key (rank, raw) is a monotone function of
+// the log-prob, so it is non-increasing along the parent's row list (lp desc,
+// token asc). The position of a candidate in the step's order is therefore the
+// number of better candidates summed over the K row lists, each count a
+// binary search on (rank, raw); equal (rank, raw) keys break ties by parent,
+// then by token within one list (an equal run can hold several tokens when
+// rounding maps distinct lps to one raw). Every candidate whose position is
+// below N writes itself to that slot: two block barriers per step instead of
+// a bitonic sort. Row lists of upcoming steps are staged into a shared ring
+// with cp.async while the current step runs, so the step's critical path has
+// no global-memory load.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async_8(void* smem_dst, const void* gsrc) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(s), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gsrc) {
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most n (0..7) committed groups of this thread are pending.
+__device__ __forceinline__ void cp_async_wait_pending(int n) {
+    switch (n) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+        case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+        case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+        case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+    }
+}
+
+constexpr int kMergeRingMax = 8;       // steps of row lists staged ahead (ring slots)
+constexpr int kRescanChunk = 2048;     // log-probs per rescan chunk
+constexpr int kMergeRankThreads = 1024;
+
+// One commit group per call (empty beyond the last step) so group counting
+// stays uniform across steps.
+__device__ __forceinline__ void merge_stage_step(const DecodeParams& p, const ExampleDesc& d, int t, int slot,
+                                                 uint64_t* ring_l, int* ring_c, float* ring_b) {
+    if (t < d.T) {
+        const int K = d.K, C = d.C;
+        const int KC = K * C;
+        const uint64_t* src = p.lists + d.list_offset + static_cast<int64_t>(t) * KC;
+        uint64_t* dst = ring_l + static_cast<int64_t>(slot) * KC;
+        for (int i = threadIdx.x; i < KC; i += blockDim.x) cp_async_8(dst + i, src + i);
+        const int64_t row0 = d.row_begin + static_cast<int64_t>(t) * K;
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            cp_async_4(ring_c + slot * K + k, p.list_count + row0 + k);
+            cp_async_4(ring_b + slot * K + k, p.list_bound + row0 + k);
+        }
+    }
+    cp_async_commit();
+}
+
+// Rare path of the ranking merge: rescan the unproven rows of step t from HBM,
+// merging every dropped candidate that beats the current N-th. Called by all
+// threads of the block.
+__device__ void rank_merge_rescan(const DecodeParams& p, const ExampleDesc& d, int t, const float* beam_raw,
+                                  const int* beam_ended, const float* beam_inv, const uint64_t* L, const int* cnt,
+                                  const float* bnd, uint64_t* cur_hi, uint64_t* cur_lo, uint64_t* st_hi,
+                                  uint64_t* st_lo, int* stage_count) {
+    const int K = d.K, C = d.C, N = d.N;
+    const int V = p.V;
+    const int tid = threadIdx.x;
+    const int NT = blockDim.x;
+    const bool has_eos = d.eos >= 0;
+    int& sh_stage = *stage_count;
+    // Rare path: rescan the unproven rows from HBM, merging every
+    // dropped candidate that beats the current N-th.
+    for (int j = tid; j < N; j += NT) { st_hi[j] = cur_hi[j]; st_lo[j] = cur_lo[j]; }
+    __syncthreads();
+    const int forced = d.forced ? d.forced[t] : -1;
+    const bool eos_blocked = has_eos && (t + 1) < d.min_length;
+    for (int k = 0; k < K; ++k) {
+        const float pr = beam_raw[k];
+        if (!isfinite(pr) || (has_eos && beam_ended[k])) continue;
+        const float b = bnd[k];
+        if (!(b > -INFINITY)) continue;
+        const float raw_u = __fadd_rn(pr, b);
+        if (raw_u == -INFINITY) continue;
+        const float inv = beam_inv[k];
+        {
+            const uint64_t gh = st_hi[N - 1];
+            const uint64_t uh = cand_hi(__fmul_rn(raw_u, inv), raw_u);
+            const bool safe = gh != 0 && (gh > uh || (gh == uh && cand_parent(st_lo[N - 1]) < k));
+            if (safe) continue;   // uniform: every thread reads the same staged top-N
+        }
+        if (tid == 0 && p.counters) atomicAdd(p.counters + 1, 1ull);
+        const float* row = p.x + d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
+        const uint64_t last = L[k * C + cnt[k] - 1];
+        const float m_lp = list_lp(last);
+        const int m_tok = list_token(last);
+        for (int base = 0; base < V; base += kRescanChunk) {
+            const uint64_t gh = st_hi[N - 1];
+            const uint64_t gl = st_lo[N - 1];
+            for (int v = base + tid; v < base + kRescanChunk && v < V; v += NT) {
+                if (forced >= 0 && v != forced) continue;
+                if (d.banned && d.banned[v]) continue;
+                if (eos_blocked && v == d.eos) continue;
+                const float lp = row[v];
+                if (!isfinite(lp)) continue;
+                const float lpc = __fadd_rn(lp, 0.0f);
+                if (lpc > m_lp || (lpc == m_lp && v <= m_tok)) continue;   // already listed
+                const float raw = __fadd_rn(pr, lp);
+                if (raw == -INFINITY) continue;
+                const uint64_t h = cand_hi(__fmul_rn(raw, inv), raw);
+                const uint64_t l = cand_lo(k, v);
+                if (key2_less(gh, gl, h, l)) {
+                    const int pos = atomicAdd(&sh_stage, 1);
+                    st_hi[N + pos] = h;
+                    st_lo[N + pos] = l;
+                }
+            }
+            __syncthreads();
+            const int staged = sh_stage;
+            __syncthreads();   // every thread holds the count before the next chunk stages
+            if (staged > 0) {
+                block_sort_desc_u128(st_hi, st_lo, N + staged);
+                if (tid == 0) sh_stage = 0;
+                __syncthreads();
+            }
+        }
+    }
+    for (int j = tid; j < N; j += NT) { cur_hi[j] = st_hi[j]; cur_lo[j] = st_lo[j]; }
+    __syncthreads();
+}
+
+// Lanes that rank one candidate together; lane l counts lists l, l + W, ...
+__device__ __forceinline__ int rank_lanes(int K) {
+    int w = 1;
+    while (w < K && w < 32) w <<= 1;
+    return w;
+}
+
+__global__ void __launch_bounds__(kMergeRankThreads) step_merge_rank_kernel(DecodeParams p, int ring_steps,
+                                                                            int max_K, int max_C, int max_N,
+                                                                            int tab_n) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int e = blockIdx.x;
+    const ExampleDesc d = p.desc[e];
+    const int K = d.K, C = d.C, N = d.N, T = d.T, P = d.P;
+    const int tid = threadIdx.x;
+    const int NT = blockDim.x;
+    const int R = ring_steps;
+    const bool has_eos = d.eos >= 0;
+
+    // Layout (sized by the call's largest K, C, N so every example fits).
+    uint64_t* ring_l = reinterpret_cast<uint64_t*>(smem);                    // [R][K*C]
+    uint64_t* top_hi = ring_l + static_cast<int64_t>(R) * max_K * max_C;   // [2][N]
+    uint64_t* top_lo = top_hi + 2 * max_N;                                   // [2][N]
+    uint64_t* st_hi = top_lo + 2 * max_N;                                    // [N + chunk]
+    uint64_t* st_lo = st_hi + (max_N + kRescanChunk);                        // [N + chunk]
+    uint64_t* carry_base = st_lo + (max_N + kRescanChunk);                   // [2][K]
+    float* f_base = reinterpret_cast<float*>(carry_base + 2 * max_K);
+    float* ring_b = f_base;                                                   // [R][K]
+    float* raw_base = ring_b + R * max_K;                                     // [2][K]
+    float* inv_base = raw_base + 2 * max_K;                                   // [2][K]
+    float* tab_pen = inv_base + 2 * max_K;                                    // [tab_n]
+    float* tab_inv = tab_pen + tab_n;                                         // [tab_n]
+    int* ring_c = reinterpret_cast<int*>(tab_inv + tab_n);                   // [R][K]
+    int* len_base = ring_c + R * max_K;                                       // [2][K]
+    int* end_base = len_base + 2 * max_K;                                     // [2][K]
+    __shared__ int sh_stage;
+
+    // Length-penalty tables: shared copies when they fit, else global.
+    for (int i = tid; i < tab_n; i += NT) {
+        tab_pen[i] = p.pen[i];
+        tab_inv[i] = p.inv_pen[i];
+    }
+    const float* pen = tab_n > 0 ? tab_pen : p.pen;
+    const float* inv_pen = tab_n > 0 ? tab_inv : p.inv_pen;
+
+    // Beam state and top-N slots are double buffered; cb / tb select the
+    // current halves (offsets, to keep the per-thread pointer count low).
+    int cb = 0;   // 0 or max_K
+    int tb = 0;   // 0 or max_N
+
+    for (int k = tid; k < K; k += NT) {
+        raw_base[cb + k] = (k == 0) ? 0.0f : -INFINITY;
+        len_base[cb + k] = 0;
+        end_base[cb + k] = 0;
+        inv_base[cb + k] = p.inv_pen[1];
+        carry_base[cb + k] = 0;
+    }
+    for (int j = tid; j < N; j += NT) {
+        top_hi[tb + j] = 0; top_lo[tb + j] = 0;
+        top_hi[(max_N - tb) + j] = 0; top_lo[(max_N - tb) + j] = 0;
+    }
+    if (tid == 0) sh_stage = 0;
+    for (int s = 0; s < R - 1; ++s) merge_stage_step(p, d, s, s, ring_l, ring_c, ring_b);
+
+    const int W = rank_lanes(K);
+    const int lane = tid & (W - 1);
+    const int groups = NT / W;
+    const int grp = tid / W;
+    const unsigned wmask = 0xFFFFFFFFu;
+    // candidates: K*C listed entries, then one bound probe per row
+    const int ncand = K * C + K;
+
+    for (int t = 0; t < T; ++t) {
+        const int slot = t % R;
+        cp_async_wait_pending(R - 2);
+        __syncthreads();   // (a) lists of step t, beam state and cleared slots visible
+        merge_stage_step(p, d, t + R - 1, (t + R - 1) % R, ring_l, ring_c, ring_b);
+
+        const uint64_t* L = ring_l + static_cast<int64_t>(slot) * K * C;
+        const int* cnt = ring_c + slot * K;
+        const float* bnd = ring_b + slot * K;
+        int unsafe = 0;
+        // Every listed entry is a candidate: an entry past position N can
+        // still place when it shares (rank, raw) with earlier entries and has
+        // a lower token. The bound probe of row k asks whether at least N
+        // candidates beat every entry the scan dropped from row k (which all
+        // have lp <= bound, hence a key at most U = (rank(bound), raw(bound))
+        // and lose ties to lower parents only); if not the row is rescanned.
+        for (int base = 0; base < ncand; base += groups) {
+            const int c = base + grp;
+            bool active = false, probe = false;
+            int k = 0, ctok = 0;
+            uint64_t ch = 0;
+            if (c < K * C) {
+                k = c / C;
+                const int i = c - k * C;
+                const float pr = raw_base[cb + k];
+                if (isfinite(pr)) {
+                    if (has_eos && end_base[cb + k]) {
+                        if (i == 0) {
+                            active = true;
+                            ch = carry_base[cb + k];
+                            ctok = d.eos;
+                        }
+                    } else if (i < cnt[k]) {
+                        const uint64_t key = L[k * C + i];
+                        const float raw = __fadd_rn(pr, list_lp(key));
+                        if (raw != -INFINITY) {
+                            active = true;
+                            ch = cand_hi(__fmul_rn(raw, inv_base[cb + k]), raw);
+                            ctok = list_token(key);
+                        }
+                    }
+                }
+            } else if (c < ncand) {
+                k = c - K * C;
+                const float pr = raw_base[cb + k];
+                if (isfinite(pr) && !(has_eos && end_base[cb + k])) {
+                    const float b = bnd[k];
+                    if (b > -INFINITY) {
+                        const float raw_u = __fadd_rn(pr, b);
+                        if (raw_u != -INFINITY) {
+                            active = true;
+                            probe = true;
+                            ch = cand_hi(__fmul_rn(raw_u, inv_base[cb + k]), raw_u);
+                        }
+                    }
+                }
+            }
+            int r = 0;
+            if (active) {
+                for (int k2 = lane; k2 < K && r < N; k2 += W) {
+                    const float p2 = raw_base[cb + k2];
+                    if (!isfinite(p2)) continue;
+                    if (has_eos && end_base[cb + k2]) {
+                        const uint64_t h2 = carry_base[cb + k2];
+                        r += (h2 > ch || (h2 == ch && k2 < k)) ? 1 : 0;
+                        continue;
+                    }
+                    const uint64_t* L2 = L + k2 * C;
+                    const float inv2 = inv_base[cb + k2];
+                    const int n2 = cnt[k2];
+                    int lo = 0, hi = n2;
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        const float raw2 = __fadd_rn(p2, list_lp(L2[mid]));
+                        const uint64_t h2 = cand_hi(__fmul_rn(raw2, inv2), raw2);
+                        if (h2 > ch) lo = mid + 1;
+                        else hi = mid;
+                    }
+                    r += lo;
+                    if (k2 < k || (k2 == k && !probe)) {
+                        // equal (rank, raw): lower parents win; within the
+                        // same parent the lower token wins
+                        for (int j = lo; j < n2 && r < N; ++j) {
+                            const uint64_t key2 = L2[j];
+                            const float raw2 = __fadd_rn(p2, list_lp(key2));
+                            if (cand_hi(__fmul_rn(raw2, inv2), raw2) != ch) break;
+                            if (k2 < k || list_token(key2) < ctok) ++r;
+                        }
+                    }
+                }
+            }
+            for (int o = W >> 1; o > 0; o >>= 1) r += __shfl_xor_sync(wmask, r, o);
+            if (active && lane == 0 && r < N) {
+                if (probe) {
+                    unsafe = 1;
+                } else {
+                    top_hi[tb + r] = ch;
+                    top_lo[tb + r] = cand_lo(k, ctok);
+                }
+            }
+        }
+        // (b) top-N of step t in the current slots; any unproven row
+        const bool any_unsafe = __syncthreads_or(unsafe) != 0;
+
+        if (any_unsafe)
+            rank_merge_rescan(p, d, t, raw_base + cb, end_base + cb, inv_base + cb, L, cnt, bnd, top_hi + tb,
+                              top_lo + tb, st_hi, st_lo, &sh_stage);
+
+        // Outputs of step t, next beam state, and the cleared slots of step t+1.
+        const bool want_pool = p.pool_scores != nullptr;
+        for (int j = tid; j < N; j += NT) {
+            const uint64_t h = top_hi[tb + j];
+            const uint64_t l = top_lo[tb + j];
+            int parent = -1, token = -1, len = 0, flp = 0;
+            float rank = -INFINITY, raw = -INFINITY;
+            bool carry = false;
+            if (h != 0) {
+                parent = cand_parent(l);
+                token = cand_token(l);
+                rank = cand_rank(h);
+                raw = cand_raw(h);
+                carry = has_eos && end_base[cb + parent];
+                len = carry ? (len_base[cb + parent] < 1 ? 1 : len_base[cb + parent]) : len_base[cb + parent] + 1;
+                flp = carry ? 0 : 1;
+            }
+            if (want_pool && j < P) {
+                const int64_t o = d.pool_offset + static_cast<int64_t>(t) * d.pool_t_stride + j;
+                p.pool_parents[o] = parent;
+                p.pool_tokens[o] = token;
+                p.pool_lengths[o] = len;
+                p.pool_raw_scores[o] = raw;
+                p.pool_scores[o] = rank;
+                if (p.pool_from_logprob) p.pool_from_logprob[o] = static_cast<uint8_t>(flp);
+            }
+            if (j < K) {
+                const int64_t o = d.sel_offset + static_cast<int64_t>(t) * d.sel_t_stride + j;
+                p.parents[o] = parent;
+                p.tokens[o] = token;
+                p.lengths[o] = len;
+                if (p.raw_scores) p.raw_scores[o] = raw;
+                if (p.scores) p.scores[o] = rank;
+                p.from_logprob[o] = static_cast<uint8_t>(flp);
+                const int ended = (parent >= 0) ? ((carry || (has_eos && token == d.eos)) ? 1 : 0) : 0;
+                raw_base[(max_K - cb) + j] = raw;
+                len_base[(max_K - cb) + j] = len;
+                end_base[(max_K - cb) + j] = ended;
+                inv_base[(max_K - cb) + j] = inv_pen[len + 1];
+                uint64_t ck = 0;
+                if (ended && isfinite(raw)) {
+                    const int cl = len < 1 ? 1 : len;
+                    ck = cand_hi(__fdiv_rn(raw, pen[cl]), raw);
+                }
+                carry_base[(max_K - cb) + j] = ck;
+            }
+            top_hi[(max_N - tb) + j] = 0;
+            top_lo[(max_N - tb) + j] = 0;
+        }
+        cb = max_K - cb;
+        tb = max_N - tb;
+    }
+    cp_async_wait_pending(0);
+    __syncthreads();
+    // Finalisation (src/differentiable_beam.cpp:1661-1667): a division, not
+    // a multiply by the reciprocal.
+    for (int k = tid; k < K; k += NT) {
+        const int len = len_base[cb + k] < 1 ? 1 : len_base[cb + k];
+        const int64_t o = d.final_offset + k;
+        if (p.final_raw_scores) p.final_raw_scores[o] = raw_base[cb + k];
+        if (p.final_scores) p.final_scores[o] = __fdiv_rn(raw_base[cb + k], pen[len]);
     }
 }
 
@@ -1229,6 +1608,52 @@ __global__ void fill_zero_kernel(float* __restrict__ dst, int64_t count) {
     if (gtid < count - tail0) dst[tail0 + gtid] = 0.0f;
 }
 
+// Zero fill through the bulk-copy (TMA) engine: one warp per CTA zeroes a
+// shared tile once and lane 0 streams it to global memory with 1-D bulk
+// stores (cp.async.bulk.global.shared::cta, no multicast). A handful of
+// instructions per 32 KB keeps the SM's load/store pipe free for the
+// latency-bound step merge that runs beside the fill. The unaligned head and
+// tail (fewer than 4 elements each) use plain stores.
+constexpr int kFillTileBytes = 32 * 1024;
+constexpr int kFillInFlight = 8;   // bulk groups a CTA keeps in flight
+
+__global__ void __launch_bounds__(32, 1) fill_zero_bulk_kernel(float* __restrict__ dst, int64_t count) {
+    extern __shared__ __align__(128) unsigned char zbuf[];
+    const int lane = threadIdx.x;
+    float4* z4 = reinterpret_cast<float4*>(zbuf);
+    for (int i = lane; i < kFillTileBytes / 16; i += 32) z4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // generic-proxy writes of the tile must be visible to the bulk engine
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(dst);
+    int64_t h = static_cast<int64_t>(((16u - (addr & 15u)) & 15u) >> 2);
+    if (h > count) h = count;
+    const int64_t body = ((count - h) >> 2) << 4;   // bytes, multiple of 16
+    const int64_t tail0 = h + (body >> 2);
+    if (blockIdx.x == 0) {
+        if (lane < h) dst[lane] = 0.0f;
+        if (lane < count - tail0) dst[tail0 + lane] = 0.0f;
+    }
+    if (lane == 0 && body > 0) {
+        char* base = reinterpret_cast<char*>(dst + h);
+        const uint32_t src = static_cast<uint32_t>(__cvta_generic_to_shared(zbuf));
+        const int64_t tiles = (body + kFillTileBytes - 1) / kFillTileBytes;
+        for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            const int64_t off = tile * kFillTileBytes;
+            const int64_t rem = body - off;
+            const uint32_t bytes = static_cast<uint32_t>(rem < kFillTileBytes ? rem : kFillTileBytes);
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                         ::"l"(base + off), "r"(src), "r"(bytes) : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kFillInFlight) : "memory");
+        }
+        // the tile must stay valid until every store has read it, and the
+        // writes are complete before the CTA retires
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
+}
+
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
@@ -1238,6 +1663,9 @@ __global__ void fill_zero_kernel(float* __restrict__ dst, int64_t count) {
 static std::mutex g_attr_mu;
 static std::vector<std::tuple<const void*, int, size_t>> g_smem_set;
 static std::vector<std::tuple<int, size_t, int>> g_row_scan_occ;
+static std::vector<std::pair<const void*, int>> g_carveout_set;
+
+static cudaError_t prefer_shared(const void* fn);
 
 static cudaError_t ensure_dynamic_smem(const void* fn, size_t smem) {
     int dev = 0;
@@ -1253,11 +1681,33 @@ static cudaError_t ensure_dynamic_smem(const void* fn, size_t smem) {
         }
     }
     err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err != cudaSuccess) return err;
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               static_cast<int>(cudaSharedmemCarveoutMaxShared));
     if (err == cudaSuccess) g_smem_set.emplace_back(fn, dev, smem);
     return err;
 }
 
+// Every kernel of the engine asks for the largest shared-memory carveout. An SM
+// switches carveout only when it is idle, so a kernel that left its SMs in a
+// small-shared-memory configuration (the zero fill, the validator) would hold
+// back a shared-memory kernel queued beside or after it until those SMs drain.
+static cudaError_t prefer_shared(const void* fn) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    for (auto& e : g_carveout_set)
+        if (e.first == fn && e.second == dev) return cudaSuccess;
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               static_cast<int>(cudaSharedmemCarveoutMaxShared));
+    if (err == cudaSuccess) g_carveout_set.emplace_back(fn, dev);
+    return err;
+}
+
 cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream) {
+    cudaError_t err = prefer_shared(reinterpret_cast<const void*>(validate_kernel));
+    if (err != cudaSuccess) return err;
     validate_kernel<<<p.B, 1024, 0, stream>>>(p);
     return cudaGetLastError();
 }
@@ -1301,8 +1751,44 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     return cudaGetLastError();
 }
 
+static size_t merge_rank_smem(int ring, int max_K, int max_C, int max_N, int tab_n) {
+    size_t b = static_cast<size_t>(2) * tab_n * sizeof(float);              // length-penalty tables
+    b += static_cast<size_t>(ring) * max_K * max_C * sizeof(uint64_t);      // ring lists
+    b += static_cast<size_t>(4) * max_N * sizeof(uint64_t);                 // top-N hi/lo, double buffered
+    b += static_cast<size_t>(2) * (max_N + kRescanChunk) * sizeof(uint64_t); // rescan staging
+    b += static_cast<size_t>(2) * max_K * sizeof(uint64_t);                 // carry keys
+    b += static_cast<size_t>(ring) * max_K * (sizeof(float) + sizeof(int)); // ring bounds / counts
+    b += static_cast<size_t>(2) * max_K * (2 * sizeof(float) + 2 * sizeof(int));
+    return b;
+}
+
+// Shared memory the ranking merge may take; beyond it the sort merge runs.
+constexpr size_t kMergeRankSmemBudget = 160 * 1024;
+
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T, int max_N,
                               bool need_sequences, cudaStream_t stream) {
+    if (!need_sequences && max_K <= 128) {
+        const int tab_n = (p.Lmax + 1 <= 4096) ? p.Lmax + 1 : 0;
+        int ring = max_T < kMergeRingMax ? max_T : kMergeRingMax;
+        if (ring < 2) ring = 2;
+        while (ring > 2 && merge_rank_smem(ring, max_K, max_C, max_N, tab_n) > kMergeRankSmemBudget) --ring;
+        const size_t smem = merge_rank_smem(ring, max_K, max_C, max_N, tab_n);
+        if (smem <= kMergeRankSmemBudget) {
+            int lanes = 1;
+            while (lanes < max_K && lanes < 32) lanes <<= 1;
+            const int64_t work = (static_cast<int64_t>(max_K) * max_C + max_K) * lanes;
+            // at most 768 threads (48K registers): a CTA always fits beside one
+            // 512-thread zero-fill block on the same SM
+            constexpr int kCap = 768;
+            int threads = static_cast<int>(work < kCap ? work : kCap);
+            threads = ((threads + 31) / 32) * 32;
+            if (threads < 64) threads = 64;
+            cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(step_merge_rank_kernel), smem);
+            if (err != cudaSuccess) return err;
+            step_merge_rank_kernel<<<p.B, threads, smem, stream>>>(p, ring, max_K, max_C, max_N, tab_n);
+            return cudaGetLastError();
+        }
+    }
     const int M = max_K * max_C;
     int cand_cap = M;
     if (cand_cap < max_N + 2048) cand_cap = max_N + 2048;
@@ -1314,7 +1800,6 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     if (threads < 128 && max_K > 64) threads = 128;
     cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(step_merge_kernel), smem);
     if (err != cudaSuccess) return err;
-    (void)need_sequences;
     step_merge_kernel<<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K);
     return cudaGetLastError();
 }
@@ -1324,6 +1809,12 @@ cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_
     const int64_t warps = static_cast<int64_t>(p.B) * max_T;
     const int threads = 256;
     const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    cudaError_t err = cudaSuccess;
+    if (max_P <= 32) err = prefer_shared(reinterpret_cast<const void*>(weights_kernel<32>));
+    else if (max_P <= 128) err = prefer_shared(reinterpret_cast<const void*>(weights_kernel<128>));
+    else if (max_P <= 512) err = prefer_shared(reinterpret_cast<const void*>(weights_kernel<512>));
+    else if (max_P <= 1024) err = prefer_shared(reinterpret_cast<const void*>(weights_kernel<1024>));
+    if (err != cudaSuccess) return err;
     if (max_P <= 32) weights_kernel<32><<<blocks, threads, 0, stream>>>(p, max_T);
     else if (max_P <= 128) weights_kernel<128><<<blocks, threads, 0, stream>>>(p, max_T);
     else if (max_P <= 512) weights_kernel<512><<<blocks, threads, 0, stream>>>(p, max_T);
@@ -1344,13 +1835,27 @@ cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool 
     return cudaGetLastError();
 }
 
-cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_t stream) {
+cudaError_t launch_fill_zero_bulk(float* dst, int64_t count, int num_sms, cudaStream_t stream) {
+    if (count <= 0) return cudaSuccess;
+    cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(fill_zero_bulk_kernel), kFillTileBytes);
+    if (err != cudaSuccess) return err;
+    const int64_t tiles = (count * 4 + kFillTileBytes - 1) / kFillTileBytes;
+    int64_t blocks = num_sms;
+    if (blocks > tiles) blocks = tiles;
+    if (blocks < 1) blocks = 1;
+    fill_zero_bulk_kernel<<<static_cast<unsigned>(blocks), 32, kFillTileBytes, stream>>>(dst, count);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_t stream, int blocks_per_sm) {
     if (count <= 0) return cudaSuccess;
     const int threads = 512;
     int64_t blocks = (count / 4 + threads - 1) / threads;
-    const int64_t max_blocks = static_cast<int64_t>(num_sms) * 4;
+    const int64_t max_blocks = static_cast<int64_t>(num_sms) * blocks_per_sm;
     if (blocks > max_blocks) blocks = max_blocks;
     if (blocks < 1) blocks = 1;
+    cudaError_t err = prefer_shared(reinterpret_cast<const void*>(fill_zero_kernel));
+    if (err != cudaSuccess) return err;
     fill_zero_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(dst, count);
     return cudaGetLastError();
 }
@@ -1397,6 +1902,8 @@ cudaError_t launch_widen_16(const uint16_t* src, float* dst, int64_t count, int 
     if (count <= 0) return cudaSuccess;
     int64_t blocks = (count + 255) / 256;
     if (blocks > 65535) blocks = 65535;
+    cudaError_t err = prefer_shared(reinterpret_cast<const void*>(widen_16_kernel));
+    if (err != cudaSuccess) return err;
     widen_16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, count, is_bf16);
     return cudaGetLastError();
 }

@@ -2,6 +2,10 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -86,12 +90,33 @@ namespace {
 struct EventPair {
     cudaEvent_t a, b;
     int kernel;
+    int dev;
 };
 std::mutex g_prof_mu;
-bool g_prof_on = false;
+unsigned g_prof_mask = 0;   // bit i: time kernel i
 std::vector<EventPair> g_prof_pending;
 double g_prof_ms[kProfiledKernels] = {0};
 long long g_prof_n[kProfiledKernels] = {0};
+
+// Timing events are recycled per device: creating and destroying events
+// around every launch costs more host time than the launches themselves.
+std::vector<std::pair<int, cudaEvent_t>> g_prof_free;
+
+cudaEvent_t prof_take_event_locked(int dev) {
+    for (size_t i = g_prof_free.size(); i-- > 0;) {
+        if (g_prof_free[i].first == dev) {
+            cudaEvent_t e = g_prof_free[i].second;
+            g_prof_free.erase(g_prof_free.begin() + static_cast<std::ptrdiff_t>(i));
+            return e;
+        }
+    }
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return e;
+}
 
 void prof_drain_locked() {
     for (EventPair& p : g_prof_pending) {
@@ -102,8 +127,8 @@ void prof_drain_locked() {
         } else {
             cudaGetLastError();
         }
-        cudaEventDestroy(p.a);
-        cudaEventDestroy(p.b);
+        g_prof_free.emplace_back(p.dev, p.a);
+        g_prof_free.emplace_back(p.dev, p.b);
     }
     g_prof_pending.clear();
 }
@@ -113,15 +138,19 @@ struct ProfileScope {
     cudaEvent_t a = nullptr, b = nullptr;
     cudaStream_t s;
     int kernel;
+    int dev = 0;
     ProfileScope(int k, cudaStream_t stream) : s(stream), kernel(k) {
-        bool on;
-        {
-            std::lock_guard<std::mutex> lock(g_prof_mu);
-            on = g_prof_on;
-        }
-        if (!on) return;
-        if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) {
+        std::lock_guard<std::mutex> lock(g_prof_mu);
+        if (!((g_prof_mask >> k) & 1u)) return;
+        if (cudaGetDevice(&dev) != cudaSuccess) {
             cudaGetLastError();
+            return;
+        }
+        a = prof_take_event_locked(dev);
+        b = prof_take_event_locked(dev);
+        if (!a || !b) {
+            if (a) g_prof_free.emplace_back(dev, a);
+            if (b) g_prof_free.emplace_back(dev, b);
             a = b = nullptr;
             return;
         }
@@ -131,7 +160,36 @@ struct ProfileScope {
         if (!a) return;
         cudaEventRecord(b, s);
         std::lock_guard<std::mutex> lock(g_prof_mu);
-        g_prof_pending.push_back(EventPair{a, b, kernel});
+        g_prof_pending.push_back(EventPair{a, b, kernel, dev});
+        if (g_prof_pending.size() >= 65536) prof_drain_locked();  // bound memory when left on
+    }
+};
+
+// Host-side phase timing of one call, printed to stderr when the environment
+// variable DBS_HOST_TRACE is set (read once). Costs one branch otherwise.
+struct HostTrace {
+    const char* what;
+    bool on;
+    std::chrono::steady_clock::time_point t0, last;
+    std::string line;
+    explicit HostTrace(const char* w) : what(w) {
+        static const bool enabled = std::getenv("DBS_HOST_TRACE") != nullptr;
+        on = enabled;
+        if (on) t0 = last = std::chrono::steady_clock::now();
+    }
+    void mark(const char* label) {
+        if (!on) return;
+        const auto now = std::chrono::steady_clock::now();
+        const double us = std::chrono::duration<double, std::micro>(now - last).count();
+        char buf[96];
+        std::snprintf(buf, sizeof(buf), " | %s +%.1fus", label, us);
+        line += buf;
+        last = now;
+    }
+    ~HostTrace() {
+        if (!on) return;
+        const double us = std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+        std::fprintf(stderr, "[dbs %s] %.1fus%s\n", what, us, line.c_str());
     }
 };
 
@@ -166,8 +224,28 @@ struct Slot {
     char* pinned = nullptr;
     size_t pinned_bytes = 0;
     cudaEvent_t done = nullptr;
+    cudaEvent_t validated = nullptr;   // input validation status has reached the staging buffer
     bool in_use = false;
+    // counters of an asynchronous decode, read back into the staging buffer
+    const unsigned long long* pending = nullptr;
 };
+
+std::atomic<unsigned long long> g_last_merge_rescans{0};
+std::atomic<unsigned long long> g_timeouts{0};
+
+// Reads the counters an asynchronous decode left in the slot (its event has
+// completed); a device wait timeout surfaces here as an error.
+void settle(Slot* s) {
+    if (!s->pending) return;
+    const unsigned long long merge = s->pending[1];
+    const unsigned long long timeout = s->pending[3];
+    s->pending = nullptr;
+    g_last_merge_rescans.store(merge);
+    if (timeout) {
+        g_timeouts.fetch_add(1);
+        throw CudaFailure("an earlier asynchronous decode reported a device wait timeout");
+    }
+}
 
 class Arena {
   public:
@@ -189,12 +267,20 @@ class Arena {
                 s = new Slot;
                 s->device = device;
                 check_cuda(cudaEventCreateWithFlags(&s->done, cudaEventDisableTiming), "cudaEventCreate");
+                check_cuda(cudaEventCreateWithFlags(&s->validated, cudaEventDisableTiming), "cudaEventCreate");
                 slots_.push_back(s);
             }
             s->in_use = true;
         }
         // the host writes the staging buffer below: the previous use must be over
         check_cuda(cudaEventSynchronize(s->done), "workspace reuse");
+        try {
+            settle(s);
+        } catch (...) {
+            std::lock_guard<std::mutex> lock(mu_);
+            s->in_use = false;
+            throw;
+        }
         if (s->dev_bytes < dev_bytes) {
             if (s->dev) check_cuda(cudaFree(s->dev), "cudaFree(workspace)");
             s->dev = nullptr;
@@ -246,11 +332,39 @@ struct Lease {
     Lease& operator=(const Lease&) = delete;
 };
 
+// Per-device helper stream and events for work that runs beside the step
+// merge (the dense gradient zero fill).
+struct Helper {
+    cudaStream_t side = nullptr;
+    cudaEvent_t before = nullptr;
+    cudaEvent_t after = nullptr;
+};
+std::mutex g_helper_mu;
+std::vector<Helper> g_helpers;
+
+Helper& helper_locked() {
+    int dev = 0;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev >= static_cast<int>(g_helpers.size())) g_helpers.resize(dev + 1);
+    Helper& h = g_helpers[dev];
+    if (!h.side) {
+        check_cuda(cudaStreamCreateWithFlags(&h.side, cudaStreamNonBlocking), "cudaStreamCreate(helper)");
+        check_cuda(cudaEventCreateWithFlags(&h.before, cudaEventDisableTiming), "cudaEventCreate");
+        check_cuda(cudaEventCreateWithFlags(&h.after, cudaEventDisableTiming), "cudaEventCreate");
+    }
+    return h;
+}
+
 }  // namespace
 
-void profile_enable(bool on) {
+void last_decode_diagnostics(unsigned long long* merge_rescans, unsigned long long* timeouts) {
+    if (merge_rescans) *merge_rescans = g_last_merge_rescans.load();
+    if (timeouts) *timeouts = g_timeouts.load();
+}
+
+void profile_enable(unsigned mask) {
     std::lock_guard<std::mutex> lock(g_prof_mu);
-    g_prof_on = on;
+    g_prof_mask = mask;
 }
 
 void profile_reset() {
@@ -276,9 +390,10 @@ void profile_read(int kernel, double* total_ms, long long* launches) {
 
 void decode(const Options& opt, const float* d_x, int V, const std::vector<ExampleSpec>& ex,
             const CallConstraints& cons, const Outputs& out, const Layout& layout, bool pool,
-            bool weights, cudaStream_t stream, DecodeStats* stats, bool synchronize) {
+            bool weights, cudaStream_t stream, DecodeStats* stats, const DecodeControl& ctl) {
     const int B = static_cast<int>(ex.size());
     if (B <= 0) return;
+    HostTrace trace("decode");
     const bool dynamic = cons.repetition_penalty > 1.0f || cons.no_repeat_ngram > 0;
 
     std::vector<dbs_dev::ExampleDesc> desc(B);
@@ -351,7 +466,9 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     ws += bytes_of<int32_t>(static_cast<size_t>(rows));
     ws += bytes_of<float>(static_cast<size_t>(rows));
     if (dynamic) ws += bytes_of<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
+    trace.mark("prepared");
     Lease lease(ws, hdr, stream);
+    trace.mark("slot");
     Carve cv{static_cast<char*>(lease.s->dev), 0, ws};
     Carve hv{lease.s->pinned, 0, hdr};
 
@@ -413,15 +530,59 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     p.final_raw_scores = out.final_raw_scores;
     p.final_scores = out.final_scores;
 
+    // status and counters are contiguous in the header: one read-back each time
+    const size_t st_off = reinterpret_cast<char*>(p.status) - static_cast<char*>(lease.s->dev);
+    const size_t st_bytes = reinterpret_cast<char*>(p.counters + 4) - reinterpret_cast<char*>(p.status);
     if (opt.validate_inputs) {
-        ProfileScope ps(kValidate, stream);
-        check_cuda(dbs_dev::launch_validate(p, stream), "validate kernel");
+        {
+            ProfileScope ps(kValidate, stream);
+            check_cuda(dbs_dev::launch_validate(p, stream), "validate kernel");
+        }
+        check_cuda(cudaMemcpyAsync(lease.s->pinned + st_off, p.status, st_bytes, cudaMemcpyDeviceToHost, stream),
+                   "read status");
+        check_cuda(cudaEventRecord(lease.s->validated, stream), "cudaEventRecord");
     }
     {
         ProfileScope ps(kRowScan, stream);
         check_cuda(dbs_dev::launch_row_scan(p, max_C, device_sm_count(), stream), "row scan kernel");
     }
-    {
+    trace.mark("row scan queued");
+    if (opt.validate_inputs) {
+        // The reference rejects NaN / +Inf before decoding. The row scan is
+        // already queued (it only writes this call's workspace and tolerates
+        // any value), so the GPU keeps streaming while the host waits for the
+        // small validation kernel; nothing that writes an output is queued
+        // before the verdict.
+        check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
+        trace.mark("validate synced");
+        for (int b = 0; b < B; ++b)
+            if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
+    }
+    if (ctl.zero_fill && ctl.zero_fill_count > 0) {
+        // zero the gradient buffer on the helper stream while the (latency
+        // bound, few-CTA) step merge runs; `stream` waits for it afterwards
+        // The merge is queued first; the fill is one 32-thread CTA per SM
+        // issuing bulk stores, so merge CTAs always fit beside it and keep
+        // the load/store pipe to themselves.
+        std::lock_guard<std::mutex> lock(g_helper_mu);
+        Helper& hp = helper_locked();
+        check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
+        {
+            ProfileScope ps(kStepMerge, stream);
+            check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream),
+                       "step merge kernel");
+        }
+        trace.mark("merge queued");
+        check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
+        {
+            ProfileScope ps(kFillZero, hp.side);
+            check_cuda(dbs_dev::launch_fill_zero_bulk(ctl.zero_fill, ctl.zero_fill_count, device_sm_count(), hp.side),
+                       "zero fill kernel");
+        }
+        check_cuda(cudaEventRecord(hp.after, hp.side), "cudaEventRecord");
+        trace.mark("fill queued");
+        check_cuda(cudaStreamWaitEvent(stream, hp.after, 0), "cudaStreamWaitEvent");
+    } else {
         ProfileScope ps(kStepMerge, stream);
         check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream), "step merge kernel");
     }
@@ -430,28 +591,27 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         ProfileScope ps(kWeights, stream);
         check_cuda(dbs_dev::launch_weights(p, max_T, max_K, max_P, stream), "weights kernel");
     }
-
-    if (synchronize) {
-        // status and counters are contiguous in the header: one read-back
-        const size_t off = reinterpret_cast<char*>(p.status) - static_cast<char*>(lease.s->dev);
-        const size_t n = reinterpret_cast<char*>(p.counters + 4) - reinterpret_cast<char*>(p.status);
-        check_cuda(cudaMemcpyAsync(lease.s->pinned + off, p.status, n, cudaMemcpyDeviceToHost, stream),
-                   "read status");
+    check_cuda(cudaMemcpyAsync(lease.s->pinned + st_off, p.status, st_bytes, cudaMemcpyDeviceToHost, stream),
+               "read counters");
+    if (ctl.synchronize) {
         check_cuda(cudaStreamSynchronize(stream), "decode");
         if (stats) {
             stats->row_rescans = h_counters[0];
             stats->merge_fallbacks = h_counters[1];
         }
-        if (h_counters[3]) throw CudaFailure("row scan: a shared-memory copy did not complete within the wait bound");
-        if (opt.validate_inputs) {
-            for (int b = 0; b < B; ++b)
-                if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
+        g_last_merge_rescans.store(h_counters[1]);
+        if (h_counters[3]) {
+            g_timeouts.fetch_add(1);
+            throw CudaFailure("row scan: a shared-memory copy did not complete within the wait bound");
         }
+    } else {
+        lease.s->pending = h_counters;
     }
 }
 
 void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, const Layout& layout,
               const BackwardInputs& in, const BackwardOutputs& out, cudaStream_t stream, bool zero_dense) {
+    HostTrace trace("backward");
     const int B = static_cast<int>(ex.size());
     if (B <= 0) return;
     std::vector<dbs_dev::ExampleDesc> desc(B);
@@ -481,7 +641,9 @@ void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, con
     const bool sparse = out.sparse_indices != nullptr;
     const size_t hdr = bytes_of<dbs_dev::ExampleDesc>(B) + bytes_of<float>(lmax + 1);
     const size_t ws = hdr + bytes_of<int32_t>(static_cast<size_t>(B) * max_T);
+    trace.mark("prepared");
     Lease lease(ws, hdr, stream);
+    trace.mark("slot");
     Carve cv{static_cast<char*>(lease.s->dev), 0, ws};
     Carve hv{lease.s->pinned, 0, hdr};
     auto* d_desc = cv.take<dbs_dev::ExampleDesc>(B);
@@ -526,6 +688,7 @@ void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, con
     p.grad_initial = out.grad_initial;
     ProfileScope ps(kBackward, stream);
     check_cuda(dbs_dev::launch_backward(p, max_K, max_P, sparse, stream), "backward kernel");
+    trace.mark("queued");
 }
 
 }  // namespace dbs_host

@@ -110,9 +110,26 @@ struct DecodeStats {
     unsigned long long merge_fallbacks = 0;
 };
 
+// How a decode call meets the host. Validation (when enabled) is always
+// checked before the heavy kernels are launched: the call waits for the small
+// validation kernel only. With `synchronize` the call also waits for the
+// whole decode (host mirrors need it); otherwise it returns as soon as the
+// kernels are queued and its diagnostics are checked when its workspace slot
+// is reused. `zero_fill` (optional) is a buffer the call zeroes on a helper
+// stream while the step merge runs; later work on `stream` sees the zeros.
+struct DecodeControl {
+    bool synchronize = true;
+    float* zero_fill = nullptr;
+    int64_t zero_fill_count = 0;
+};
+
 void decode(const Options& opt, const float* d_x, int V, const std::vector<ExampleSpec>& ex,
             const CallConstraints& cons, const Outputs& out, const Layout& layout, bool pool,
-            bool weights, cudaStream_t stream, DecodeStats* stats, bool synchronize = true);
+            bool weights, cudaStream_t stream, DecodeStats* stats, const DecodeControl& ctl);
+
+// Diagnostics of the most recent decode whose counters have been read back
+// (process-wide): rows rescanned by the step merge, device wait timeouts.
+void last_decode_diagnostics(unsigned long long* merge_rescans, unsigned long long* timeouts);
 
 struct BackwardInputs {
     // trace (device), tight layout from `decode`
@@ -145,12 +162,12 @@ void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, con
 
 int device_sm_count();
 
-// Live kernel timing: when enabled, every engine launch is bracketed by a pair
-// of CUDA events recorded on the launch stream; read() waits for them and
-// returns the summed device time per kernel.
+// Live kernel timing: every launch of a kernel whose bit is set in the mask is
+// bracketed by a pair of CUDA events recorded on the launch stream; read()
+// waits for them and returns the summed device time per kernel.
 enum ProfiledKernel { kValidate = 0, kRowScan = 1, kStepMerge = 2, kWeights = 3, kFillZero = 4, kBackward = 5,
                       kProfiledKernels = 6 };
-void profile_enable(bool on);
+void profile_enable(unsigned mask);
 void profile_reset();
 void profile_read(int kernel, double* total_ms, long long* launches);
 

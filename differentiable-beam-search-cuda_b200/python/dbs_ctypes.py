@@ -194,12 +194,18 @@ DEVICE_FUNCTIONS = {
              ctypes.POINTER(DBSDeviceDecodeOutputs), _VP]),
     "dbs_device_backward_batch": (
         _I, [_VP, _I, _I, _I, ctypes.POINTER(DBSDeviceDecodeOutputs), _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
+    "dbs_device_decode_batch_ex": (_I, [_VP, _VP, _I, _I, _I, ctypes.POINTER(DBSDeviceDecodeOutputs), _VP, _I64, _VP]),
+    "dbs_device_backward_batch_ex": (
+        _I, [_VP, _I, _I, _I, ctypes.POINTER(DBSDeviceDecodeOutputs), _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I,
+             _VP]),
     "dbs_device_last_rescan_counts": (_I, [_VP, ctypes.POINTER(_I64), ctypes.POINTER(_I64)]),
     "dbs_device_profile": (_I, [_I]),
     "dbs_device_profile_read": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_I64)]),
+    "dbs_device_profile_kernels": (_I, [ctypes.c_uint]),
 }
 
 PROFILED_KERNELS = ("validate", "row_scan", "step_merge", "weights", "fill_zero", "backward")
+DBS_DEVICE_GRAD_PREZEROED = 1
 
 
 def load_library(path: Optional[str] = None, device_api: bool = True) -> ctypes.CDLL:

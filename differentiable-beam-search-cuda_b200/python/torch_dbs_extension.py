@@ -215,34 +215,46 @@ class DeviceTrace:
 
 
 def device_decode(x4: torch.Tensor, options: DBSOptions, with_pool: bool = False,
-                  with_weights: bool = False) -> DeviceTrace:
-    """Decode a contiguous fp32 CUDA tensor [B,T,K,V] on its device."""
+                  with_weights: bool = False, zero_fill: Optional[torch.Tensor] = None) -> DeviceTrace:
+    """Decode a contiguous fp32 CUDA tensor [B,T,K,V] on its device.
+
+    `zero_fill`, when given, is a float32 tensor the call zeroes beside the
+    step merge (the autograd path passes the gradient its backward fills).
+    """
     B, T, K, V = (int(s) for s in x4.shape)
     P = max(K, K * options.relaxed_pool_multiplier)
     trace = DeviceTrace(B, T, K, x4.device, with_pool=with_pool, P=P, with_weights=with_weights)
     lib = _library()
     h = _handle(options)
     outs = trace.struct()
+    zf = None if zero_fill is None else _vp(zero_fill)
+    zn = 0 if zero_fill is None else int(zero_fill.numel())
     with torch.cuda.device(x4.device):
-        rc = lib.dbs_device_decode_batch(h, _vp(x4), B, T, V, ctypes.byref(outs), _stream_ptr(x4.device))
+        rc = lib.dbs_device_decode_batch_ex(h, _vp(x4), B, T, V, ctypes.byref(outs), zf, zn, _stream_ptr(x4.device))
     _check(rc, h, "dbs_decode")
     return trace
 
 
 def device_backward_dense(trace: DeviceTrace, grad_final: torch.Tensor, options: DBSOptions, V: int,
-                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Dense surrogate gradient [B,T,K,V] of the final scores, on the device."""
+                          out: Optional[torch.Tensor] = None, prezeroed: bool = False) -> torch.Tensor:
+    """Dense surrogate gradient [B,T,K,V] of the final scores, on the device.
+
+    With `prezeroed`, `out` already holds zeros and only its non-zero
+    entries are written.
+    """
     B, T, K = (int(s) for s in trace.parents.shape)
     device = trace.parents.device
     if out is None:
         out = torch.empty((B, T, K, V), dtype=torch.float32, device=device)
+        prezeroed = False
     g = grad_final.detach().to(device=device, dtype=torch.float32).contiguous()
     lib = _library()
     h = _handle(options)
     tr = trace.struct()
+    flags = dbs_ctypes.DBS_DEVICE_GRAD_PREZEROED if prezeroed else 0
     with torch.cuda.device(device):
-        rc = lib.dbs_device_backward_batch(h, B, T, V, ctypes.byref(tr), None, None, _vp(g), _vp(out), None, None,
-                                           None, None, _stream_ptr(device))
+        rc = lib.dbs_device_backward_batch_ex(h, B, T, V, ctypes.byref(tr), None, None, _vp(g), _vp(out), None, None,
+                                              None, None, flags, _stream_ptr(device))
     _check(rc, h, "dbs_backward")
     return out
 
@@ -261,10 +273,14 @@ class _DBSFinalScores(torch.autograd.Function):
         # (python/torch_dbs_extension.py:244-245).
         x = log_probs.detach().to(device=device, dtype=torch.float32).contiguous()
         x4 = x.unsqueeze(0) if unbatched else x
-        trace = device_decode(x4, options)
+        # The dense gradient is allocated here and zeroed beside the step
+        # merge, so the backward only writes its non-zero entries.
+        grad = torch.empty_like(x4) if ctx.needs_log_probs_grad else None
+        trace = device_decode(x4, options, zero_fill=grad)
         ctx.V = int(x4.size(3))
         if ctx.needs_log_probs_grad:
             ctx.trace = trace
+            ctx.grad = grad
         scores = trace.final_scores
         if unbatched:
             scores = scores.squeeze(0)
@@ -278,10 +294,13 @@ class _DBSFinalScores(torch.autograd.Function):
         g = grad_output
         if g.dim() == 1:
             g = g.unsqueeze(0)
-        grad = device_backward_dense(trace, g, ctx.options, ctx.V)
+        # the pre-zeroed buffer serves the first backward; a repeated backward
+        # (retain_graph) gets a fresh, zero-filled one
+        pre = getattr(ctx, "grad", None)
+        grad = device_backward_dense(trace, g, ctx.options, ctx.V, out=pre, prezeroed=pre is not None)
+        ctx.grad = None
         if ctx.unbatched:
             grad = grad.squeeze(0)
-        del ctx.trace
         return grad.to(device=ctx.input_device, dtype=ctx.input_dtype), None
 
 

@@ -91,9 +91,31 @@ DBS_EXPORT int dbs_device_backward_batch(DBSDecoderHandle* handle, int batch_siz
                                          int64_t* sparse_counts, float* grad_initial_scores,
                                          void* cuda_stream);
 
-/* Diagnostics of the last device decode on this handle: rows whose guessed
- * scan threshold was too high and were rescanned, and rows the step merge
- * could not prove complete and rescanned. */
+/* dbs_device_decode_batch plus an optional buffer to zero: `zero_fill`
+ * (count elements, device) is cleared on a helper stream while the step
+ * merge runs, and later work on `cuda_stream` sees the zeros. The autograd
+ * path uses it for the dense gradient its backward will scatter into. */
+DBS_EXPORT int dbs_device_decode_batch_ex(DBSDecoderHandle* handle, const float* log_probs, int batch_size,
+                                          int steps, int vocab_size, const DBSDeviceDecodeOutputs* outputs,
+                                          float* zero_fill, int64_t zero_fill_count, void* cuda_stream);
+
+/* dbs_device_backward_batch with flags; DBS_DEVICE_GRAD_PREZEROED means the
+ * dense grad_log_probs already holds zeros (e.g. from zero_fill above), so
+ * only the non-zero entries are written. */
+#define DBS_DEVICE_GRAD_PREZEROED 1
+DBS_EXPORT int dbs_device_backward_batch_ex(DBSDecoderHandle* handle, int batch_size, int steps,
+                                            int vocab_size, const DBSDeviceDecodeOutputs* trace,
+                                            const float* grad_selected_weights,
+                                            const float* grad_relaxed_weights,
+                                            const float* grad_final_scores, float* grad_log_probs,
+                                            int64_t* sparse_indices, float* sparse_values,
+                                            int64_t* sparse_counts, float* grad_initial_scores, int flags,
+                                            void* cuda_stream);
+
+/* Diagnostics of the most recent device decode whose counters have been read
+ * back (process-wide): rows rescanned by the row scan (always 0: the scan is
+ * exact in one pass) and rows the step merge could not prove complete and
+ * rescanned from HBM. */
 DBS_EXPORT int dbs_device_last_rescan_counts(DBSDecoderHandle* handle, int64_t* row_rescans,
                                              int64_t* merge_rescans);
 
@@ -106,6 +128,10 @@ DBS_EXPORT int dbs_device_last_rescan_counts(DBSDecoderHandle* handle, int64_t* 
  * src/differentiable_beam.cpp:3115-3143). */
 DBS_EXPORT int dbs_device_profile(int enable);
 DBS_EXPORT int dbs_device_profile_read(int kernel, double* total_ms, int64_t* launches);
+/* Times only the kernels whose bit (1 << kernel id above) is set in `mask`
+ * (0 stops timing), so a benchmark can time one kernel inside a timed region
+ * with two events per launch of that kernel and none elsewhere. */
+DBS_EXPORT int dbs_device_profile_kernels(unsigned mask);
 
 #ifdef __cplusplus
 }
