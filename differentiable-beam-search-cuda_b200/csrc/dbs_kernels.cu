@@ -1591,6 +1591,159 @@ __global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max
 }
 
 // ---------------------------------------------------------------------------
+// 4b. Dense surrogate backward for beams of at most 32: everything that does
+//     not depend on the reverse recursion (per-step dot products and pool
+//     centres, each selected slot's own rank gradient times 1/gnmt, the whole
+//     relaxed-pool contribution) is computed for all steps in parallel first;
+//     the recursion itself (draw = next_g[k] + own term, then the per-parent
+//     sums in the reference's order: selected k ascending, then pool q
+//     ascending) runs in one warp out of shared memory, lane k owning beam k.
+//     The arithmetic is the same sequence of rounded operations as the block
+//     kernel above. A gradient index receives at most two contributions (the
+//     selected slot and the pool slot of the same candidate); both are added
+//     with atomicAdd into the zeroed buffer, which is exact in either order.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) backward_sweep_kernel(BackwardParams p, int max_T, int max_K, int max_P,
+                                                             int with_pool) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int e = blockIdx.x;
+    const ExampleDesc d = p.desc[e];
+    const int K = d.K, T = d.T, P = d.P;
+    const int64_t V = p.V;
+    const int tid = threadIdx.x;
+    const int NT = blockDim.x;
+    float* own = reinterpret_cast<float*>(smem);                 // [T*K] drank * inv_pen[len]
+    int* par = reinterpret_cast<int*>(own + max_T * max_K);      // [T*K] parent (-1 none)
+    int* tok = par + max_T * max_K;                              // [T*K] token if it writes, else -1
+    float* dot = reinterpret_cast<float*>(tok + max_T * max_K);  // [T]
+    float* center = dot + max_T;                                 // [T]
+    int* relax = reinterpret_cast<int*>(center + max_T);         // [T]
+    int* ppar = relax + max_T;                                   // [T*P] pool parent with a draw, else -1
+    float* pdraw = reinterpret_cast<float*>(ppar + (with_pool ? max_T * max_P : 0));  // [T*P]
+
+    // per-step reductions, in the reference's sequential order
+    for (int t = tid; t < T; t += NT) {
+        const int64_t so = d.sel_offset + static_cast<int64_t>(t) * d.sel_t_stride;
+        const int64_t po = d.pool_offset + static_cast<int64_t>(t) * d.pool_t_stride;
+        float dt = 0.0f;
+        if (p.grad_selected)
+            for (int k = 0; k < K; ++k) dt = __fadd_rn(dt, __fmul_rn(p.weights[so + k], p.grad_selected[so + k]));
+        dot[t] = dt;
+        int rl = 0;
+        float ctr = 0.0f;
+        if (p.grad_relaxed) {
+            float denom = 0.0f, numer = 0.0f;
+            for (int q = 0; q < P; ++q) {
+                const float w = p.relaxed_weights[po + q];
+                const float a = __fmul_rn(w, __fsub_rn(1.0f, w));
+                denom = __fadd_rn(denom, a);
+                numer = __fadd_rn(numer, __fmul_rn(p.grad_relaxed[po + q], a));
+            }
+            if (denom > 1.0e-12f) {
+                rl = 1;
+                ctr = __fdiv_rn(numer, denom);
+            }
+        }
+        relax[t] = rl;
+        center[t] = ctr;
+    }
+    __syncthreads();
+    // selected slots: the part of each draw that does not depend on next_g
+    for (int idx = tid; idx < T * K; idx += NT) {
+        const int t = idx / K;
+        const int k = idx - t * K;
+        const int64_t so = d.sel_offset + static_cast<int64_t>(t) * d.sel_t_stride;
+        const int parent = p.parents[so + k];
+        float m = 0.0f;
+        int tk = -1;
+        if (parent >= 0) {
+            float drank = 0.0f;
+            if (p.grad_selected) {
+                const float w = p.weights[so + k];
+                drank = __fadd_rn(drank, __fdiv_rn(__fmul_rn(w, __fsub_rn(p.grad_selected[so + k], dot[t])),
+                                                   p.selected_temperature));
+            }
+            if (p.grad_final && t == T - 1) drank = __fadd_rn(drank, p.grad_final[d.final_offset + k]);
+            const int len = p.lengths[so + k] < 1 ? 1 : p.lengths[so + k];
+            m = __fmul_rn(drank, p.inv_pen[len]);
+            const int token = p.tokens[so + k];
+            if (p.from_logprob[so + k] && token >= 0) tk = token;
+        }
+        own[idx] = m;
+        par[idx] = parent;
+        tok[idx] = tk;
+    }
+    // relaxed pool: independent of the recursion, written now
+    if (with_pool) {
+        const float inv_temp_soft = __fdiv_rn(1.0f, p.soft_topk_temperature);
+        for (int idx = tid; idx < T * P; idx += NT) {
+            const int t = idx / P;
+            const int q = idx - t * P;
+            int pp = -1;
+            float draw = 0.0f;
+            if (relax[t]) {
+                const int64_t po = d.pool_offset + static_cast<int64_t>(t) * d.pool_t_stride;
+                const int parent = p.pool_parents[po + q];
+                if (parent >= 0) {
+                    const float w = p.relaxed_weights[po + q];
+                    const float a = __fmul_rn(w, __fsub_rn(1.0f, w));
+                    const float drank = __fmul_rn(__fmul_rn(a, inv_temp_soft), __fsub_rn(p.grad_relaxed[po + q], center[t]));
+                    if (drank != 0.0f) {
+                        const int len = p.pool_lengths[po + q] < 1 ? 1 : p.pool_lengths[po + q];
+                        draw = __fmul_rn(drank, p.inv_pen[len]);
+                        const int token = p.pool_tokens[po + q];
+                        if (draw != 0.0f && p.pool_from_logprob[po + q] && token >= 0) {
+                            const int64_t gi = (static_cast<int64_t>(t) * K + parent) * V + token;
+                            atomicAdd(p.grad_dense + d.grad_offset + gi, draw);
+                        }
+                    }
+                }
+                pp = (parent >= 0 && draw != 0.0f) ? parent : -1;
+            }
+            ppar[idx] = pp;
+            pdraw[idx] = draw;
+        }
+    }
+    __syncthreads();
+    if (tid >= 32) return;
+    // the recursion: one warp, lane k = beam k
+    const int lane = tid;
+    float g = 0.0f;
+    for (int t = T - 1; t >= 0; --t) {
+        float draw = 0.0f;
+        int sp = -1;
+        if (lane < K) {
+            const int idx = t * K + lane;
+            const int parent = par[idx];
+            if (parent >= 0) {
+                draw = __fadd_rn(g, own[idx]);
+                const int tk = tok[idx];
+                if (draw != 0.0f && tk >= 0) {
+                    const int64_t gi = (static_cast<int64_t>(t) * K + parent) * V + tk;
+                    if (with_pool && relax[t]) atomicAdd(p.grad_dense + d.grad_offset + gi, draw);
+                    else p.grad_dense[d.grad_offset + gi] = draw;
+                }
+                if (draw != 0.0f) sp = parent;
+            }
+        }
+        float acc = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            const int pk = __shfl_sync(0xFFFFFFFFu, sp, k);
+            const float dk = __shfl_sync(0xFFFFFFFFu, draw, k);
+            if (pk == lane) acc = __fadd_rn(acc, dk);
+        }
+        if (with_pool && relax[t]) {
+            const int* pq = ppar + t * P;
+            const float* dq = pdraw + t * P;
+            for (int q = 0; q < P; ++q)
+                if (pq[q] == lane) acc = __fadd_rn(acc, dq[q]);
+        }
+        g = acc;
+    }
+    if (lane < K && p.grad_initial) p.grad_initial[d.final_offset + lane] = g;
+}
+
+// ---------------------------------------------------------------------------
 // 5. Zero fill with 128-bit stores (dense gradient).
 // ---------------------------------------------------------------------------
 __global__ void fill_zero_kernel(float* __restrict__ dst, int64_t count) {
@@ -1823,7 +1976,25 @@ cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_
     return cudaGetLastError();
 }
 
+static size_t backward_sweep_smem(int max_T, int max_K, int max_P, bool with_pool) {
+    size_t b = static_cast<size_t>(max_T) * max_K * (sizeof(float) + 2 * sizeof(int));
+    b += static_cast<size_t>(max_T) * (2 * sizeof(float) + sizeof(int));
+    if (with_pool) b += static_cast<size_t>(max_T) * max_P * (sizeof(int) + sizeof(float));
+    return b;
+}
+constexpr size_t kBackwardSweepSmemBudget = 96 * 1024;
+
 cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool sparse, cudaStream_t stream) {
+    if (!sparse && max_K <= 32 && p.grad_dense) {
+        const bool with_pool = p.grad_relaxed != nullptr;
+        const size_t smem = backward_sweep_smem(p.max_T, max_K, max_P, with_pool);
+        if (smem <= kBackwardSweepSmemBudget) {
+            cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(backward_sweep_kernel), smem);
+            if (err != cudaSuccess) return err;
+            backward_sweep_kernel<<<p.B, 256, smem, stream>>>(p, p.max_T, max_K, max_P, with_pool ? 1 : 0);
+            return cudaGetLastError();
+        }
+    }
     const size_t smem = static_cast<size_t>(max_K) * 3 * sizeof(float) + static_cast<size_t>(max_P) * sizeof(float) +
                         static_cast<size_t>(max_K + max_P) * sizeof(int) + 16 +
                         static_cast<size_t>(max_K + max_P) * (sizeof(int64_t) + sizeof(float));
