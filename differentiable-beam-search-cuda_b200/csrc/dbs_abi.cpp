@@ -1540,6 +1540,53 @@ DBS_EXPORT int dbs_device_backward_batch_ex(DBSDecoderHandle* handle, int batch_
     });
 }
 
+DBS_EXPORT int dbs_device_backward_sparse_noalloc(DBSDecoderHandle* handle, int batch_size, int steps,
+                                                  int vocab_size, const DBSDeviceDecodeOutputs* trace,
+                                                  const float* grad_selected_weights,
+                                                  const float* grad_relaxed_weights,
+                                                  const float* grad_final_scores, int64_t* sparse_indices,
+                                                  float* sparse_values, int64_t* sparse_counts,
+                                                  float* grad_initial_scores, void* cuda_stream) {
+    if (!handle || !trace) {
+        set_error(handle, "invalid decoder or trace pointer");
+        return -1;
+    }
+    return guarded(handle, [&]() {
+        const Options& opt = handle->options;
+        if (batch_size <= 0 || steps <= 0 || vocab_size <= 0)
+            throw std::invalid_argument("backward dimensions must be positive");
+        if (!sparse_indices || !sparse_values || !sparse_counts)
+            throw std::invalid_argument("sparse outputs need indices, values and counts");
+        if (grad_selected_weights && !trace->weights)
+            throw std::invalid_argument("grad_selected_weights needs the selected weights of the trace");
+        if (grad_relaxed_weights && (!trace->relaxed_weights || !trace->pool_parents))
+            throw std::invalid_argument("grad_relaxed_weights needs the relaxed pool of the trace");
+        dbs_host::BackwardInputs in;
+        in.parents = trace->parents;
+        in.tokens = trace->tokens;
+        in.lengths = trace->lengths;
+        in.weights = trace->weights;
+        in.from_logprob = trace->from_logprob;
+        in.pool_parents = trace->pool_parents;
+        in.pool_tokens = trace->pool_tokens;
+        in.pool_lengths = trace->pool_lengths;
+        in.relaxed_weights = trace->relaxed_weights;
+        in.pool_from_logprob = trace->pool_from_logprob;
+        in.grad_selected = grad_selected_weights;
+        in.grad_relaxed = grad_relaxed_weights;
+        in.grad_final = grad_final_scores;
+        dbs_host::BackwardOutputs bo;
+        bo.sparse_indices = sparse_indices;
+        bo.sparse_values = sparse_values;
+        bo.sparse_counts = sparse_counts;
+        bo.grad_initial = grad_initial_scores;
+        dbs_host::backward_sparse_noalloc(opt, vocab_size, batch_size, steps, in, bo,
+                                          static_cast<cudaStream_t>(cuda_stream));
+        clear_error(handle);
+        return 0;
+    });
+}
+
 DBS_EXPORT int dbs_device_profile(int enable) {
     try {
         if (enable < 0) {

@@ -154,6 +154,18 @@ cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_
 // the SMs' load/store pipes and registers to a kernel running beside it.
 cudaError_t launch_fill_zero_bulk(float* dst, int64_t count, int num_sms, cudaStream_t stream);
 
+// Sparse backward of a uniform batch whose only scratch is a static device
+// array (no allocation on the call path); inv_pen_host holds 1/gnmt(l) for
+// l = 0 .. T+1. Returns cudaErrorInvalidValue beyond the limits below.
+constexpr int kNoAllocMaxSteps = 510;
+constexpr int kNoAllocMaxStepCounts = 1 << 18;   // batch_size * steps (1 MiB of int32)
+constexpr int kNoAllocMaxBeamPlusPool = 4096;
+cudaError_t launch_backward_noalloc(const BackwardParams& p, int T, int K, int P, const float* inv_pen_host,
+                                    cudaStream_t stream);
+// Looks up this device's scratch address and sets the kernel's shared-memory
+// limit; the first call on each device does this work.
+cudaError_t noalloc_prepare();
+
 // Limits of this implementation.
 constexpr int kMaxMergeCandidates = 8192;   // K * C per step handled by one CTA
 constexpr int kRowScanThreads = 256;

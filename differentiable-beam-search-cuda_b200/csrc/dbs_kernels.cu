@@ -1406,10 +1406,13 @@ __global__ void weights_kernel(DecodeParams p, int max_T) {
 //    example walks t = T-1 .. 0. prev_raw_grad is accumulated per parent in
 //    the reference's order (selected k ascending, then pool p ascending).
 // ---------------------------------------------------------------------------
-__global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max_P) {
+// The per-example body; `d`, the 1/gnmt table and the [B, max_T] step-count
+// scratch come from the caller so the no-allocation variant below can supply
+// them without device metadata.
+__device__ __forceinline__ void backward_example(const BackwardParams& p, const ExampleDesc& d, int e,
+                                                 const float* __restrict__ inv_pen, int32_t* step_counts,
+                                                 int sparse, int max_K, int max_P) {
     extern __shared__ __align__(16) unsigned char smem[];
-    const int e = blockIdx.x;
-    const ExampleDesc d = p.desc[e];
     const int K = d.K, T = d.T, P = d.P;
     const int64_t V = p.V;
     const int tid = threadIdx.x;
@@ -1470,7 +1473,7 @@ __global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max
                 }
                 if (p.grad_final && t == T - 1) drank = __fadd_rn(drank, p.grad_final[d.final_offset + k]);
                 const int len = p.lengths[so + k] < 1 ? 1 : p.lengths[so + k];
-                draw = __fadd_rn(next_g[k], __fmul_rn(drank, p.inv_pen[len]));
+                draw = __fadd_rn(next_g[k], __fmul_rn(drank, inv_pen[len]));
                 const int token = p.tokens[so + k];
                 if (draw != 0.0f && p.from_logprob[so + k] && token >= 0) {
                     const int64_t gi = (static_cast<int64_t>(t) * K + parent) * V + token;
@@ -1499,7 +1502,7 @@ __global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max
                     const float drank = __fmul_rn(__fmul_rn(a, inv_temp_soft), __fsub_rn(p.grad_relaxed[po + q], center));
                     if (drank != 0.0f) {
                         const int len = p.pool_lengths[po + q] < 1 ? 1 : p.pool_lengths[po + q];
-                        draw = __fmul_rn(drank, p.inv_pen[len]);
+                        draw = __fmul_rn(drank, inv_pen[len]);
                         const int token = p.pool_tokens[po + q];
                         if (draw != 0.0f && p.pool_from_logprob[po + q] && token >= 0) {
                             const int64_t gi = (static_cast<int64_t>(t) * K + parent) * V + token;
@@ -1553,7 +1556,7 @@ __global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max
                     ++m;
                     a = b;
                 }
-                p.step_counts[static_cast<int64_t>(e) * p.max_T + t] = m;
+                step_counts[static_cast<int64_t>(e) * p.max_T + t] = m;
             }
         }
         __syncthreads();
@@ -1567,7 +1570,7 @@ __global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max
         __syncthreads();
         int64_t off = 0;
         for (int t = 0; t < T; ++t) {
-            const int m = p.step_counts[static_cast<int64_t>(e) * p.max_T + t];
+            const int m = step_counts[static_cast<int64_t>(e) * p.max_T + t];
             const int64_t src = d.sparse_offset + static_cast<int64_t>(t) * (K + P);
             const int64_t dst = d.sparse_offset + off;
             if (dst != src) {
@@ -1588,6 +1591,12 @@ __global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max
         }
         if (tid == 0) p.sparse_counts[e] = off;
     }
+}
+
+__global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max_P) {
+    const int e = blockIdx.x;
+    const ExampleDesc d = p.desc[e];
+    backward_example(p, d, e, p.inv_pen, p.step_counts, sparse, max_K, max_P);
 }
 
 // ---------------------------------------------------------------------------
@@ -1984,6 +1993,12 @@ static size_t backward_sweep_smem(int max_T, int max_K, int max_P, bool with_poo
 }
 constexpr size_t kBackwardSweepSmemBudget = 96 * 1024;
 
+static size_t backward_smem_bytes(int max_K, int max_P) {
+    return static_cast<size_t>(max_K) * 3 * sizeof(float) + static_cast<size_t>(max_P) * sizeof(float) +
+           static_cast<size_t>(max_K + max_P) * sizeof(int) + 16 +
+           static_cast<size_t>(max_K + max_P) * (sizeof(int64_t) + sizeof(float));
+}
+
 cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool sparse, cudaStream_t stream) {
     if (!sparse && max_K <= 32 && p.grad_dense) {
         const bool with_pool = p.grad_relaxed != nullptr;
@@ -1995,9 +2010,7 @@ cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool 
             return cudaGetLastError();
         }
     }
-    const size_t smem = static_cast<size_t>(max_K) * 3 * sizeof(float) + static_cast<size_t>(max_P) * sizeof(float) +
-                        static_cast<size_t>(max_K + max_P) * sizeof(int) + 16 +
-                        static_cast<size_t>(max_K + max_P) * (sizeof(int64_t) + sizeof(float));
+    const size_t smem = backward_smem_bytes(max_K, max_P);
     cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(backward_kernel), smem);
     if (err != cudaSuccess) return err;
     int threads = 128;
@@ -2076,6 +2089,100 @@ cudaError_t launch_widen_16(const uint16_t* src, float* dst, int64_t count, int 
     cudaError_t err = prefer_shared(reinterpret_cast<const void*>(widen_16_kernel));
     if (err != cudaSuccess) return err;
     widen_16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, count, is_bf16);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Sparse backward that allocates nothing (dbs_device_backward_sparse_noalloc).
+//
+// Callers that may not allocate device memory on their call path (code that
+// runs while a framework's caching allocator owns the device, inside a
+// capture or replay region it manages, or in a real-time loop where
+// cudaMalloc's implicit synchronisation is not acceptable) still need the
+// sparse backward. Its only scratch, the per-(example, step) entry counts
+// used to compact the sparse segments, lives in the file-scope array below;
+// the example descriptors of the uniform batch are computed in the kernel and
+// the 1/gnmt table travels in the kernel parameters. Every scratch slot is
+// written before it is read, so nothing has to start at zero.
+//
+// Limits: batch_size * steps <= kNoAllocMaxStepCounts (1 MiB of scratch),
+// steps <= kNoAllocMaxSteps (the parameter table), beam + pool <= 4096.
+// There is one scratch array per device, so calls on one device must not
+// overlap in time (on different streams they would race on it); calls in a
+// row on one stream are ordered and safe.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) int32_t g_noalloc_step_counts[kNoAllocMaxStepCounts];
+
+struct NoAllocPenalty {
+    float inv_pen[kNoAllocMaxSteps + 2];   // 1 / gnmt(l), l = 0 .. steps + 1
+};
+
+__global__ void backward_noalloc_kernel(BackwardParams p, int T, int K, int P, NoAllocPenalty tab,
+                                        int32_t* scratch) {
+    const int e = blockIdx.x;
+    ExampleDesc d{};
+    d.T = T;
+    d.K = K;
+    d.P = P;
+    d.sel_offset = static_cast<int64_t>(e) * T * K;
+    d.pool_offset = static_cast<int64_t>(e) * T * P;
+    d.final_offset = static_cast<int64_t>(e) * K;
+    d.sparse_offset = static_cast<int64_t>(e) * T * (K + P);
+    d.sel_stride = K;
+    d.pool_stride = P;
+    d.sel_t_stride = K;
+    d.pool_t_stride = P;
+    backward_example(p, d, e, tab.inv_pen, scratch, 1, K, P);
+}
+
+// Scratch address per device, looked up once with that device current.
+static std::mutex g_noalloc_mu;
+static std::vector<int32_t*> g_noalloc_ptr;
+
+static cudaError_t noalloc_scratch(int32_t** out) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (dev >= static_cast<int>(g_noalloc_ptr.size())) g_noalloc_ptr.resize(dev + 1, nullptr);
+    if (!g_noalloc_ptr[dev]) {
+        void* ptr = nullptr;
+        err = cudaGetSymbolAddress(&ptr, g_noalloc_step_counts);
+        if (err != cudaSuccess) return err;
+        g_noalloc_ptr[dev] = static_cast<int32_t*>(ptr);
+    }
+    *out = g_noalloc_ptr[dev];
+    return cudaSuccess;
+}
+
+cudaError_t noalloc_prepare() {
+    int32_t* ptr = nullptr;
+    cudaError_t err = noalloc_scratch(&ptr);
+    if (err != cudaSuccess) return err;
+    return ensure_dynamic_smem(reinterpret_cast<const void*>(backward_noalloc_kernel),
+                               backward_smem_bytes(kNoAllocMaxBeamPlusPool, 0));
+}
+
+cudaError_t launch_backward_noalloc(const BackwardParams& p, int T, int K, int P, const float* inv_pen_host,
+                                    cudaStream_t stream) {
+    if (T < 1 || T > kNoAllocMaxSteps || K < 1 || P < K || K + P > kNoAllocMaxBeamPlusPool ||
+        static_cast<int64_t>(p.B) * T > kNoAllocMaxStepCounts)
+        return cudaErrorInvalidValue;
+    int32_t* scratch = nullptr;
+    cudaError_t err = noalloc_prepare();
+    if (err != cudaSuccess) return err;
+    err = noalloc_scratch(&scratch);
+    if (err != cudaSuccess) return err;
+    NoAllocPenalty tab{};
+    for (int l = 0; l < T + 2; ++l) tab.inv_pen[l] = inv_pen_host[l];
+    BackwardParams q = p;
+    q.desc = nullptr;
+    q.inv_pen = nullptr;
+    q.step_counts = scratch;
+    q.max_T = T;
+    const size_t smem = backward_smem_bytes(K, P);
+    const int threads = P > 512 ? 256 : 128;
+    backward_noalloc_kernel<<<p.B, threads, smem, stream>>>(q, T, K, P, tab, scratch);
     return cudaGetLastError();
 }
 

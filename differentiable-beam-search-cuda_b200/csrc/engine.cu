@@ -44,18 +44,21 @@ int device_sm_count() {
 // gnmt_length_penalty (src/differentiable_beam.cpp:277-282), evaluated on the
 // host with the same float powf as the reference, plus its reciprocal
 // 1.0f / pen as used by the scan and the backward.
+static float gnmt_host(float alpha, int l) {
+    if (alpha == 0.0f) return 1.0f;
+    const int ll = l < 1 ? 1 : l;
+    return std::pow((5.0f + static_cast<float>(ll)) / 6.0f, alpha);
+}
+static float reciprocal_host(float v) {
+    volatile float one = 1.0f;
+    return one / v;
+}
 static void penalty_tables(float alpha, int lmax, std::vector<float>& pen, std::vector<float>& inv) {
     pen.resize(lmax + 1);
     inv.resize(lmax + 1);
     for (int l = 0; l <= lmax; ++l) {
-        float v = 1.0f;
-        if (alpha != 0.0f) {
-            const int ll = l < 1 ? 1 : l;
-            v = std::pow((5.0f + static_cast<float>(ll)) / 6.0f, alpha);
-        }
-        pen[l] = v;
-        volatile float one = 1.0f;
-        inv[l] = one / v;
+        pen[l] = gnmt_host(alpha, l);
+        inv[l] = reciprocal_host(pen[l]);
     }
 }
 
@@ -689,6 +692,47 @@ void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, con
     ProfileScope ps(kBackward, stream);
     check_cuda(dbs_dev::launch_backward(p, max_K, max_P, sparse, stream), "backward kernel");
     trace.mark("queued");
+}
+
+void backward_sparse_noalloc(const Options& opt, int V, int B, int T, const BackwardInputs& in,
+                             const BackwardOutputs& out, cudaStream_t stream) {
+    const int K = opt.beam_size;
+    const int P = std::max(K, K * opt.relaxed_pool_multiplier);
+    if (T > dbs_dev::kNoAllocMaxSteps)
+        throw LengthError("the allocation-free backward takes at most " + std::to_string(dbs_dev::kNoAllocMaxSteps) +
+                          " steps");
+    if (static_cast<int64_t>(B) * T > dbs_dev::kNoAllocMaxStepCounts)
+        throw LengthError("the allocation-free backward takes at most " +
+                          std::to_string(dbs_dev::kNoAllocMaxStepCounts) + " batch_size * steps (its static scratch)");
+    if (K + P > dbs_dev::kNoAllocMaxBeamPlusPool)
+        throw LengthError("the allocation-free backward takes at most " +
+                          std::to_string(dbs_dev::kNoAllocMaxBeamPlusPool) + " beam + pool entries per step");
+    float inv[dbs_dev::kNoAllocMaxSteps + 2];
+    for (int l = 0; l < T + 2; ++l) inv[l] = reciprocal_host(gnmt_host(opt.length_penalty_alpha, l));
+    dbs_dev::BackwardParams p{};
+    p.V = V;
+    p.B = B;
+    p.Lmax = T + 1;
+    p.selected_temperature = opt.selected_temperature;
+    p.soft_topk_temperature = opt.soft_topk_temperature;
+    p.parents = in.parents;
+    p.tokens = in.tokens;
+    p.lengths = in.lengths;
+    p.weights = in.weights;
+    p.from_logprob = in.from_logprob;
+    p.pool_parents = in.pool_parents;
+    p.pool_tokens = in.pool_tokens;
+    p.pool_lengths = in.pool_lengths;
+    p.relaxed_weights = in.relaxed_weights;
+    p.pool_from_logprob = in.pool_from_logprob;
+    p.grad_selected = in.grad_selected;
+    p.grad_relaxed = in.grad_relaxed;
+    p.grad_final = in.grad_final;
+    p.sparse_indices = out.sparse_indices;
+    p.sparse_values = out.sparse_values;
+    p.sparse_counts = out.sparse_counts;
+    p.grad_initial = out.grad_initial;
+    check_cuda(dbs_dev::launch_backward_noalloc(p, T, K, P, inv, stream), "allocation-free backward kernel");
 }
 
 }  // namespace dbs_host

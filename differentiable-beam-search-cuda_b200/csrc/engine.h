@@ -160,6 +160,13 @@ void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, con
               const BackwardInputs& in, const BackwardOutputs& out, cudaStream_t stream,
               bool zero_dense = true);
 
+// Sparse backward of a uniform batch (every example has T steps and the
+// options' beam size) that allocates no device or pinned memory: its scratch
+// is a static device array (one per device, so calls on one device must not
+// overlap). Throws LengthError beyond the scratch limits.
+void backward_sparse_noalloc(const Options& opt, int V, int B, int T, const BackwardInputs& in,
+                             const BackwardOutputs& out, cudaStream_t stream);
+
 int device_sm_count();
 
 // Live kernel timing: every launch of a kernel whose bit is set in the mask is

@@ -202,6 +202,8 @@ DEVICE_FUNCTIONS = {
     "dbs_device_profile": (_I, [_I]),
     "dbs_device_profile_read": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_I64)]),
     "dbs_device_profile_kernels": (_I, [ctypes.c_uint]),
+    "dbs_device_backward_sparse_noalloc": (
+        _I, [_VP, _I, _I, _I, ctypes.POINTER(DBSDeviceDecodeOutputs), _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
 }
 
 PROFILED_KERNELS = ("validate", "row_scan", "step_merge", "weights", "fill_zero", "backward")

@@ -112,6 +112,27 @@ DBS_EXPORT int dbs_device_backward_batch_ex(DBSDecoderHandle* handle, int batch_
                                             int64_t* sparse_counts, float* grad_initial_scores, int flags,
                                             void* cuda_stream);
 
+/* Sparse backward of a uniform batch that allocates nothing on its call path:
+ * same arguments, outputs and results as dbs_device_backward_batch with
+ * sparse outputs (grad_log_probs NULL). For callers that must not allocate
+ * device memory where they call it (a caching allocator owns the device, a
+ * capture or replay region, a latency-critical loop where cudaMalloc's
+ * implicit synchronisation is unacceptable). Its scratch is a static device
+ * array of 1 MiB per device, which limits it to batch_size * steps <= 262144,
+ * steps <= 510 and beam + pool <= 4096 (-2 with a "takes at most" message
+ * beyond them). The first call on a device looks the scratch up and loads
+ * the module, so make one call before any region that forbids that. The
+ * scratch is shared by all calls on a device: calls must not overlap in time
+ * (two streams would race); calls in a row on one stream are fine. No
+ * counterpart in the reference, whose backward allocates host memory. */
+DBS_EXPORT int dbs_device_backward_sparse_noalloc(DBSDecoderHandle* handle, int batch_size, int steps,
+                                                  int vocab_size, const DBSDeviceDecodeOutputs* trace,
+                                                  const float* grad_selected_weights,
+                                                  const float* grad_relaxed_weights,
+                                                  const float* grad_final_scores, int64_t* sparse_indices,
+                                                  float* sparse_values, int64_t* sparse_counts,
+                                                  float* grad_initial_scores, void* cuda_stream);
+
 /* Diagnostics of the most recent device decode whose counters have been read
  * back (process-wide): rows rescanned by the row scan (always 0: the scan is
  * exact in one pass) and rows the step merge could not prove complete and
