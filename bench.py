@@ -113,6 +113,11 @@ class ClockSampler:
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        # nvidia-smi's start-up contends with this process's CUDA calls: let it
+        # deliver its first sample before the timed region begins
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 10.0 and self.proc.poll() is None:
+            time.sleep(0.05)
 
     def _read(self):
         for line in self.proc.stdout:
