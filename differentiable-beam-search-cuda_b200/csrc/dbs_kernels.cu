@@ -1874,8 +1874,11 @@ cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-// per-warp survivor buffer: C kept + 8 + one 128-value group of appends + head/tail
-static int row_scan_capw(int max_C) { return max_C + 128 + 24; }
+// Per-warp survivor buffer: C kept + max(C, 16) appended between compactions +
+// one 128-value group of appends + 8. A compaction sorts the buffer, so for
+// large C it runs once per C survivors (a few times per row) rather than once
+// per 16.
+static int row_scan_capw(int max_C) { return max_C + (max_C > 16 ? max_C : 16) + 128 + 8; }
 
 static size_t row_scan_smem(int capw) {
     const size_t warp_bytes = static_cast<size_t>(kScanStages) * kScanChunkF4 * 16 + kScanStages * sizeof(uint64_t) +
@@ -1925,7 +1928,7 @@ static size_t merge_rank_smem(int ring, int max_K, int max_C, int max_N, int tab
 }
 
 // Shared memory the ranking merge may take; beyond it the sort merge runs.
-constexpr size_t kMergeRankSmemBudget = 160 * 1024;
+constexpr size_t kMergeRankSmemBudget = 200 * 1024;
 
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T, int max_N,
                               bool need_sequences, cudaStream_t stream) {

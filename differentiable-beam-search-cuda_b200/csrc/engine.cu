@@ -409,11 +409,15 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         const int N = pool ? P : e.K;
         int slack = 0;
         if (dynamic) slack = 8 + N / 8;
-        const int C = N + slack;
-        if (static_cast<int64_t>(e.K) * C > dbs_dev::kMaxMergeCandidates) {
-            throw LengthError("beam_size * relaxed pool exceeds the per-step merge capacity of " +
-                              std::to_string(dbs_dev::kMaxMergeCandidates) + " candidates");
-        }
+        // Row list capacity. A row can contribute at most N candidates, so
+        // C = N (+ slack for the penalty / n-gram masks) never needs the
+        // merge's rescan path; when K * (N + slack) exceeds the merge's
+        // per-step candidate capacity the lists are cut to the capacity and
+        // the merge proves per step that nothing dropped could have entered
+        // (rescanning the row from HBM otherwise), which stays exact.
+        int C = N + slack;
+        if (static_cast<int64_t>(e.K) * C > dbs_dev::kMaxMergeCandidates)
+            C = std::max(1, dbs_dev::kMaxMergeCandidates / e.K);
         if (e.K > 1024) throw LengthError("beam_size above 1024 is not supported by the device decoder");
         dbs_dev::ExampleDesc& d = desc[b];
         d.x_offset = e.x_offset;

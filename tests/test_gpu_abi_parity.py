@@ -142,6 +142,36 @@ def test_large_pool(libdbs, oracle_lib):
     assert_decode_equal(got, want, "K=32")
 
 
+@pytest.mark.parametrize("K,T,V,mult,alpha", [
+    (64, 4, 3000, 8, 0.0),      # P = 512: row lists cut to 128 entries
+    (128, 3, 2000, 8, 0.3),     # P = 1024: row lists cut to 64 entries
+    (96, 3, 1500, 2, 0.0),      # P = 192, K*P above the per-step capacity
+])
+def test_beam_times_pool_above_merge_capacity(libdbs, oracle_lib, K, T, V, mult, alpha):
+    # K * P exceeds the merge's per-step candidate capacity, so the row lists
+    # are shorter than P and the merge must prove (or rescan) every step;
+    # at t = 0 the single live parent always needs its row rescanned.
+    rng = np.random.default_rng(K * 7 + V)
+    bias = -1.1 * np.log(np.arange(V, dtype=np.float32) + 1.0)
+    x = log_softmax_np(1.5 * rng.standard_normal((T, K, V)).astype(np.float32) + bias)
+    opts = dict(beam_size=K, relaxed_pool_multiplier=mult, length_penalty_alpha=alpha, eos_token=2)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, {})
+    got = _product_decode(libdbs, opts, x, T, V, {})
+    assert_decode_equal(got, want, f"K={K} P={want['P']}")
+
+
+def test_large_beam_with_constraints(libdbs, oracle_lib):
+    rng = np.random.default_rng(77)
+    T, K, V = 4, 64, 1200
+    x = log_softmax_np(1.5 * rng.standard_normal((T, K, V)).astype(np.float32))
+    banned = (rng.random(V) < 0.05).astype(np.uint8)
+    opts = dict(beam_size=K, relaxed_pool_multiplier=4, eos_token=2, min_length=2)
+    cons = dict(banned=banned, repetition_penalty=1.3, no_repeat_ngram_size=2)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, cons)
+    got = _product_decode(libdbs, opts, x, T, V, cons)
+    assert_decode_equal(got, want, "K=64 constrained")
+
+
 def test_dense_ties_force_the_rescan_path(libdbs, oracle_lib):
     # every row is constant: every list boundary is an exact tie, so the step
     # merge has to rescan rows to prove the token order

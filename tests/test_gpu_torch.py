@@ -36,6 +36,8 @@ OPTION_SETS = [
          vocab_block=7, length_penalty_alpha=0.35, soft_topk_tolerance=1e-5, soft_topk_max_iters=64, min_length=2),
     dict(beam_size=8, eos_token=2, length_penalty_alpha=0.2, selected_temperature=0.7),
     dict(beam_size=33),
+    # K*K above the merge's per-step capacity: row lists are cut to 64
+    dict(beam_size=128, eos_token=2, length_penalty_alpha=0.3),
 ]
 
 
