@@ -106,7 +106,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", self.uuid, f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", "-i", self.uuid, f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -114,9 +114,9 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
         # nvidia-smi's start-up contends with this process's CUDA calls: let it
-        # deliver its first sample before the timed region begins
+        # settle (three samples delivered) before the timed region begins
         t0 = time.time()
-        while not self.lines and time.time() - t0 < 10.0 and self.proc.poll() is None:
+        while len(self.lines) < 3 and time.time() - t0 < 10.0 and self.proc.poll() is None:
             time.sleep(0.05)
 
     def _read(self):

@@ -153,6 +153,133 @@ __device__ __forceinline__ int find_example(const int64_t* prefix, int B, int64_
     return lo;
 }
 
+// Moves the n_top largest (hi, lo) keys of hi/lo[0..m) to the front, sorted
+// descending; the rest of the arrays is left in an unspecified order. A
+// radix select over the 64-bit hi keys (8 bits per pass, most significant
+// first) narrows the keys that can be among the n_top until at most
+// `tmp_cap` of them remain; those are gathered into tmp_hi/tmp_lo, sorted and
+// copied back. Keys tied on hi beyond that capacity fall back to a full sort.
+// Must be called by all threads of the block; ends with a barrier.
+__device__ __noinline__ void block_top_n_u128(uint64_t* hi, uint64_t* lo, int m, int n_top, uint64_t* tmp_hi, uint64_t* tmp_lo,
+                                 int tmp_cap) {
+    __shared__ int hist[256];
+    __shared__ int sh_sel[3];   // chosen digit, keys above the group, keys in the group
+    __shared__ int sh_n;
+    if (n_top >= m) {
+        block_sort_desc_u128(hi, lo, m);
+        return;
+    }
+    // Key 0 marks an empty candidate slot. With at most n_top real keys the
+    // answer is all of them, sorted, followed by empty slots.
+    if (threadIdx.x == 0) sh_n = 0;
+    __syncthreads();
+    {
+        int c = 0;
+        for (int i = threadIdx.x; i < m; i += blockDim.x) c += hi[i] != 0;
+        if (c) atomicAdd(&sh_n, c);
+    }
+    __syncthreads();
+    const int real = sh_n;
+    __syncthreads();
+    if (real <= n_top && real <= tmp_cap) {
+        if (threadIdx.x == 0) sh_n = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < m; i += blockDim.x) {
+            if (hi[i] != 0) {
+                const int pos = atomicAdd(&sh_n, 1);
+                tmp_hi[pos] = hi[i];
+                tmp_lo[pos] = lo[i];
+            }
+        }
+        __syncthreads();
+        block_sort_desc_u128(tmp_hi, tmp_lo, real);
+        for (int i = threadIdx.x; i < n_top; i += blockDim.x) {
+            hi[i] = i < real ? tmp_hi[i] : 0;
+            lo[i] = i < real ? tmp_lo[i] : 0;
+        }
+        __syncthreads();
+        return;
+    }
+    // aim for a small final sort: at most max(2 n_top, 256) keys
+    int target = 2 * n_top < 256 ? 256 : 2 * n_top;
+    if (target > tmp_cap) target = tmp_cap;
+    uint64_t prefix = 0, mask = 0;
+    int need = n_top;
+    int above = 0, group = m;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < m; i += blockDim.x) {
+            const uint64_t k = hi[i];
+            if ((k & mask) == prefix) atomicAdd(&hist[static_cast<int>((k >> shift) & 0xFFu)], 1);
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            // digit d* with sum_{d > d*} < need <= sum_{d >= d*}: suffix sums
+            // over 8 digits per lane, then across lanes from the top
+            const int lane = threadIdx.x;
+            int loc[8];
+            int tot = 0;
+#pragma unroll
+            for (int j = 7; j >= 0; --j) {
+                loc[j] = hist[lane * 8 + j];
+                tot += loc[j];
+            }
+            int incl = tot;   // inclusive suffix sum over lanes >= lane
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_down_sync(0xFFFFFFFFu, incl, o);
+                if (lane + o < 32) incl += v;
+            }
+            const int excl = incl - tot;   // keys in digits of higher lanes
+            if (excl < need && need <= incl) {
+                int run = excl;
+                for (int j = 7; j >= 0; --j) {
+                    if (run + loc[j] >= need) {
+                        sh_sel[0] = lane * 8 + j;
+                        sh_sel[1] = run;
+                        sh_sel[2] = loc[j];
+                        break;
+                    }
+                    run += loc[j];
+                }
+            }
+        }
+        __syncthreads();
+        const int d = sh_sel[0];
+        above += sh_sel[1];
+        need -= sh_sel[1];
+        group = sh_sel[2];
+        prefix |= static_cast<uint64_t>(d) << shift;
+        mask |= static_cast<uint64_t>(0xFFu) << shift;
+        __syncthreads();   // sh_sel is rewritten by the next pass
+        if (above + group <= target) break;
+    }
+    if (above + group > tmp_cap) {   // massive ties on hi: sort everything
+        block_sort_desc_u128(hi, lo, m);
+        return;
+    }
+    // gather every key whose masked prefix is >= the chosen one
+    if (threadIdx.x == 0) sh_n = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+        const uint64_t k = hi[i];
+        if ((k & mask) >= prefix) {
+            const int pos = atomicAdd(&sh_n, 1);
+            tmp_hi[pos] = k;
+            tmp_lo[pos] = lo[i];
+        }
+    }
+    __syncthreads();
+    const int g = sh_n;
+    block_sort_desc_u128(tmp_hi, tmp_lo, g);
+    for (int i = threadIdx.x; i < n_top; i += blockDim.x) {
+        hi[i] = tmp_hi[i];
+        lo[i] = tmp_lo[i];
+    }
+    __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // 0. Sampled input validation (validate_logprob_tensor,
 //    src/differentiable_beam.cpp:385-402): indices 0, s, 2s, ... of the
@@ -205,6 +332,9 @@ __global__ void validate_kernel(DecodeParams p) {
 constexpr int kScanStages = 4;
 constexpr int kScanChunkF4 = 128;       // 2 KB per chunk: 4 float4 per lane
 constexpr int kScanWarpsPerCta = 4;
+// Lists longer than 32 entries (buffer capacity above 2*32 + 136) compact by
+// radix selection, which needs a 256-bin histogram per warp.
+__host__ __device__ constexpr int row_scan_hist_ints(int capw) { return capw > 2 * 32 + 136 ? 256 : 0; }
 
 __device__ __forceinline__ void warp_sort_desc_u64(uint64_t* a, int n, int lane) {
     if (n <= 1) { __syncwarp(); return; }
@@ -296,6 +426,81 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     return false;
 }
 
+// Lists longer than 32 entries: shrink a warp's survivor buffer to the
+// entries whose lp is at least the C-th largest lp in it (at least C entries;
+// more only when that lp value repeats), keeping token order. The C-th
+// largest comes from a radix select over ord(lp) (8 bits per pass, 256-bin
+// histogram per warp), so a compaction costs a few passes over the buffer
+// instead of a sort. Afterwards only lp strictly above that value can enter
+// (a later element with the same lp has a larger token and loses the tie),
+// and `evict` holds the largest lp dropped. Called by all lanes of the warp.
+__device__ __noinline__ int warp_compact_select(uint64_t* buf, int cnt, int C, int lane, int* hist, float& thr, float& evict) {
+    constexpr unsigned FULL = 0xFFFFFFFFu;
+    uint32_t prefix = 0, mask = 0;
+    int need = C;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = lane; i < 256; i += 32) hist[i] = 0;
+        __syncwarp();
+        for (int i = lane; i < cnt; i += 32) {
+            const uint32_t u = static_cast<uint32_t>(buf[i] >> 32);
+            if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 0xFFu], 1);
+        }
+        __syncwarp();
+        int loc[8];
+        int tot = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            loc[j] = hist[lane * 8 + j];
+            tot += loc[j];
+        }
+        int incl = tot;   // keys in digits of lanes >= this lane
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_down_sync(FULL, incl, o);
+            if (lane + o < 32) incl += v;
+        }
+        const int excl = incl - tot;
+        int digit = -1, skipped = 0;
+        if (excl < need && need <= incl) {
+            int run = excl;
+            for (int j = 7; j >= 0; --j) {
+                if (run + loc[j] >= need) {
+                    digit = lane * 8 + j;
+                    skipped = run;
+                    break;
+                }
+                run += loc[j];
+            }
+        }
+        const unsigned owner = __ballot_sync(FULL, digit >= 0);
+        const int src = __ffs(owner) - 1;
+        digit = __shfl_sync(FULL, digit, src);
+        skipped = __shfl_sync(FULL, skipped, src);
+        need -= skipped;
+        prefix |= static_cast<uint32_t>(digit) << shift;
+        mask |= 0xFFu << shift;
+        __syncwarp();
+    }
+    // in-place, order-preserving compaction of the entries with ord(lp) >= prefix
+    const unsigned lt = (1u << lane) - 1u;
+    float dropped = -INFINITY;
+    int w = 0;
+    for (int base = 0; base < cnt; base += 32) {
+        const int i = base + lane;
+        const uint64_t k = i < cnt ? buf[i] : 0;
+        const bool keep = i < cnt && static_cast<uint32_t>(k >> 32) >= prefix;
+        if (i < cnt && !keep) dropped = fmaxf(dropped, list_lp(k));
+        const unsigned b = __ballot_sync(FULL, keep);
+        __syncwarp();
+        if (keep) buf[w + __popc(b & lt)] = k;
+        w += __popc(b);
+        __syncwarp();
+    }
+    evict = fmaxf(evict, warp_max(dropped));
+    thr = fmaxf(thr, nextafterf(unord_f32(prefix), INFINITY));
+    return w;
+}
+
 struct RowJob {
     const float* row;
     int64_t r;
@@ -334,17 +539,20 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     return j;
 }
 
-__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 1) row_scan_kernel(DecodeParams p, int capw) {
+__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 5) row_scan_kernel(DecodeParams p, int capw) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     constexpr unsigned FULL = 0xFFFFFFFFu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // per-warp region: ring | barriers | survivor buffer
     const size_t ring_bytes = static_cast<size_t>(kScanStages) * kScanChunkF4 * 16;
-    const size_t warp_bytes = ring_bytes + kScanStages * sizeof(uint64_t) + static_cast<size_t>(capw) * sizeof(uint64_t);
+    const int hist_ints = row_scan_hist_ints(capw);
+    const size_t warp_bytes = ring_bytes + kScanStages * sizeof(uint64_t) + static_cast<size_t>(capw) * sizeof(uint64_t) +
+                              static_cast<size_t>(hist_ints) * sizeof(int);
     unsigned char* base = smem_raw + warp * ((warp_bytes + 127) & ~static_cast<size_t>(127));
     float4* ring = reinterpret_cast<float4*>(base);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + ring_bytes);
     uint64_t* buf = full + kScanStages;
+    int* hist = reinterpret_cast<int*>(buf + capw);
     unsigned long long* err = p.counters ? p.counters + 3 : nullptr;
     unsigned long long* next_row = p.counters + 2;
     const unsigned lt_mask = (1u << lane) - 1u;
@@ -443,6 +651,11 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 1) row_scan_kernel(Deco
             };
             auto compact = [&]() {
                 __syncwarp();
+                if (C > 32 && hist_ints) {
+                    cnt = warp_compact_select(buf, cnt, C, lane, hist, thr, evict);
+                    if (cnt <= capw - 128 - 8 - 32) return;
+                    // the C-th lp value repeats too often to free room: cut exactly
+                }
                 warp_sort_desc_u64(buf, cnt, lane);
                 if (cnt > C) {
                     evict = fmaxf(evict, list_lp(buf[C]));
@@ -519,6 +732,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 1) row_scan_kernel(Deco
                 consider(in, t0 + lane, lp);
             }
             __syncwarp();
+            // long lists: cut to about C before the one full sort of the row
+            if (C > 32 && hist_ints && cnt > C + 32) cnt = warp_compact_select(buf, cnt, C, lane, hist, thr, evict);
             warp_sort_desc_u64(buf, cnt, lane);
             const int keep = cnt < C ? cnt : C;
             for (int i = lane; i < keep; i += 32) out[i] = buf[i];
@@ -609,8 +824,8 @@ __device__ __forceinline__ bool in_list(const int32_t* a, int n, int v) {
     return false;
 }
 
-__global__ void __launch_bounds__(kMergeThreads) step_merge_kernel(DecodeParams p, int cand_cap,
-                                                                   int seq_T, int seq_K) {
+__global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodeParams p, int cand_cap,
+                                                                   int seq_T, int seq_K, int sel_cap) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     const ExampleDesc d = p.desc[e];
@@ -634,6 +849,10 @@ __global__ void __launch_bounds__(kMergeThreads) step_merge_kernel(DecodeParams 
     s.row_cnt = s.ended_next + K;
     s.unsafe = s.row_cnt + K;
     s.blocked_n = s.unsafe + K;
+    // selection scratch after the per-beam arrays (sized by the call's largest K)
+    uint64_t* sel_hi = reinterpret_cast<uint64_t*>(
+        (reinterpret_cast<uintptr_t>(f_base + 3 * seq_K + 7 * seq_K) + 15) & ~static_cast<uintptr_t>(15));
+    uint64_t* sel_lo = sel_hi + sel_cap;
     __shared__ int sh_any_unsafe;
     __shared__ int sh_stage;
 
@@ -723,7 +942,8 @@ __global__ void __launch_bounds__(kMergeThreads) step_merge_kernel(DecodeParams 
             clo[idx] = l;
         }
         __syncthreads();
-        block_sort_desc_u128(chi, clo, M);
+        if (M > 1024) block_top_n_u128(chi, clo, M, N, sel_hi, sel_lo, sel_cap);
+        else block_sort_desc_u128(chi, clo, M);
 
         // Exactness proof per truncated row: every entry the scan dropped has
         // lp <= bound, so its candidate is at most U = (rank(bound),
@@ -1882,7 +2102,8 @@ static int row_scan_capw(int max_C) { return max_C + (max_C > 16 ? max_C : 16) +
 
 static size_t row_scan_smem(int capw) {
     const size_t warp_bytes = static_cast<size_t>(kScanStages) * kScanChunkF4 * 16 + kScanStages * sizeof(uint64_t) +
-                              static_cast<size_t>(capw) * sizeof(uint64_t);
+                              static_cast<size_t>(capw) * sizeof(uint64_t) +
+                              static_cast<size_t>(row_scan_hist_ints(capw)) * sizeof(int);
     return static_cast<size_t>(kScanWarpsPerCta) * ((warp_bytes + 127) & ~static_cast<size_t>(127));
 }
 
@@ -1932,7 +2153,7 @@ constexpr size_t kMergeRankSmemBudget = 200 * 1024;
 
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T, int max_N,
                               bool need_sequences, cudaStream_t stream) {
-    if (!need_sequences && max_K <= 128) {
+    if (!need_sequences && static_cast<int64_t>(max_K) * max_C <= 1024) {
         const int tab_n = (p.Lmax + 1 <= 4096) ? p.Lmax + 1 : 0;
         int ring = max_T < kMergeRingMax ? max_T : kMergeRingMax;
         if (ring < 2) ring = 2;
@@ -1957,15 +2178,17 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     const int M = max_K * max_C;
     int cand_cap = M;
     if (cand_cap < max_N + 2048) cand_cap = max_N + 2048;
+    const int sel_cap = max_N + 2048;
     const size_t smem = static_cast<size_t>(cand_cap) * 2 * sizeof(uint64_t) +
                         static_cast<size_t>(max_K) * 3 * sizeof(float) +
-                        static_cast<size_t>(max_K) * 7 * sizeof(int) + 64;
+                        static_cast<size_t>(max_K) * 7 * sizeof(int) + 64 +
+                        16 + static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t);
     int threads = 64;
     while (threads < kMergeThreads && threads * 2 <= (M + 1) / 2) threads <<= 1;
     if (threads < 128 && max_K > 64) threads = 128;
     cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(step_merge_kernel), smem);
     if (err != cudaSuccess) return err;
-    step_merge_kernel<<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K);
+    step_merge_kernel<<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap);
     return cudaGetLastError();
 }
 

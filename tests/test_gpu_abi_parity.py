@@ -160,6 +160,19 @@ def test_beam_times_pool_above_merge_capacity(libdbs, oracle_lib, K, T, V, mult,
     assert_decode_equal(got, want, f"K={K} P={want['P']}")
 
 
+def test_massive_ties_with_large_beam(libdbs, oracle_lib):
+    # constant rows: thousands of candidates share one key prefix, so the
+    # merge's radix selection cannot narrow them and sorts them all
+    T, K, V = 3, 64, 400
+    x = np.full((T, K, V), -2.0, dtype=np.float32)
+    x[:, :, 5] = -1.0
+    x[1, 7, 100:180] = -1.5
+    opts = dict(beam_size=K, relaxed_pool_multiplier=8)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, {})
+    got = _product_decode(libdbs, opts, x, T, V, {})
+    assert_decode_equal(got, want, "ties K=64")
+
+
 def test_large_beam_with_constraints(libdbs, oracle_lib):
     rng = np.random.default_rng(77)
     T, K, V = 4, 64, 1200
