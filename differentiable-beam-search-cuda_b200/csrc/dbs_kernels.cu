@@ -436,14 +436,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
 // and `evict` holds the largest lp dropped. Called by all lanes of the warp.
 __device__ __noinline__ int warp_compact_select(uint64_t* buf, int cnt, int C, int lane, int* hist, float& thr, float& evict) {
     constexpr unsigned FULL = 0xFFFFFFFFu;
-    uint32_t prefix = 0, mask = 0;
+    // The keys share their leading bits (similar lp values): start the radix
+    // passes at the highest bit where the smallest and largest key differ.
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0;
+    for (int i = lane; i < cnt; i += 32) {
+        const uint32_t u = static_cast<uint32_t>(buf[i] >> 32);
+        kmin = min(kmin, u);
+        kmax = max(kmax, u);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(FULL, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(FULL, kmax, o));
+    }
+    const int top_bit = (kmin == kmax) ? 0 : 31 - __clz(kmin ^ kmax);
+    int shift = top_bit >= 8 ? top_bit - 7 : 0;   // digit = bits [shift, shift + 8)
+    uint32_t mask = shift + 8 >= 32 ? 0u : ~((1u << (shift + 8)) - 1u);   // bits above the digit
+    uint32_t prefix = kmax & mask;   // shared by every key
     int need = C;
-    for (int shift = 24; shift >= 0; shift -= 8) {
+    for (;;) {
         for (int i = lane; i < 256; i += 32) hist[i] = 0;
         __syncwarp();
         for (int i = lane; i < cnt; i += 32) {
             const uint32_t u = static_cast<uint32_t>(buf[i] >> 32);
-            if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 0xFFu], 1);
+            const bool in = (u & mask) == prefix;
+            const int bin = in ? static_cast<int>((u >> shift) & 0xFFu) : -1;
+            // lanes with the same bin add once (the leading bits repeat a lot)
+            const unsigned act = __activemask();
+            const unsigned same = __match_any_sync(act, bin);
+            if (in && lane == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
         }
         __syncwarp();
         int loc[8];
@@ -480,6 +501,10 @@ __device__ __noinline__ int warp_compact_select(uint64_t* buf, int cnt, int C, i
         prefix |= static_cast<uint32_t>(digit) << shift;
         mask |= 0xFFu << shift;
         __syncwarp();
+        if (shift == 0) break;
+        // the last digit may overlap bits already decided: they match the
+        // prefix for every key in the group, so the pass stays consistent
+        shift = shift >= 8 ? shift - 8 : 0;
     }
     // in-place, order-preserving compaction of the entries with ord(lp) >= prefix
     const unsigned lt = (1u << lane) - 1u;
@@ -539,7 +564,7 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     return j;
 }
 
-__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 5) row_scan_kernel(DecodeParams p, int capw) {
+__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(DecodeParams p, int capw) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     constexpr unsigned FULL = 0xFFFFFFFFu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -716,6 +741,12 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 5) row_scan_kernel(Deco
                 } else {
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
+                        // a 128-value group without a survivor only feeds the bound
+                        const float m4 = fmaxf(fmaxf(q[u].x, q[u].y), fmaxf(q[u].z, q[u].w));
+                        if (!__any_sync(FULL, m4 >= thr)) {
+                            rej = fmaxf(rej, m4);
+                            continue;
+                        }
                         const int v0 = tok0 + 4 * (u * 32 + lane);
                         consider(in[u], v0 + 0, q[u].x);
                         consider(in[u], v0 + 1, q[u].y);
@@ -986,8 +1017,11 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                 const int m_tok = list_token(last);
                 const int32_t* pre = need_seq ? seq_a + static_cast<int64_t>(k) * seq_T : nullptr;
                 const int plen = need_seq ? sl_prev[k] : 0;
+                // Candidates that beat G are staged behind the top N and merged
+                // in whenever the staging room could overflow (and at the end
+                // of the row); G only improves, so it is re-read per chunk.
+                const int stage_room = cand_cap - N;
                 for (int base = 0; base < V; base += kChunk) {
-                    // G is re-read each chunk; it only improves.
                     const uint64_t gh = (N - 1 < M) ? chi[N - 1] : 0;
                     const uint64_t gl = (N - 1 < M) ? clo[N - 1] : 0;
                     for (int v = base + tid; v < base + kChunk && v < V; v += NT) {
@@ -1021,8 +1055,10 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                     __syncthreads();
                     const int staged = sh_stage;
                     __syncthreads();   // every thread holds the count before the next chunk stages
-                    if (staged > 0) {
-                        block_sort_desc_u128(chi, clo, N + staged);
+                    const bool last_chunk = base + kChunk >= V;
+                    if (staged > 0 && (last_chunk || staged > stage_room - kChunk)) {
+                        if (N + staged > 1024) block_top_n_u128(chi, clo, N + staged, N, sel_hi, sel_lo, sel_cap);
+                        else block_sort_desc_u128(chi, clo, N + staged);
                         for (int i = N + tid; i < N + staged; i += NT) { chi[i] = 0; clo[i] = 0; }
                         __syncthreads();
                         if (tid == 0) sh_stage = 0;
