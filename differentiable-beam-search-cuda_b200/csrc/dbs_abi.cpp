@@ -1335,7 +1335,8 @@ static dbs_host::Outputs to_outputs(const DBSDeviceDecodeOutputs* o) {
 
 static void run_device_decode(DBSDecoderHandle* handle, const float* x, int V, const std::vector<ExampleSpec>& spec,
                               const CallConstraints& cons, const DBSDeviceDecodeOutputs* outputs, void* stream,
-                              float* zero_fill = nullptr, int64_t zero_fill_count = 0) {
+                              float* zero_fill = nullptr, int64_t zero_fill_count = 0,
+                              const dbs_host::DecodeControl* split = nullptr) {
     const Options& opt = handle->options;
     if (!outputs || !outputs->parents || !outputs->tokens || !outputs->lengths || !outputs->from_logprob)
         throw std::invalid_argument("device outputs need parents, tokens, lengths and from_logprob");
@@ -1346,7 +1347,7 @@ static void run_device_decode(DBSDecoderHandle* handle, const float* x, int V, c
     const Layout L = dbs_host::make_layout(opt, spec, V);
     dbs_host::DecodeStats st;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);  // NULL = legacy default stream
-    dbs_host::DecodeControl ctl;
+    dbs_host::DecodeControl ctl = split ? *split : dbs_host::DecodeControl{};
     ctl.synchronize = false;  // validation is still checked before the decode is queued
     ctl.zero_fill = zero_fill;
     ctl.zero_fill_count = zero_fill_count;
@@ -1535,6 +1536,89 @@ DBS_EXPORT int dbs_device_backward_batch_ex(DBSDecoderHandle* handle, int batch_
             handle->stats.used_dense_backward = sparse ? 0 : 1;
             handle->stats.last_backward_ns = now_ns() - t0;
         }
+        clear_error(handle);
+        return 0;
+    });
+}
+
+// Uniform-batch example specs of the device entry points.
+static std::vector<ExampleSpec> uniform_spec(const Options& opt, int batch_size, int steps, int vocab_size) {
+    const int64_t stride = static_cast<int64_t>(steps) * opt.beam_size * vocab_size;
+    std::vector<ExampleSpec> spec(static_cast<size_t>(batch_size));
+    for (int b = 0; b < batch_size; ++b) {
+        spec[b].T = steps;
+        spec[b].K = opt.beam_size;
+        spec[b].k_stride = opt.beam_size;
+        spec[b].x_offset = stride * b;
+        spec[b].eos = opt.eos_token;
+        spec[b].min_length = opt.min_length;
+    }
+    return spec;
+}
+
+DBS_EXPORT int dbs_device_row_list_capacity(DBSDecoderHandle* handle, int with_pool, int* capacity) {
+    if (!handle || !capacity) {
+        set_error(handle, "invalid decoder or output pointer");
+        return -1;
+    }
+    return guarded(handle, [&]() {
+        *capacity = dbs_host::list_capacity(handle->options, handle->options.beam_size, with_pool != 0, false);
+        clear_error(handle);
+        return 0;
+    });
+}
+
+DBS_EXPORT int dbs_device_scan_rows(DBSDecoderHandle* handle, const float* log_probs, int batch_size, int steps,
+                                    int vocab_size, int with_pool, int64_t row_begin, int64_t row_end,
+                                    uint64_t* lists, int32_t* list_counts, float* list_bounds, void* cuda_stream) {
+    if (!handle || !lists || !list_counts || !list_bounds) {
+        set_error(handle, "invalid decoder or row list pointer");
+        return -1;
+    }
+    return guarded(handle, [&]() {
+        const Options& opt = handle->options;
+        if (batch_size <= 0) throw std::invalid_argument("batch_size must be positive");
+        check_example(opt, log_probs, steps, vocab_size, opt.beam_size, opt.eos_token, nullptr);
+        const int64_t rows = static_cast<int64_t>(batch_size) * steps * opt.beam_size;
+        if (row_begin < 0 || row_end < row_begin || row_end > rows)
+            throw std::invalid_argument("row range outside the batch's rows");
+        const std::vector<ExampleSpec> spec = uniform_spec(opt, batch_size, steps, vocab_size);
+        const Layout L = dbs_host::make_layout(opt, spec, vocab_size);
+        dbs_host::DecodeControl ctl;
+        ctl.synchronize = false;
+        ctl.lists = lists;
+        ctl.list_count = list_counts;
+        ctl.list_bound = list_bounds;
+        ctl.scan_begin = row_begin;
+        ctl.scan_end = row_end;
+        ctl.merge = false;
+        dbs_host::Outputs none{};
+        dbs_host::decode(opt, log_probs, vocab_size, spec, CallConstraints{}, none, L, with_pool != 0, false,
+                         static_cast<cudaStream_t>(cuda_stream), nullptr, ctl);
+        clear_error(handle);
+        return 0;
+    });
+}
+
+DBS_EXPORT int dbs_device_merge_rows(DBSDecoderHandle* handle, const float* log_probs, int batch_size, int steps,
+                                     int vocab_size, const uint64_t* lists, const int32_t* list_counts,
+                                     const float* list_bounds, const DBSDeviceDecodeOutputs* outputs,
+                                     void* cuda_stream) {
+    if (!handle || !outputs || !lists || !list_counts || !list_bounds) {
+        set_error(handle, "invalid decoder, row list or output pointer");
+        return -1;
+    }
+    return guarded(handle, [&]() {
+        const Options& opt = handle->options;
+        if (batch_size <= 0) throw std::invalid_argument("batch_size must be positive");
+        check_example(opt, log_probs, steps, vocab_size, opt.beam_size, opt.eos_token, nullptr);
+        dbs_host::DecodeControl ctl;
+        ctl.lists = const_cast<uint64_t*>(lists);   // read only when scan is off
+        ctl.list_count = const_cast<int32_t*>(list_counts);
+        ctl.list_bound = const_cast<float*>(list_bounds);
+        ctl.scan = false;
+        run_device_decode(handle, log_probs, vocab_size, uniform_spec(opt, batch_size, steps, vocab_size),
+                          CallConstraints{}, outputs, cuda_stream, nullptr, 0, &ctl);
         clear_error(handle);
         return 0;
     });

@@ -140,7 +140,9 @@ struct BackwardParams {
 
 // Host-side launchers (dbs_kernels.cu). All are asynchronous on `stream`.
 cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream);
-cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream);
+// Scans the rows claimed from counters[2] (the first row to scan) up to
+// p.total_rows; `rows` is how many that is (-1: p.total_rows), for sizing.
+cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream, int64_t rows = -1);
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T,
                               int max_N, bool need_sequences, cudaStream_t stream);
 cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_P,

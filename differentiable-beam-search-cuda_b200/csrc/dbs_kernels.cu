@@ -2143,8 +2143,9 @@ static size_t row_scan_smem(int capw) {
     return static_cast<size_t>(kScanWarpsPerCta) * ((warp_bytes + 127) & ~static_cast<size_t>(127));
 }
 
-cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream) {
-    if (p.total_rows <= 0) return cudaSuccess;
+cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream, int64_t rows) {
+    if (rows < 0) rows = p.total_rows;
+    if (rows <= 0) return cudaSuccess;
     const int capw = row_scan_capw(max_C);
     const int threads = kScanWarpsPerCta * 32;
     const size_t smem = row_scan_smem(capw);
@@ -2167,7 +2168,7 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     }
     if (per_sm < 1) per_sm = 1;
     int64_t ctas = static_cast<int64_t>(num_sms) * per_sm;
-    const int64_t need = (p.total_rows + kScanWarpsPerCta - 1) / kScanWarpsPerCta;
+    const int64_t need = (rows + kScanWarpsPerCta - 1) / kScanWarpsPerCta;
     if (ctas > need) ctas = need;
     row_scan_kernel<<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw);
     return cudaGetLastError();

@@ -391,6 +391,24 @@ void profile_read(int kernel, double* total_ms, long long* launches) {
     *launches = g_prof_n[kernel];
 }
 
+// A row can contribute at most N candidates, so C = N (+ slack for the
+// penalty / n-gram masks) never needs the merge's rescan path; when
+// K * (N + slack) exceeds the merge's per-step candidate capacity the lists
+// are cut to the capacity and the merge proves per step that nothing dropped
+// could have entered (rescanning the row from HBM otherwise), which stays
+// exact.
+static int list_capacity_for(int N, int K, bool dynamic) {
+    const int slack = dynamic ? 8 + N / 8 : 0;
+    int C = N + slack;
+    if (static_cast<int64_t>(K) * C > dbs_dev::kMaxMergeCandidates) C = std::max(1, dbs_dev::kMaxMergeCandidates / K);
+    return C;
+}
+
+int list_capacity(const Options& opt, int K, bool pool, bool dynamic) {
+    const int P = std::max(K, K * opt.relaxed_pool_multiplier);
+    return list_capacity_for(pool ? P : K, K, dynamic);
+}
+
 void decode(const Options& opt, const float* d_x, int V, const std::vector<ExampleSpec>& ex,
             const CallConstraints& cons, const Outputs& out, const Layout& layout, bool pool,
             bool weights, cudaStream_t stream, DecodeStats* stats, const DecodeControl& ctl) {
@@ -407,17 +425,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         const ExampleSpec& e = ex[b];
         const int P = layout.P[b];
         const int N = pool ? P : e.K;
-        int slack = 0;
-        if (dynamic) slack = 8 + N / 8;
-        // Row list capacity. A row can contribute at most N candidates, so
-        // C = N (+ slack for the penalty / n-gram masks) never needs the
-        // merge's rescan path; when K * (N + slack) exceeds the merge's
-        // per-step candidate capacity the lists are cut to the capacity and
-        // the merge proves per step that nothing dropped could have entered
-        // (rescanning the row from HBM otherwise), which stays exact.
-        int C = N + slack;
-        if (static_cast<int64_t>(e.K) * C > dbs_dev::kMaxMergeCandidates)
-            C = std::max(1, dbs_dev::kMaxMergeCandidates / e.K);
+        const int C = list_capacity_for(N, e.K, dynamic);
         if (e.K > 1024) throw LengthError("beam_size above 1024 is not supported by the device decoder");
         dbs_dev::ExampleDesc& d = desc[b];
         d.x_offset = e.x_offset;
@@ -468,10 +476,17 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     hdr += 2 * bytes_of<float>(lmax + 1);
     hdr += bytes_of<int32_t>(B);
     hdr += bytes_of<unsigned long long>(4);
+    const bool ext_lists = ctl.lists != nullptr;
+    const int64_t scan_begin = std::max<int64_t>(0, ctl.scan_begin);
+    const int64_t scan_end = ctl.scan_end < 0 ? rows : std::min<int64_t>(rows, ctl.scan_end);
+    if (ext_lists && (!ctl.list_count || !ctl.list_bound)) throw InvalidArgument("row lists need counts and bounds");
+    if (!ext_lists && !(ctl.scan && ctl.merge)) throw InvalidArgument("a split decode needs caller row lists");
     size_t ws = hdr;
-    ws += bytes_of<uint64_t>(static_cast<size_t>(list_entries));
-    ws += bytes_of<int32_t>(static_cast<size_t>(rows));
-    ws += bytes_of<float>(static_cast<size_t>(rows));
+    if (!ext_lists) {
+        ws += bytes_of<uint64_t>(static_cast<size_t>(list_entries));
+        ws += bytes_of<int32_t>(static_cast<size_t>(rows));
+        ws += bytes_of<float>(static_cast<size_t>(rows));
+    }
     if (dynamic) ws += bytes_of<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
     trace.mark("prepared");
     Lease lease(ws, hdr, stream);
@@ -494,11 +509,18 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     unsigned long long* h_counters = hv.take<unsigned long long>(4);
     std::memset(h_status, 0, sizeof(int32_t) * B);
     std::memset(h_counters, 0, sizeof(unsigned long long) * 4);
+    h_counters[2] = static_cast<unsigned long long>(scan_begin);   // first row the scan claims
     check_cuda(cudaMemcpyAsync(lease.s->dev, lease.s->pinned, cv.off, cudaMemcpyHostToDevice, stream),
                "upload decode metadata");
-    p.lists = cv.take<uint64_t>(static_cast<size_t>(list_entries));
-    p.list_count = cv.take<int32_t>(static_cast<size_t>(rows));
-    p.list_bound = cv.take<float>(static_cast<size_t>(rows));
+    if (ext_lists) {
+        p.lists = ctl.lists;
+        p.list_count = ctl.list_count;
+        p.list_bound = ctl.list_bound;
+    } else {
+        p.lists = cv.take<uint64_t>(static_cast<size_t>(list_entries));
+        p.list_count = cv.take<int32_t>(static_cast<size_t>(rows));
+        p.list_bound = cv.take<float>(static_cast<size_t>(rows));
+    }
     p.seq_scratch = dynamic ? cv.take<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T) : nullptr;
 
     p.x = d_x;
@@ -540,7 +562,8 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     // status and counters are contiguous in the header: one read-back each time
     const size_t st_off = reinterpret_cast<char*>(p.status) - static_cast<char*>(lease.s->dev);
     const size_t st_bytes = reinterpret_cast<char*>(p.counters + 4) - reinterpret_cast<char*>(p.status);
-    if (opt.validate_inputs) {
+    const bool validate = opt.validate_inputs && ctl.scan;   // a merge-only call trusts its scan call
+    if (validate) {
         {
             ProfileScope ps(kValidate, stream);
             check_cuda(dbs_dev::launch_validate(p, stream), "validate kernel");
@@ -549,12 +572,15 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
                    "read status");
         check_cuda(cudaEventRecord(lease.s->validated, stream), "cudaEventRecord");
     }
-    {
+    if (ctl.scan && scan_end > scan_begin) {
         ProfileScope ps(kRowScan, stream);
-        check_cuda(dbs_dev::launch_row_scan(p, max_C, device_sm_count(), stream), "row scan kernel");
+        dbs_dev::DecodeParams ps_p = p;
+        ps_p.total_rows = scan_end;   // rows are claimed from scan_begin up to here
+        check_cuda(dbs_dev::launch_row_scan(ps_p, max_C, device_sm_count(), stream, scan_end - scan_begin),
+                   "row scan kernel");
     }
     trace.mark("row scan queued");
-    if (opt.validate_inputs) {
+    if (validate) {
         // The reference rejects NaN / +Inf before decoding. The row scan is
         // already queued (it only writes this call's workspace and tolerates
         // any value), so the GPU keeps streaming while the host waits for the
@@ -565,7 +591,9 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         for (int b = 0; b < B; ++b)
             if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
     }
-    if (ctl.zero_fill && ctl.zero_fill_count > 0) {
+    if (!ctl.merge) {
+        // scan-only call: read the counters back for the timeout check
+    } else if (ctl.zero_fill && ctl.zero_fill_count > 0) {
         // zero the gradient buffer on the helper stream while the (latency
         // bound, few-CTA) step merge runs; `stream` waits for it afterwards
         // The merge is queued first; the fill is one 32-thread CTA per SM
@@ -594,7 +622,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream), "step merge kernel");
     }
     const bool want_w = (p.weights && p.scores) || (p.relaxed_weights && p.pool_scores);
-    if (want_w) {
+    if (want_w && ctl.merge) {
         ProfileScope ps(kWeights, stream);
         check_cuda(dbs_dev::launch_weights(p, max_T, max_K, max_P, stream), "weights kernel");
     }

@@ -121,7 +121,22 @@ struct DecodeControl {
     bool synchronize = true;
     float* zero_fill = nullptr;
     int64_t zero_fill_count = 0;
+    // Split decode (row-sharded multi-GPU): caller-owned row lists for all
+    // rows (row r at r * list_capacity entries), the row range this call
+    // scans ([scan_begin, scan_end), -1 = all rows), and which halves run.
+    uint64_t* lists = nullptr;
+    int32_t* list_count = nullptr;
+    float* list_bound = nullptr;
+    int64_t scan_begin = 0;
+    int64_t scan_end = -1;
+    bool scan = true;
+    bool merge = true;
 };
+
+// Row-list capacity C of one example (the per-row candidate list length the
+// row scan keeps): N = P in pool mode else K, plus slack with sequence
+// constraints, cut to the merge's per-step capacity.
+int list_capacity(const Options& opt, int K, bool pool, bool dynamic);
 
 void decode(const Options& opt, const float* d_x, int V, const std::vector<ExampleSpec>& ex,
             const CallConstraints& cons, const Outputs& out, const Layout& layout, bool pool,

@@ -235,6 +235,61 @@ def device_decode(x4: torch.Tensor, options: DBSOptions, with_pool: bool = False
     return trace
 
 
+def row_shards(rows: int, world: int):
+    """Contiguous row ranges of a row-sharded decode: rank r scans
+    [r * per, min(rows, (r + 1) * per)); every rank's range is padded to `per`
+    rows so the all-gather moves equal chunks."""
+    if world < 1:
+        raise ValueError("world size must be positive")
+    per = max(1, -(-rows // world))
+    return per, [(min(rows, r * per), min(rows, (r + 1) * per)) for r in range(world)]
+
+
+def decode_row_sharded(x4: torch.Tensor, options: DBSOptions, with_pool: bool = False, with_weights: bool = False,
+                       group=None, all_gather=None) -> DeviceTrace:
+    """Decode a uniform batch whose log-probs every rank holds, with the row
+    scan split across the ranks of `group`: each rank scans its contiguous
+    share of the B*T*K rows, one all-gather assembles every row's candidate
+    list on every rank, and each rank runs the (sequential, small) step merge
+    itself. Every rank returns the trace dbs_device_decode_batch would
+    produce. `all_gather(out, inp)` defaults to
+    torch.distributed.all_gather_into_tensor on `group`."""
+    import torch.distributed as dist
+    B, T, K, V = (int(s) for s in x4.shape)
+    world = dist.get_world_size(group) if all_gather is None else all_gather.world
+    rank = dist.get_rank(group) if all_gather is None else all_gather.rank
+    lib = _library()
+    h = _handle(options)
+    cap = ctypes.c_int()
+    _check(lib.dbs_device_row_list_capacity(h, 1 if with_pool else 0, ctypes.byref(cap)), h, "dbs_decode")
+    C = int(cap.value)
+    rows = B * T * K
+    per, ranges = row_shards(rows, world)
+    dev = x4.device
+    lists = torch.empty((world * per, C), dtype=torch.int64, device=dev)
+    counts = torch.empty((world * per,), dtype=torch.int32, device=dev)
+    bounds = torch.empty((world * per,), dtype=torch.float32, device=dev)
+    begin, end = ranges[rank]
+    stream = _stream_ptr(dev)
+    with torch.cuda.device(dev):
+        rc = lib.dbs_device_scan_rows(h, _vp(x4), B, T, V, 1 if with_pool else 0, begin, end, _vp(lists), _vp(counts),
+                                      _vp(bounds), stream)
+    _check(rc, h, "dbs_decode")
+    sl = slice(rank * per, (rank + 1) * per)
+    gather = all_gather if all_gather is not None else (
+        lambda out, inp: dist.all_gather_into_tensor(out, inp, group=group))
+    for t in (lists, counts, bounds):
+        gather(t, t[sl].clone())
+    P = max(K, K * options.relaxed_pool_multiplier)
+    trace = DeviceTrace(B, T, K, dev, with_pool=with_pool, P=P, with_weights=with_weights)
+    outs = trace.struct()
+    with torch.cuda.device(dev):
+        rc = lib.dbs_device_merge_rows(h, _vp(x4), B, T, V, _vp(lists), _vp(counts), _vp(bounds), ctypes.byref(outs),
+                                       stream)
+    _check(rc, h, "dbs_decode")
+    return trace
+
+
 def device_backward_dense(trace: DeviceTrace, grad_final: torch.Tensor, options: DBSOptions, V: int,
                           out: Optional[torch.Tensor] = None, prezeroed: bool = False) -> torch.Tensor:
     """Dense surrogate gradient [B,T,K,V] of the final scores, on the device.

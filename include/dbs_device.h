@@ -112,6 +112,28 @@ DBS_EXPORT int dbs_device_backward_batch_ex(DBSDecoderHandle* handle, int batch_
                                             int64_t* sparse_counts, float* grad_initial_scores, int flags,
                                             void* cuda_stream);
 
+/* Split decode of a uniform batch for row-sharded multi-GPU runs. The decode
+ * is a row scan (every [V] row reduced to its best C candidates, C from
+ * dbs_device_row_list_capacity) followed by the sequential step merge.
+ * dbs_device_scan_rows scans rows [row_begin, row_end) of the batch (global
+ * row r = (b*steps + t)*beam_size + k) into caller-owned device arrays that
+ * cover all rows: lists [rows * C] (64-bit entries), list_counts [rows],
+ * list_bounds [rows]; it validates the input like dbs_device_decode_batch.
+ * Once every row is present (e.g. after an all-gather of each rank's range),
+ * dbs_device_merge_rows runs the merge (and weights) and writes the same
+ * outputs as dbs_device_decode_batch with the same log_probs. The entry
+ * format is internal; only this library's scan produces lists the merge
+ * accepts. with_pool must match the outputs' pool_scores (NULL or not).
+ * No counterpart in the reference (its CPU decoder has no sharding). */
+DBS_EXPORT int dbs_device_row_list_capacity(DBSDecoderHandle* handle, int with_pool, int* capacity);
+DBS_EXPORT int dbs_device_scan_rows(DBSDecoderHandle* handle, const float* log_probs, int batch_size, int steps,
+                                    int vocab_size, int with_pool, int64_t row_begin, int64_t row_end,
+                                    uint64_t* lists, int32_t* list_counts, float* list_bounds, void* cuda_stream);
+DBS_EXPORT int dbs_device_merge_rows(DBSDecoderHandle* handle, const float* log_probs, int batch_size, int steps,
+                                     int vocab_size, const uint64_t* lists, const int32_t* list_counts,
+                                     const float* list_bounds, const DBSDeviceDecodeOutputs* outputs,
+                                     void* cuda_stream);
+
 /* Sparse backward of a uniform batch that allocates nothing on its call path:
  * same arguments, outputs and results as dbs_device_backward_batch with
  * sparse outputs (grad_log_probs NULL). For callers that must not allocate
