@@ -564,7 +564,7 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     return j;
 }
 
-__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(DecodeParams p, int capw) {
+__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(DecodeParams p, int capw, int speculate) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     constexpr unsigned FULL = 0xFFFFFFFFu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -643,6 +643,13 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
         }
     };
 
+    // Lists longer than 32 (when each warp scans many rows): the warp starts
+    // a row at a speculative threshold, the (3C/2)-th largest lp of the
+    // previous row it scanned. If fewer than C entries reach it the row is
+    // scanned again from global memory without a threshold, so the list
+    // stays exact; otherwise far fewer elements take the slow path than with
+    // a threshold that starts at -FLT_MAX.
+    float spec = -FLT_MAX;
     while (true) {
         issue_more();
         const RowJob& j = cur;
@@ -660,7 +667,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             }
         } else {
             int cnt = 0;
-            float thr = -FLT_MAX;
+            const bool spec_used = speculate && C > 32 && hist_ints && spec > -FLT_MAX;
+            float thr = spec_used ? spec : -FLT_MAX;
             float rej = -INFINITY;
             float evict = -INFINITY;
             auto allowed = [&](int v, float lp) {
@@ -763,9 +771,35 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 consider(in, t0 + lane, lp);
             }
             __syncwarp();
-            // long lists: cut to about C before the one full sort of the row
-            if (C > 32 && hist_ints && cnt > C + 32) cnt = warp_compact_select(buf, cnt, C, lane, hist, thr, evict);
+            if (spec_used && cnt < C) {
+                // the speculative threshold dropped part of the best C: scan
+                // the row again (global memory, token order) without one
+                cnt = 0;
+                thr = -FLT_MAX;
+                rej = -INFINITY;
+                evict = -INFINITY;
+                for (int base = 0; base < p.V; base += 128) {
+                    const int t0 = base + 4 * lane;
+                    float v4[4];
+                    bool in4[4];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        in4[c] = t0 + c < p.V;
+                        v4[c] = in4[c] ? j.row[t0 + c] : -INFINITY;
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) consider(in4[c], t0 + c, v4[c]);
+                    if (cnt > capw - 128 - 8) compact();
+                }
+                __syncwarp();
+            }
+            // long lists: cut to about 3C/2 (the next row's speculative
+            // threshold comes from there) before the one full sort of the row
+            const int k_spec = C + C / 2;
+            if (C > 32 && hist_ints && cnt > k_spec + 32)
+                cnt = warp_compact_select(buf, cnt, k_spec, lane, hist, thr, evict);
             warp_sort_desc_u64(buf, cnt, lane);
+            if (C > 32 && hist_ints && cnt >= k_spec) spec = list_lp(buf[k_spec - 1]);
             const int keep = cnt < C ? cnt : C;
             for (int i = lane; i < keep; i += 32) out[i] = buf[i];
             rej = warp_max(rej);
@@ -2170,7 +2204,10 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     int64_t ctas = static_cast<int64_t>(num_sms) * per_sm;
     const int64_t need = (rows + kScanWarpsPerCta - 1) / kScanWarpsPerCta;
     if (ctas > need) ctas = need;
-    row_scan_kernel<<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw);
+    // The speculative threshold pays off over several rows per warp; with
+    // few rows a failed guess (a second read of the row) only adds to the tail.
+    const int speculate = (max_C > 32 && rows >= 4 * ctas * kScanWarpsPerCta) ? 1 : 0;
+    row_scan_kernel<<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw, speculate);
     return cudaGetLastError();
 }
 

@@ -160,6 +160,32 @@ def test_beam_times_pool_above_merge_capacity(libdbs, oracle_lib, K, T, V, mult,
     assert_decode_equal(got, want, f"K={K} P={want['P']}")
 
 
+@pytest.mark.parametrize("mult", [8, 16])
+def test_rows_of_very_different_sharpness(libdbs, oracle_lib, mult):
+    # Long row lists start from a threshold taken from an earlier row; rows
+    # that alternate between sharp and flat distributions make that guess
+    # far too high (the row is scanned again) or far too low (slow but exact).
+    rng = np.random.default_rng(mult)
+    T, K, V = 4, 8, 6000
+    scale = np.where(np.arange(K) % 2 == 0, 12.0, 0.3).astype(np.float32)
+    x = log_softmax_np(rng.standard_normal((T, K, V)).astype(np.float32) * scale[None, :, None])
+    opts = dict(beam_size=K, relaxed_pool_multiplier=mult, eos_token=2)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, {})
+    got = _product_decode(libdbs, opts, x, T, V, {})
+    assert_decode_equal(got, want, f"mult={mult}")
+    # a batch with enough rows (9600) that every warp scans several and the
+    # speculative threshold is used, failing on every sharp-after-flat row
+    B, T, V = 40, 30, 2000
+    xb = log_softmax_np(rng.standard_normal((B, T, K, V)).astype(np.float32) * scale[None, None, :, None])
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    br = dec.decode_batch(np.ascontiguousarray(xb), B, T, V, 4)
+    for b in range(0, B, 3):
+        w = _oracle_decode(oracle_lib, opts, xb[b], T, V, {})
+        assert_decode_equal(dc.read_result(libdbs, libdbs.dbs_batch_result_at(br, b)), w, f"batch example {b}")
+    libdbs.dbs_free_batch_result(br)
+    dec.close()
+
+
 def test_massive_ties_with_large_beam(libdbs, oracle_lib):
     # constant rows: thousands of candidates share one key prefix, so the
     # merge's radix selection cannot narrow them and sorts them all
