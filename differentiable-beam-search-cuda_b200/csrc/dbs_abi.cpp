@@ -310,9 +310,23 @@ size_t device_budget_bytes() {
 // Runs the device decode of `hx` over the caller array x (host or device) and
 // returns the host mirror. Host inputs are staged in example chunks that fit
 // half of the free device memory; each example is packed tight [T,K,V].
+// Reads a caller array that may live on the device into host memory.
+template <class T>
+std::vector<T> host_copy(const T* p, size_t n) {
+    std::vector<T> v(n);
+    if (n == 0 || !p) return v;
+    if (is_device_pointer(p)) {
+        dbs_host::check_cuda(cudaMemcpy(v.data(), p, n * sizeof(T), cudaMemcpyDeviceToHost), "read caller array");
+    } else {
+        std::memcpy(v.data(), p, n * sizeof(T));
+    }
+    return v;
+}
+
 std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt, const float* x, int V,
                                         const std::vector<HostExample>& hx, const CallConstraints& cons,
-                                        DBSDecoderHandle* stats_handle) {
+                                        DBSDecoderHandle* stats_handle,
+                                        const dbs_host::TokenFilter* filter = nullptr) {
     auto store = std::make_shared<ResultStore>();
     store->opt = opt;
     store->V = V;
@@ -453,7 +467,17 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
         o.final_scores = reinterpret_cast<float*>(take(nfin * 4));
         const float* dx = x_dev ? x : xs.as<float>();
         dbs_host::DecodeStats st;
-        dbs_host::decode(opt, dx, V, spec, cons, o, CL, true, true, s, &st, dbs_host::DecodeControl{});
+        if (filter) {
+            // one example (dbs_decode_constrained_ex): the host checks need the
+            // constraint arrays in host memory
+            const HostExample& e = hx[b0];
+            const std::vector<uint8_t> hb = host_copy(e.banned, e.banned ? static_cast<size_t>(V) : 0);
+            const std::vector<int32_t> hf = host_copy(e.forced, e.forced ? static_cast<size_t>(e.T) : 0);
+            dbs_host::decode_filtered(opt, dx, V, spec[0], e.banned ? hb.data() : nullptr,
+                                      e.forced ? hf.data() : nullptr, cons, o, CL, s, &st, *filter);
+        } else {
+            dbs_host::decode(opt, dx, V, spec, cons, o, CL, true, true, s, &st, dbs_host::DecodeControl{});
+        }
         if (stats_handle) {
             stats_handle->last_row_rescans.store(static_cast<int64_t>(st.row_rescans));
             stats_handle->last_merge_rescans.store(static_cast<int64_t>(st.merge_fallbacks));
@@ -626,18 +650,6 @@ int guarded(DBSDecoderHandle* h, F&& body) {
     }
 }
 
-// Reads a caller array that may live on the device into host memory.
-template <class T>
-std::vector<T> host_copy(const T* p, size_t n) {
-    std::vector<T> v(n);
-    if (n == 0 || !p) return v;
-    if (is_device_pointer(p)) {
-        dbs_host::check_cuda(cudaMemcpy(v.data(), p, n * sizeof(T), cudaMemcpyDeviceToHost), "read caller array");
-    } else {
-        std::memcpy(v.data(), p, n * sizeof(T));
-    }
-    return v;
-}
 
 }  // namespace
 
@@ -728,10 +740,9 @@ DBS_EXPORT const char* dbs_last_error(DBSDecoderHandle* handle) {
 
 static int decode_constrained_impl(DBSDecoderHandle* handle, const float* log_probs, int steps, int vocab_size,
                                    const uint8_t* banned, const int32_t* forced, int min_length, float rep,
-                                   int ngram, bool has_filter, DBSResultHandle** out_result) {
+                                   int ngram, const DBSAdvancedConstraintsC* filter_src,
+                                   DBSResultHandle** out_result) {
     const int64_t t0 = now_ns();
-    if (has_filter)
-        throw std::invalid_argument("token_filter callbacks are not supported by the device decoder");
     const Options& opt = handle->options;
     std::vector<int32_t> forced_host;
     if (forced && steps > 0) forced_host = host_copy(forced, static_cast<size_t>(steps));
@@ -748,7 +759,18 @@ static int decode_constrained_impl(DBSDecoderHandle* handle, const float* log_pr
     CallConstraints cons;
     cons.repetition_penalty = rep;
     cons.no_repeat_ngram = ngram;
-    auto store = run_decode(handle, opt, log_probs, vocab_size, {e}, cons, handle);
+    dbs_host::TokenFilter filter;
+    if (filter_src && filter_src->token_filter) {
+        // the reference calls the filter with the constraints' batch index,
+        // the step, the parent beam, its token prefix and the token
+        const DBSTokenFilterFn fn = filter_src->token_filter;
+        void* user = filter_src->token_filter_user_data;
+        const int batch_index = filter_src->batch_index;
+        filter = [fn, user, batch_index](int step, int parent, const int32_t* prefix, int prefix_len, int token) {
+            return fn(user, batch_index, step, parent, prefix, prefix_len, token);
+        };
+    }
+    auto store = run_decode(handle, opt, log_probs, vocab_size, {e}, cons, handle, filter ? &filter : nullptr);
     auto r = std::make_unique<DBSResultHandle>();
     r->store = store;
     r->index = 0;
@@ -763,7 +785,7 @@ DBS_EXPORT int dbs_decode(DBSDecoderHandle* handle, const float* log_probs, int 
     if (out_result) *out_result = nullptr;
     if (!handle || !out_result) return -1;
     return guarded(handle, [&]() {
-        return decode_constrained_impl(handle, log_probs, steps, vocab_size, nullptr, nullptr, -1, 1.0f, 0, false,
+        return decode_constrained_impl(handle, log_probs, steps, vocab_size, nullptr, nullptr, -1, 1.0f, 0, nullptr,
                                        out_result);
     });
 }
@@ -795,9 +817,8 @@ DBS_EXPORT int dbs_decode_constrained_ex(DBSDecoderHandle* handle, const float* 
         const int min_length = c ? c->min_length : -1;
         const float rep = (c && c->repetition_penalty > 0.0f) ? c->repetition_penalty : 1.0f;
         const int ngram = c ? c->no_repeat_ngram_size : 0;
-        const bool filter = c && c->token_filter;
         return decode_constrained_impl(handle, log_probs, steps, vocab_size, banned, forced, min_length, rep, ngram,
-                                       filter, out_result);
+                                       c, out_result);
     });
 }
 

@@ -78,6 +78,16 @@ struct DecodeParams {
     float log_repetition_penalty; // logf(repetition_penalty), host computed
     int32_t no_repeat_ngram;      // > 0 enables
     int32_t validate_inputs;
+    // Stepwise decoding (host token filters): the merge runs steps
+    // [t_begin, t_end) only, loading the beam state from merge_state when
+    // t_begin > 0 and storing it there when steps remain; row_allow [K][V]
+    // holds the host filter's verdict for the rows scanned in this launch;
+    // force_seq keeps the beams' token prefixes without sequence constraints.
+    int32_t t_begin;
+    int32_t t_end;
+    float* merge_state;            // [B][4][max K]: raw, len, ended, prefix length
+    const uint8_t* row_allow;
+    int32_t force_seq;
     // workspace
     uint64_t* lists;              // row lists, key = ord(lp)<<32 | ~token
     int32_t* list_count;          // [total_rows]

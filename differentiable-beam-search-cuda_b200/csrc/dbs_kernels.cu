@@ -535,6 +535,7 @@ struct RowJob {
     int eos;
     bool eos_blocked;
     const uint8_t* banned;
+    const uint8_t* allow;   // host filter verdicts of this row, or nullptr
     int h;       // unaligned head elements
     int nv;      // float4 in the aligned body
     int chunks;
@@ -555,6 +556,7 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     j.eos = d.eos;
     j.eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
     j.banned = d.banned;
+    j.allow = p.row_allow ? p.row_allow + static_cast<int64_t>(k) * p.V : nullptr;
     const uintptr_t addr = reinterpret_cast<uintptr_t>(j.row);
     int h = static_cast<int>(((16u - (addr & 15u)) & 15u) >> 2);
     if (h > p.V) h = p.V;
@@ -660,7 +662,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             if (lane == 0) {
                 const float lp = j.row[j.forced];
                 const bool ok = isfinite(lp) && !(j.banned && j.banned[j.forced]) &&
-                                !(j.eos_blocked && j.forced == j.eos);
+                                !(j.eos_blocked && j.forced == j.eos) && !(j.allow && !j.allow[j.forced]);
                 if (ok) out[0] = list_key(lp, j.forced);
                 p.list_count[j.r] = ok ? 1 : 0;
                 p.list_bound[j.r] = -INFINITY;
@@ -672,7 +674,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             float rej = -INFINITY;
             float evict = -INFINITY;
             auto allowed = [&](int v, float lp) {
-                return lp != INFINITY && !(j.banned && j.banned[v]) && !(j.eos_blocked && v == j.eos);
+                return lp != INFINITY && !(j.banned && j.banned[v]) && !(j.eos_blocked && v == j.eos) &&
+                       !(j.allow && !j.allow[v]);
             };
             auto consider = [&](bool in, int v, float lp) {
                 const bool pass = in && lp >= thr;
@@ -923,8 +926,8 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
 
     const bool use_rep = p.repetition_penalty > 1.0f;
     const bool use_ngram = p.no_repeat_ngram > 0;
-    const bool need_seq = use_rep || use_ngram;
-    // Beam prefixes (only with repetition penalty / n-gram constraints):
+    const bool need_seq = use_rep || use_ngram || p.force_seq;
+    // Beam prefixes (with repetition penalty / n-gram constraints / filters):
     // [2][K][seq_T] in global scratch, plus n-gram blocked sets [K][seq_T].
     // per-example region of 3 * seq_K * seq_T (seq_K = largest K of the call)
     int32_t* seq_a = need_seq ? p.seq_scratch + static_cast<int64_t>(e) * 3 * seq_K * seq_T : nullptr;
@@ -935,15 +938,29 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
     int* sl_prev = seq_len_a;
     int* sl_next = seq_len_b;
 
+    // beam state: fresh at step 0, else what the previous launch stored
+    const int t_first = p.t_begin > 0 ? p.t_begin : 0;
+    const int t_stop = p.t_end < T ? p.t_end : T;
+    float* state = p.merge_state ? p.merge_state + static_cast<int64_t>(e) * 4 * seq_K : nullptr;
     for (int k = tid; k < K; k += NT) {
-        s.prev_raw[k] = (k == 0) ? 0.0f : -INFINITY;
-        s.prev_len[k] = 0;
-        s.ended[k] = 0;
-        if (need_seq) sl_prev[k] = 0;
+        if (t_first > 0 && state) {
+            s.prev_raw[k] = state[k];
+            s.prev_len[k] = __float_as_int(state[seq_K + k]);
+            s.ended[k] = __float_as_int(state[2 * seq_K + k]);
+            if (need_seq) sl_prev[k] = __float_as_int(state[3 * seq_K + k]);
+        } else {
+            s.prev_raw[k] = (k == 0) ? 0.0f : -INFINITY;
+            s.prev_len[k] = 0;
+            s.ended[k] = 0;
+            if (need_seq) sl_prev[k] = 0;
+        }
+    }
+    if (need_seq && (t_first & 1)) {   // the prefix buffers swap once per step
+        int32_t* tmp = seq_a; seq_a = seq_b; seq_b = tmp;
     }
     __syncthreads();
 
-    for (int t = 0; t < T; ++t) {
+    for (int t = t_first; t < t_stop; ++t) {
         const int64_t row0 = d.row_begin + static_cast<int64_t>(t) * K;
         const int forced = d.forced ? d.forced[t] : -1;
         const bool eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
@@ -1062,6 +1079,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                         if (forced >= 0 && v != forced) continue;
                         if (d.banned && d.banned[v]) continue;
                         if (eos_blocked && v == d.eos) continue;
+                        if (p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v]) continue;
                         float lp = row[v];
                         if (!isfinite(lp)) continue;
                         const float lpc = __fadd_rn(lp, 0.0f);
@@ -1179,6 +1197,17 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
             int* tl = sl_prev; sl_prev = sl_next; sl_next = tl;
         }
         __syncthreads();
+    }
+    if (t_stop < T) {   // more steps follow in a later launch: keep the state
+        if (state) {
+            for (int k = tid; k < K; k += NT) {
+                state[k] = s.prev_raw[k];
+                state[seq_K + k] = __int_as_float(s.prev_len[k]);
+                state[2 * seq_K + k] = __int_as_float(s.ended[k]);
+                state[3 * seq_K + k] = __int_as_float(need_seq ? sl_prev[k] : 0);
+            }
+        }
+        return;
     }
     // Finalisation (src/differentiable_beam.cpp:1661-1667): a division, not
     // a multiply by the reciprocal.

@@ -415,7 +415,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     const int B = static_cast<int>(ex.size());
     if (B <= 0) return;
     HostTrace trace("decode");
-    const bool dynamic = cons.repetition_penalty > 1.0f || cons.no_repeat_ngram > 0;
+    const bool dynamic = cons.repetition_penalty > 1.0f || cons.no_repeat_ngram > 0 || ctl.force_seq;
 
     std::vector<dbs_dev::ExampleDesc> desc(B);
     std::vector<int64_t> row_prefix(B + 1, 0);
@@ -487,7 +487,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         ws += bytes_of<int32_t>(static_cast<size_t>(rows));
         ws += bytes_of<float>(static_cast<size_t>(rows));
     }
-    if (dynamic) ws += bytes_of<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
+    if (dynamic && !ctl.seq_scratch) ws += bytes_of<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
     trace.mark("prepared");
     Lease lease(ws, hdr, stream);
     trace.mark("slot");
@@ -521,7 +521,14 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         p.list_count = cv.take<int32_t>(static_cast<size_t>(rows));
         p.list_bound = cv.take<float>(static_cast<size_t>(rows));
     }
-    p.seq_scratch = dynamic ? cv.take<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T) : nullptr;
+    p.seq_scratch = !dynamic ? nullptr
+                  : ctl.seq_scratch ? ctl.seq_scratch
+                                    : cv.take<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
+    p.t_begin = ctl.t_begin;
+    p.t_end = ctl.t_end;
+    p.merge_state = ctl.merge_state;
+    p.row_allow = ctl.row_allow;
+    p.force_seq = ctl.force_seq ? 1 : 0;
 
     p.x = d_x;
     p.V = V;
@@ -622,7 +629,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream), "step merge kernel");
     }
     const bool want_w = (p.weights && p.scores) || (p.relaxed_weights && p.pool_scores);
-    if (want_w && ctl.merge) {
+    if (want_w && ctl.merge && ctl.weights) {
         ProfileScope ps(kWeights, stream);
         check_cuda(dbs_dev::launch_weights(p, max_T, max_K, max_P, stream), "weights kernel");
     }
@@ -765,6 +772,123 @@ void backward_sparse_noalloc(const Options& opt, int V, int B, int T, const Back
     p.sparse_counts = out.sparse_counts;
     p.grad_initial = out.grad_initial;
     check_cuda(dbs_dev::launch_backward_noalloc(p, T, K, P, inv, stream), "allocation-free backward kernel");
+}
+
+// Filter-free checks that decide whether the reference consults the token
+// filter (scan_parent_row_scalar_advanced, src/differentiable_beam.cpp:512-549:
+// forced, banned, EOS before min_length, then the n-gram check of
+// token_allowed_by_advanced_constraints, :327-351).
+static bool ngram_repeats(const std::vector<int32_t>& pre, int n, int token) {
+    if (n <= 0) return false;
+    if (n == 1) {
+        for (int32_t v : pre)
+            if (v == token) return true;
+        return false;
+    }
+    const int len = static_cast<int>(pre.size());
+    if (len + 1 < n) return false;
+    const int suffix = len - (n - 1);
+    for (int i = 0; i + n <= len; ++i) {
+        bool same = true;
+        for (int j = 0; j < n - 1 && same; ++j) same = pre[i + j] == pre[suffix + j];
+        if (same && pre[i + n - 1] == token) return true;
+    }
+    return false;
+}
+
+// Device allocation of the filtered decode, released in stream order.
+struct StepBuffer {
+    void* ptr = nullptr;
+    cudaStream_t stream;
+    StepBuffer(size_t n, cudaStream_t s) : stream(s) {
+        if (n) check_cuda(cudaMallocAsync(&ptr, n, s), "cudaMallocAsync(filtered decode)");
+    }
+    ~StepBuffer() {
+        if (ptr) cudaFreeAsync(ptr, stream);
+    }
+    StepBuffer(const StepBuffer&) = delete;
+    StepBuffer& operator=(const StepBuffer&) = delete;
+    template <class T>
+    T* as() const { return static_cast<T*>(ptr); }
+};
+
+void decode_filtered(const Options& opt, const float* d_x, int V, const ExampleSpec& ex, const uint8_t* h_banned,
+                     const int32_t* h_forced, const CallConstraints& cons, const Outputs& out, const Layout& layout,
+                     cudaStream_t stream, DecodeStats* stats, const TokenFilter& filter) {
+    const int T = ex.T, K = ex.K;
+    const bool pool = out.pool_scores != nullptr;
+    const int C = list_capacity(opt, K, pool, true);
+    const int64_t rows = static_cast<int64_t>(T) * K;
+    // state kept between the per-step launches (device) and its host mirror
+    StepBuffer lists(static_cast<size_t>(rows) * C * sizeof(uint64_t), stream);
+    StepBuffer counts(static_cast<size_t>(rows) * sizeof(int32_t), stream);
+    StepBuffer bounds(static_cast<size_t>(rows) * sizeof(float), stream);
+    StepBuffer state(static_cast<size_t>(4) * K * sizeof(float), stream);
+    StepBuffer seq(static_cast<size_t>(3) * K * T * sizeof(int32_t), stream);
+    StepBuffer allow(static_cast<size_t>(K) * V, stream);
+    std::vector<uint8_t> h_allow(static_cast<size_t>(K) * V);
+    std::vector<float> h_state(static_cast<size_t>(4) * K);
+    std::vector<int32_t> h_seq(static_cast<size_t>(K) * T);
+    std::vector<std::vector<int32_t>> prefix(K);
+    std::vector<float> raw(K, -std::numeric_limits<float>::infinity());
+    std::vector<int> len(K, 0), ended(K, 0);
+    raw[0] = 0.0f;
+    const int min_len = ex.min_length;
+    for (int t = 0; t < T; ++t) {
+        if (t > 0) {
+            // beams after step t-1: state and the prefix buffer of parity t
+            check_cuda(cudaMemcpyAsync(h_state.data(), state.ptr, h_state.size() * sizeof(float),
+                                       cudaMemcpyDeviceToHost, stream), "read beam state");
+            const int32_t* cur = seq.as<int32_t>() + ((t & 1) ? static_cast<size_t>(K) * T : 0);
+            check_cuda(cudaMemcpyAsync(h_seq.data(), cur, h_seq.size() * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                       stream), "read beam prefixes");
+            check_cuda(cudaStreamSynchronize(stream), "filtered decode step");
+            for (int k = 0; k < K; ++k) {
+                raw[k] = h_state[k];
+                int v = 0;
+                std::memcpy(&v, &h_state[K + k], sizeof(int));
+                len[k] = v;
+                std::memcpy(&v, &h_state[2 * K + k], sizeof(int));
+                ended[k] = v;
+                std::memcpy(&v, &h_state[3 * K + k], sizeof(int));
+                prefix[k].assign(h_seq.begin() + static_cast<size_t>(k) * T, h_seq.begin() + static_cast<size_t>(k) * T + v);
+            }
+        }
+        const int forced = h_forced ? h_forced[t] : -1;
+        std::fill(h_allow.begin(), h_allow.end(), uint8_t{0});
+        for (int k = 0; k < K; ++k) {
+            if (!std::isfinite(raw[k]) || (ex.eos >= 0 && ended[k])) continue;   // not scanned
+            const int new_len = len[k] + 1;
+            uint8_t* a = h_allow.data() + static_cast<size_t>(k) * V;
+            for (int v = 0; v < V; ++v) {
+                if (forced >= 0 && v != forced) continue;
+                if (h_banned && h_banned[v]) continue;
+                if (ex.eos >= 0 && v == ex.eos && new_len < min_len) continue;
+                if (ngram_repeats(prefix[k], cons.no_repeat_ngram, v)) continue;
+                a[v] = filter(t, k, prefix[k].empty() ? nullptr : prefix[k].data(), static_cast<int>(prefix[k].size()),
+                              v) != 0;
+            }
+        }
+        check_cuda(cudaMemcpyAsync(allow.ptr, h_allow.data(), h_allow.size(), cudaMemcpyHostToDevice, stream),
+                   "upload filter verdicts");
+        DecodeControl ctl;
+        ctl.synchronize = true;
+        ctl.lists = lists.as<uint64_t>();
+        ctl.list_count = counts.as<int32_t>();
+        ctl.list_bound = bounds.as<float>();
+        ctl.scan_begin = static_cast<int64_t>(t) * K;
+        ctl.scan_end = static_cast<int64_t>(t + 1) * K;
+        ctl.t_begin = t;
+        ctl.t_end = t + 1;
+        ctl.merge_state = state.as<float>();
+        ctl.seq_scratch = seq.as<int32_t>();
+        ctl.row_allow = allow.as<uint8_t>();
+        ctl.force_seq = true;
+        ctl.weights = t + 1 == T;
+        Options step_opt = opt;
+        step_opt.validate_inputs = t == 0 ? opt.validate_inputs : 0;
+        decode(step_opt, d_x, V, {ex}, cons, out, layout, pool, out.weights != nullptr, stream, stats, ctl);
+    }
 }
 
 }  // namespace dbs_host

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <functional>
 #include <vector>
 
 #include <cuda_runtime.h>
@@ -131,7 +132,33 @@ struct DecodeControl {
     int64_t scan_end = -1;
     bool scan = true;
     bool merge = true;
+    // Stepwise decode (host token filter): merge steps [t_begin, t_end) with
+    // the beam state in merge_state and the prefixes in seq_scratch (both
+    // caller-owned, kept between calls), row verdicts in row_allow [K][V].
+    int t_begin = 0;
+    int t_end = 1 << 30;
+    float* merge_state = nullptr;
+    int32_t* seq_scratch = nullptr;
+    const uint8_t* row_allow = nullptr;
+    bool force_seq = false;
+    bool weights = true;
 };
+
+// Host token filter of the reference's advanced constraints
+// (DBSAdvancedConstraintsC.token_filter): non-zero allows `token` after the
+// beam `parent` whose tokens so far are prefix[0..prefix_len).
+using TokenFilter = std::function<int(int step, int parent, const int32_t* prefix, int prefix_len, int token)>;
+
+// Decode of one example whose candidates also pass a host token filter. The
+// filter depends on each beam's prefix, so the decode runs one step at a
+// time: the device scans the step's rows with the filter's verdicts and
+// merges the step; the host reads the beams back and asks the filter about
+// the next step's tokens, in the reference's order (parent ascending, token
+// ascending, only tokens that pass the forced / banned / min-EOS / n-gram
+// checks). Synchronous.
+void decode_filtered(const Options& opt, const float* d_x, int V, const ExampleSpec& ex, const uint8_t* h_banned,
+                     const int32_t* h_forced, const CallConstraints& cons, const Outputs& out, const Layout& layout,
+                     cudaStream_t stream, DecodeStats* stats, const TokenFilter& filter);
 
 // Row-list capacity C of one example (the per-row candidate list length the
 // row scan keeps): N = P in pool mode else K, plus slack with sequence

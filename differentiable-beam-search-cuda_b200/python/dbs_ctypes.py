@@ -347,8 +347,9 @@ class Decoder:
         return r
 
     def decode_constrained_ex(self, x, steps, vocab, banned=None, forced=None, min_length=-1,
-                              repetition_penalty=1.0, no_repeat_ngram_size=0, token_filter=None):
+                              repetition_penalty=1.0, no_repeat_ngram_size=0, token_filter=None, batch_index=0):
         c = DBSAdvancedConstraintsC()
+        c.batch_index = batch_index
         c.banned_tokens = _ptr(banned)
         c.forced_tokens = _ptr(forced)
         c.min_length = min_length

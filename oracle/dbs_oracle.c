@@ -237,7 +237,7 @@ int oracle_decode(const oracle_options* opt, const float* x, int T, int V,
     const int P = oracle_pool_size(opt);
     const int eos = opt->eos_token;
     const float alpha = opt->length_penalty_alpha;
-    const int advanced = c && (c->repetition_penalty > 1.0f || c->no_repeat_ngram_size > 0);
+    const int advanced = c && (c->repetition_penalty > 1.0f || c->no_repeat_ngram_size > 0 || c->token_filter);
     const float log_pen = (c && c->repetition_penalty > 1.0f) ? logf(c->repetition_penalty) : 0.0f;
 
     for (size_t i = 0; i < (size_t)T * K; ++i) {
@@ -292,6 +292,11 @@ int oracle_decode(const oracle_options* opt, const float* x, int T, int V,
                 if (eos >= 0 && v == eos && new_len < min_len) continue;
                 if (advanced && c->no_repeat_ngram_size > 0 &&
                     repeats_ngram(pre, plen, v, c->no_repeat_ngram_size)) continue;
+                /* the filter sees the beam's prefix (NULL when empty) and runs
+                 * after the n-gram check, before the finiteness check */
+                if (advanced && c->token_filter &&
+                    c->token_filter(c->token_filter_user_data, c->batch_index, t, b, plen ? pre : NULL, plen, v) == 0)
+                    continue;
                 float lp = row[v];
                 if (!isfinite(lp)) continue;
                 if (advanced && c->repetition_penalty > 1.0f && prefix_has(pre, plen, v))

@@ -42,12 +42,18 @@ typedef struct oracle_options {
 
 /* Decode constraints (DecodeConstraints, src/differentiable_beam.cpp:184-200).
  * min_length < 0 means "use options.min_length". */
+typedef int (*oracle_token_filter)(void* user_data, int batch_index, int step, int parent_beam,
+                                   const int32_t* prefix_tokens, int prefix_len, int token);
+
 typedef struct oracle_constraints {
     const uint8_t* banned_tokens;   /* [V] or NULL */
     const int32_t* forced_tokens;   /* [T] or NULL, -1 = free */
     int min_length;
     float repetition_penalty;       /* <= 1 disables */
     int no_repeat_ngram_size;       /* <= 0 disables */
+    oracle_token_filter token_filter; /* NULL or non-zero = allow (token_allowed_by_advanced_constraints, :339-349) */
+    void* token_filter_user_data;
+    int batch_index;
 } oracle_constraints;
 
 /* Output arrays of one decode (DecodeResult, :202-237). All are caller-owned.

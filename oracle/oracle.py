@@ -44,6 +44,10 @@ class _Opts(ctypes.Structure):
     ]
 
 
+TOKEN_FILTER_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                   ctypes.POINTER(ctypes.c_int32), ctypes.c_int, ctypes.c_int)
+
+
 class _Cons(ctypes.Structure):
     _fields_ = [
         ("banned_tokens", ctypes.c_void_p),
@@ -51,6 +55,9 @@ class _Cons(ctypes.Structure):
         ("min_length", ctypes.c_int),
         ("repetition_penalty", ctypes.c_float),
         ("no_repeat_ngram_size", ctypes.c_int),
+        ("token_filter", TOKEN_FILTER_FN),
+        ("token_filter_user_data", ctypes.c_void_p),
+        ("batch_index", ctypes.c_int),
     ]
 
 
@@ -108,7 +115,7 @@ class OracleLib:
 
     def decode(self, opts: _Opts, x: np.ndarray, steps: int, vocab: int, banned=None, forced=None,
                min_length: Optional[int] = None, repetition_penalty: float = 1.0,
-               no_repeat_ngram_size: int = 0) -> Dict[str, np.ndarray]:
+               no_repeat_ngram_size: int = 0, token_filter=None, batch_index: int = 0) -> Dict[str, np.ndarray]:
         x = np.ascontiguousarray(x, dtype=np.float32)
         K = opts.beam_size
         P = self.lib.oracle_pool_size(ctypes.byref(opts))
@@ -118,13 +125,14 @@ class OracleLib:
         cons_ptr = None
         keep = []
         if banned is not None or forced is not None or min_length is not None or \
-                repetition_penalty != 1.0 or no_repeat_ngram_size:
+                repetition_penalty != 1.0 or no_repeat_ngram_size or token_filter is not None:
             b = None if banned is None else np.ascontiguousarray(banned, dtype=np.uint8)
             f = None if forced is None else np.ascontiguousarray(forced, dtype=np.int32)
             keep += [b, f]
             c = _Cons(None if b is None else b.ctypes.data_as(ctypes.c_void_p),
                       None if f is None else f.ctypes.data_as(ctypes.c_void_p),
-                      -1 if min_length is None else min_length, repetition_penalty, no_repeat_ngram_size)
+                      -1 if min_length is None else min_length, repetition_penalty, no_repeat_ngram_size,
+                      TOKEN_FILTER_FN() if token_filter is None else token_filter, None, batch_index)
             cons_ptr = ctypes.byref(c)
         rc = self.lib.oracle_decode(ctypes.byref(opts), x.ctypes.data_as(ctypes.c_void_p), steps, vocab, cons_ptr,
                                     ctypes.byref(res))

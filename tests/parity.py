@@ -161,3 +161,16 @@ def config1_input():
     torch.manual_seed(0)
     x = torch.log_softmax(1.5 * torch.randn(4, 4, 4, 32000, dtype=torch.float32), dim=-1).numpy()
     return x, hashlib.sha256(x.tobytes()).hexdigest()
+
+
+def logging_filter(log):
+    """A deterministic token filter that depends on the beam's prefix and
+    appends every call (batch index, step, parent, prefix, token) to `log`;
+    returns the raw callable (wrap it in the binding's CFUNCTYPE)."""
+    def fn(user, batch_index, step, parent, prefix, prefix_len, token):
+        pre = tuple(prefix[i] for i in range(prefix_len)) if prefix_len else ()
+        log.append((batch_index, step, parent, pre, token))
+        last = pre[-1] if pre else 0
+        return int((token * 7 + step * 3 + parent + last) % 5 != 0)
+    return fn
+

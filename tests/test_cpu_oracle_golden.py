@@ -72,3 +72,36 @@ def test_oracle_live_against_reference_random(oracle_lib):
         want = dc.decode_and_read(ref, dc.Options(**opts), np.ascontiguousarray(x), T, V, **cons)
         got = oracle_lib.decode(o, x, T, V, **cons)
         assert_decode_equal(got, want, f"random {i}")
+
+
+def test_oracle_token_filter_matches_reference(oracle_lib):
+    """The token filter: same results and the same sequence of filter calls
+    (batch index, step, parent, prefix, token) as the reference library."""
+    import dbs_ctypes as dc
+    from oracle import TOKEN_FILTER_FN, reference_library_path
+    from parity import logging_filter
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+    ref = dc.load_library(path, device_api=False)
+    rng = np.random.default_rng(31)
+    for i in range(12):
+        T, K, V = int(rng.integers(1, 6)), int(rng.integers(1, 5)), int(rng.integers(5, 40))
+        x = (rng.standard_normal((T, K, V)) * 2).astype(np.float32)
+        x = x - np.log(np.exp(x).sum(-1, keepdims=True))
+        opts = dict(beam_size=K, eos_token=int(rng.integers(-1, V)), relaxed_pool_multiplier=2,
+                    length_penalty_alpha=0.3)
+        cons = dict(banned=(rng.random(V) < 0.1).astype(np.uint8), no_repeat_ngram_size=int(rng.integers(0, 3)),
+                    repetition_penalty=float(rng.choice([1.0, 1.4])), min_length=int(rng.integers(-1, 3)))
+        log_ref, log_orc = [], []
+        f_ref = dc.TOKEN_FILTER_FN(logging_filter(log_ref))
+        f_orc = TOKEN_FILTER_FN(logging_filter(log_orc))
+        dec = dc.Decoder(ref, dc.Options(**opts))
+        r = dec.decode_constrained_ex(np.ascontiguousarray(x), T, V, token_filter=f_ref, batch_index=3, **cons)
+        want = dc.read_result(ref, r)
+        ref.dbs_free_result(r)
+        dec.close()
+        got = oracle_lib.decode(oracle_lib.options(**opts), x, T, V, token_filter=f_orc, batch_index=3, **cons)
+        assert_decode_equal(got, want, f"filter case {i}")
+        assert log_orc == log_ref, f"filter case {i}: call sequence differs"
+

@@ -255,14 +255,29 @@ def test_validation_disabled_skips_pos_inf(libdbs, oracle_lib):
     assert_decode_equal(got, want, "+inf")
 
 
-def test_token_filter_is_rejected(libdbs):
-    T, K, V = 1, 2, 5
-    x = np.full((T, K, V), -1.0, dtype=np.float32)
-    dec = dc.Decoder(libdbs, dc.Options(beam_size=K))
-    cb = dc.TOKEN_FILTER_FN(lambda *a: 1)
-    with pytest.raises(dc.DBSError, match="token_filter"):
-        dec.decode_constrained_ex(x, T, V, token_filter=cb)
+@pytest.mark.parametrize("seed", range(3))
+def test_token_filter_matches_oracle(libdbs, oracle_lib, seed):
+    """Host token filter: same results as the oracle and the same sequence of
+    filter calls (which the CPU tests pin to the reference library)."""
+    from oracle import TOKEN_FILTER_FN
+    from parity import logging_filter
+    rng = np.random.default_rng(500 + seed)
+    T, K, V = 5, 3 + seed, 300
+    x = log_softmax_np(rng.standard_normal((T, K, V)).astype(np.float32) * 2)
+    opts = dict(beam_size=K, eos_token=4, relaxed_pool_multiplier=3, length_penalty_alpha=0.2)
+    cons = dict(banned=(rng.random(V) < 0.05).astype(np.uint8), forced=np.array([-1, 7, -1, -1, -1], np.int32),
+                min_length=2, repetition_penalty=1.3, no_repeat_ngram_size=2 if seed else 0)
+    log_got, log_want = [], []
+    f_got = dc.TOKEN_FILTER_FN(logging_filter(log_got))
+    f_want = TOKEN_FILTER_FN(logging_filter(log_want))
+    want = oracle_lib.decode(oracle_lib.options(**opts), x, T, V, token_filter=f_want, batch_index=seed, **cons)
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    r = dec.decode_constrained_ex(np.ascontiguousarray(x), T, V, token_filter=f_got, batch_index=seed, **cons)
+    got = dc.read_result(libdbs, r)
+    libdbs.dbs_free_result(r)
     dec.close()
+    assert_decode_equal(got, want, f"filter seed {seed}")
+    assert log_got == log_want
 
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
