@@ -1055,7 +1055,6 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         if (sh_any_unsafe) {
             // Rescan the unproven rows from HBM and merge in every dropped
             // candidate that beats the current N-th (rare path).
-            constexpr int kChunk = 2048;
             for (int k = 0; k < K; ++k) {
                 if (!s.unsafe[k]) continue;
                 if (tid == 0 && p.counters) atomicAdd(p.counters + 1, 1ull);
@@ -1072,15 +1071,30 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                 // in whenever the staging room could overflow (and at the end
                 // of the row); G only improves, so it is re-read per chunk.
                 const int stage_room = cand_cap - N;
-                for (int base = 0; base < V; base += kChunk) {
+                // chunks of 2048: staged candidates are merged only when the
+                // room could overflow, so G stays fresh without extra merges
+                constexpr int chunk = 2048;
+                for (int base = 0; base < V; base += chunk) {
                     const uint64_t gh = (N - 1 < M) ? chi[N - 1] : 0;
                     const uint64_t gl = (N - 1 < M) ? clo[N - 1] : 0;
-                    for (int v = base + tid; v < base + kChunk && v < V; v += NT) {
+                    const int lim = base + chunk < V ? base + chunk : V;
+                    // four loads in flight per thread before any of them is used
+                    for (int v0 = base + tid; v0 < lim; v0 += 4 * NT) {
+                        float lv[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int v = v0 + u * NT;
+                            lv[u] = v < lim ? __ldg(row + v) : -INFINITY;
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                        const int v = v0 + u * NT;
+                        if (v >= lim) continue;
                         if (forced >= 0 && v != forced) continue;
                         if (d.banned && d.banned[v]) continue;
                         if (eos_blocked && v == d.eos) continue;
                         if (p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v]) continue;
-                        float lp = row[v];
+                        float lp = lv[u];
                         if (!isfinite(lp)) continue;
                         const float lpc = __fadd_rn(lp, 0.0f);
                         if (lpc > m_lp || (lpc == m_lp && v <= m_tok)) continue;  // already listed
@@ -1103,12 +1117,13 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                             chi[N + pos] = h;
                             clo[N + pos] = l;
                         }
+                        }
                     }
                     __syncthreads();
                     const int staged = sh_stage;
                     __syncthreads();   // every thread holds the count before the next chunk stages
-                    const bool last_chunk = base + kChunk >= V;
-                    if (staged > 0 && (last_chunk || staged > stage_room - kChunk)) {
+                    const bool last_chunk = lim >= V;
+                    if (staged > 0 && (last_chunk || staged > stage_room - chunk)) {
                         if (N + staged > 1024) block_top_n_u128(chi, clo, N + staged, N, sel_hi, sel_lo, sel_cap);
                         else block_sort_desc_u128(chi, clo, N + staged);
                         for (int i = N + tid; i < N + staged; i += NT) { chi[i] = 0; clo[i] = 0; }
