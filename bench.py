@@ -57,7 +57,25 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override B (profiling a smaller case only; bench lines use the default 64)")
+    ap.add_argument("--pool-decode", type=int, default=None, metavar="MULT",
+                    help="profiling only: run the relaxed-pool device decode (relaxed_pool_multiplier MULT) "
+                         "--steps times on the workload and print no bench line")
     return ap.parse_args()
+
+
+def pool_decode_loop(args):
+    """Device decode with the relaxed pool and weights (the ABI's work per
+    call), for profiling the long-list row scan and the merge."""
+    import torch
+    import torch_dbs_extension as ext
+    B, T, K, V = (WORKLOAD[k] for k in "BTKV")
+    B = args.batch or B
+    x = make_inputs(torch, B, T, K, V, 0, torch.device("cuda", 0))
+    opts = ext.DBSOptions(**dict(OPTIONS, relaxed_pool_multiplier=args.pool_decode))
+    for _ in range(args.steps):
+        ext.device_decode(x, opts, with_pool=True, with_weights=True)
+    torch.cuda.synchronize()
+    print(f"pool decode x{args.steps} done")
 
 
 def measured_peaks():
@@ -249,6 +267,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.pool_decode:
+        pool_decode_loop(args)
         return
 
     import numpy as np
