@@ -2271,7 +2271,7 @@ constexpr size_t kMergeRankSmemBudget = 200 * 1024;
 
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T, int max_N,
                               bool need_sequences, cudaStream_t stream) {
-    if (!need_sequences && static_cast<int64_t>(max_K) * max_C <= 1024) {
+    if (!need_sequences && static_cast<int64_t>(max_K) * max_C <= 256) {
         const int tab_n = (p.Lmax + 1 <= 4096) ? p.Lmax + 1 : 0;
         int ring = max_T < kMergeRingMax ? max_T : kMergeRingMax;
         if (ring < 2) ring = 2;

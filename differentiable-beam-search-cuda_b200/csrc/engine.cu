@@ -180,6 +180,14 @@ struct HostTrace {
         on = enabled;
         if (on) t0 = last = std::chrono::steady_clock::now();
     }
+    // DBS_HOST_TRACE=<us> prints only calls slower than that many microseconds
+    static double threshold_us() {
+        static const double t = [] {
+            const char* v = std::getenv("DBS_HOST_TRACE");
+            return v ? std::atof(v) : 0.0;
+        }();
+        return t;
+    }
     void mark(const char* label) {
         if (!on) return;
         const auto now = std::chrono::steady_clock::now();
@@ -192,7 +200,7 @@ struct HostTrace {
     ~HostTrace() {
         if (!on) return;
         const double us = std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
-        std::fprintf(stderr, "[dbs %s] %.1fus%s\n", what, us, line.c_str());
+        if (us >= threshold_us()) std::fprintf(stderr, "[dbs %s] %.1fus%s\n", what, us, line.c_str());
     }
 };
 
@@ -571,13 +579,19 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     const size_t st_bytes = reinterpret_cast<char*>(p.counters + 4) - reinterpret_cast<char*>(p.status);
     const bool validate = opt.validate_inputs && ctl.scan;   // a merge-only call trusts its scan call
     if (validate) {
+        // the small validation kernel runs on the helper stream beside the row
+        // scan (both only read log_probs), so it costs the scan no time
+        std::lock_guard<std::mutex> lock(g_helper_mu);
+        Helper& hp = helper_locked();
+        check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
+        check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
         {
-            ProfileScope ps(kValidate, stream);
-            check_cuda(dbs_dev::launch_validate(p, stream), "validate kernel");
+            ProfileScope ps(kValidate, hp.side);
+            check_cuda(dbs_dev::launch_validate(p, hp.side), "validate kernel");
         }
-        check_cuda(cudaMemcpyAsync(lease.s->pinned + st_off, p.status, st_bytes, cudaMemcpyDeviceToHost, stream),
+        check_cuda(cudaMemcpyAsync(lease.s->pinned + st_off, p.status, st_bytes, cudaMemcpyDeviceToHost, hp.side),
                    "read status");
-        check_cuda(cudaEventRecord(lease.s->validated, stream), "cudaEventRecord");
+        check_cuda(cudaEventRecord(lease.s->validated, hp.side), "cudaEventRecord");
     }
     if (ctl.scan && scan_end > scan_begin) {
         ProfileScope ps(kRowScan, stream);
