@@ -326,7 +326,8 @@ std::vector<T> host_copy(const T* p, size_t n) {
 std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt, const float* x, int V,
                                         const std::vector<HostExample>& hx, const CallConstraints& cons,
                                         DBSDecoderHandle* stats_handle,
-                                        const dbs_host::TokenFilter* filter = nullptr) {
+                                        const dbs_host::TokenFilter* filter = nullptr,
+                                        const uint16_t* x16 = nullptr, bool x16_bf16 = false) {
     auto store = std::make_shared<ResultStore>();
     store->opt = opt;
     store->V = V;
@@ -370,7 +371,7 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
 
     CallStream cs(nullptr);
     cudaStream_t s = cs.s;
-    const bool x_dev = is_device_pointer(x);
+    const bool x_dev = x16 != nullptr || is_device_pointer(x);   // 16-bit inputs arrive on the device
     const size_t budget = device_budget_bytes();
     int b0 = 0;
     while (b0 < B) {
@@ -476,7 +477,10 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
             dbs_host::decode_filtered(opt, dx, V, spec[0], e.banned ? hb.data() : nullptr,
                                       e.forced ? hf.data() : nullptr, cons, o, CL, s, &st, *filter);
         } else {
-            dbs_host::decode(opt, dx, V, spec, cons, o, CL, true, true, s, &st, dbs_host::DecodeControl{});
+            dbs_host::DecodeControl ctl;
+            ctl.x16 = x16;
+            ctl.x16_bf16 = x16_bf16;
+            dbs_host::decode(opt, x16 ? nullptr : dx, V, spec, cons, o, CL, true, true, s, &st, ctl);
         }
         if (stats_handle) {
             stats_handle->last_row_rescans.store(static_cast<int64_t>(st.row_rescans));
@@ -958,13 +962,44 @@ static int decode_typed_impl(DBSDecoderHandle* handle, const void* log_probs, in
                              "stage typed log_probs");
         d_src = src.as<uint16_t>();
     }
-    DeviceBuffer wide(static_cast<size_t>(count) * 4, cs.s);
-    dbs_host::check_cuda(
-        dbs_dev::launch_widen_16(d_src, wide.as<float>(), count, data_type == DBS_DTYPE_BF16 ? 1 : 0, cs.s),
-        "widen kernel");
-    dbs_host::check_cuda(cudaStreamSynchronize(cs.s), "widen");
-    return batched ? dbs_decode_batch(handle, wide.as<float>(), batch, steps, vocab_size, 0, out_b)
-                   : dbs_decode(handle, wide.as<float>(), steps, vocab_size, out_r);
+    dbs_host::check_cuda(cudaStreamSynchronize(cs.s), "stage typed log_probs");
+    // the decode reads the 16-bit values natively (exact widening on load)
+    const int64_t t0 = now_ns();
+    const Options& opt = handle->options;
+    const int B = batched ? batch : 1;
+    const int64_t stride = static_cast<int64_t>(steps) * opt.beam_size * vocab_size;
+    std::vector<HostExample> hx(static_cast<size_t>(B));
+    for (int b = 0; b < B; ++b) {
+        check_example(opt, reinterpret_cast<const float*>(d_src), steps, vocab_size, opt.beam_size, opt.eos_token,
+                      nullptr);
+        hx[b].T = steps;
+        hx[b].K = opt.beam_size;
+        hx[b].k_stride = opt.beam_size;
+        hx[b].eos = opt.eos_token;
+        hx[b].min_length = opt.min_length;
+        hx[b].x_offset = stride * b;
+    }
+    auto store = run_decode(handle, opt, nullptr, vocab_size, hx, CallConstraints{}, handle, nullptr, d_src,
+                            data_type == DBS_DTYPE_BF16);
+    if (batched) {
+        auto br = std::make_unique<DBSBatchResultHandle>();
+        br->store = store;
+        br->items.resize(static_cast<size_t>(B));
+        for (int b = 0; b < B; ++b) {
+            br->items[b].store = store;
+            br->items[b].index = b;
+        }
+        record_decode(handle, store->ex[0], now_ns() - t0, 1, false);
+        *out_b = br.release();
+    } else {
+        auto r = std::make_unique<DBSResultHandle>();
+        r->store = store;
+        r->index = 0;
+        record_decode(handle, store->ex[0], now_ns() - t0, 1, false);
+        *out_r = r.release();
+    }
+    clear_error(handle);
+    return 0;
 }
 
 DBS_EXPORT int dbs_decode_typed(DBSDecoderHandle* handle, const void* log_probs, int data_type, int steps,

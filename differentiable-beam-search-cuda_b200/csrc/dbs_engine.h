@@ -62,6 +62,10 @@ struct ExampleDesc {
 // Options shared by every example of one call.
 struct DecodeParams {
     const float* x;
+    // 16-bit log-probs read natively instead of x (fp16 or bf16 bit
+    // patterns, widened exactly on load); nullptr for fp32 inputs
+    const uint16_t* x16;
+    int32_t x16_bf16;
     int32_t V;
     int32_t B;
     int64_t total_rows;

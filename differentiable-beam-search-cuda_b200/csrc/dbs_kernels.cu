@@ -6,6 +6,8 @@
 // (src/differentiable_beam.cpp:501-506, :1536-1537, :1666, :2108-2111).
 #include "dbs_engine.h"
 
+#include <cuda_fp16.h>
+
 #include <cfloat>
 #include <cmath>
 #include <cstdint>
@@ -29,6 +31,26 @@ __device__ __forceinline__ uint32_t ord_f32(float f) {
 __device__ __forceinline__ float unord_f32(uint32_t k) {
     uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
     return __uint_as_float(u);
+}
+
+// Exact widening of one fp16 / bf16 bit pattern.
+__device__ __forceinline__ float widen16(uint32_t h, bool bf16) {
+    return bf16 ? __uint_as_float(h << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+}
+
+// The 8 values of one 16-byte vector of 16-bit elements, in memory order.
+__device__ __forceinline__ void unpack8(const uint4& v, bool bf16, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = widen16(w[i] & 0xFFFFu, bf16);
+        f[2 * i + 1] = widen16(w[i] >> 16, bf16);
+    }
+}
+
+// Log-prob at element index i of the call's input, whatever its width.
+__device__ __forceinline__ float lp_at(const DecodeParams& p, int64_t i) {
+    return p.x16 ? widen16(__ldg(p.x16 + i), p.x16_bf16 != 0) : __ldg(p.x + i);
 }
 
 // Row list entry: larger key = better (lp desc, token asc).
@@ -299,7 +321,7 @@ __global__ void validate_kernel(DecodeParams p) {
         const int64_t rem = i - t * kv;
         const int64_t k = rem / V;
         const int64_t v = rem - k * V;
-        const float x = p.x[d.x_offset + (t * d.k_stride + k) * V + v];
+        const float x = lp_at(p, d.x_offset + (t * d.k_stride + k) * V + v);
         if (isnan(x) || x == INFINITY) bad = 1;
     }
     bad = __syncthreads_or(bad);
@@ -527,7 +549,7 @@ __device__ __noinline__ int warp_compact_select(uint64_t* buf, int cnt, int C, i
 }
 
 struct RowJob {
-    const float* row;
+    const void* row;    // first element of the row (fp32 or 16-bit)
     int64_t r;
     int64_t list_at;  // first list entry of the row
     int C;
@@ -541,6 +563,13 @@ struct RowJob {
     int chunks;
 };
 
+template <bool k16>
+__device__ __forceinline__ float row_lp(const RowJob& j, int i, bool bf16) {
+    if constexpr (k16) return widen16(static_cast<const uint16_t*>(j.row)[i], bf16);
+    else return static_cast<const float*>(j.row)[i];
+}
+
+template <bool k16>
 __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int& e) {
     while (r >= p.row_prefix[e + 1]) ++e;
     const ExampleDesc& d = p.desc[e];
@@ -548,7 +577,9 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     const int64_t lr = r - d.row_begin;
     const int t = static_cast<int>(lr / d.K);
     const int k = static_cast<int>(lr - static_cast<int64_t>(t) * d.K);
-    j.row = p.x + d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * p.V;
+    const int64_t elem = d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * p.V;
+    if constexpr (k16) j.row = p.x16 + elem;
+    else j.row = p.x + elem;
     j.r = r;
     j.list_at = d.list_offset + lr * d.C;
     j.C = d.C;
@@ -557,15 +588,18 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     j.eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
     j.banned = d.banned;
     j.allow = p.row_allow ? p.row_allow + static_cast<int64_t>(k) * p.V : nullptr;
+    // head elements up to the first 16-byte boundary, then 16-byte vectors
+    constexpr int kShift = k16 ? 1 : 2;   // log2(element bytes)
     const uintptr_t addr = reinterpret_cast<uintptr_t>(j.row);
-    int h = static_cast<int>(((16u - (addr & 15u)) & 15u) >> 2);
+    int h = static_cast<int>(((16u - (addr & 15u)) & 15u) >> kShift);
     if (h > p.V) h = p.V;
     j.h = h;
-    j.nv = (p.V - h) >> 2;
+    j.nv = (p.V - h) >> (4 - kShift);
     j.chunks = j.forced >= 0 ? 0 : (j.nv + kScanChunkF4 - 1) / kScanChunkF4;
     return j;
 }
 
+template <bool k16>
 __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(DecodeParams p, int capw, int speculate) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     constexpr unsigned FULL = 0xFFFFFFFFu;
@@ -582,6 +616,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     int* hist = reinterpret_cast<int*>(buf + capw);
     unsigned long long* err = p.counters ? p.counters + 3 : nullptr;
     unsigned long long* next_row = p.counters + 2;
+    const bool bf16 = p.x16_bf16 != 0;
     const unsigned lt_mask = (1u << lane) - 1u;
 
     if (lane == 0) {
@@ -602,7 +637,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     int64_t r_cur = claim();
     if (r_cur >= p.total_rows) return;
     e_cur = find_example(p.row_prefix, p.B, r_cur);
-    RowJob cur = make_job(p, r_cur, e_cur);
+    RowJob cur = make_job<k16>(p, r_cur, e_cur);
     e_nxt = e_cur;
     RowJob nxt = cur;
     bool have_nxt = false;
@@ -622,7 +657,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 if (!have_nxt) {
                     const int64_t rn = claim();
                     if (rn >= p.total_rows) break;
-                    nxt = make_job(p, rn, e_nxt);
+                    nxt = make_job<k16>(p, rn, e_nxt);
                     have_nxt = true;
                 }
                 issue_in_cur = false;
@@ -632,7 +667,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             const int s = static_cast<int>(n_issued % kScanStages);
             const int f0 = ic * kScanChunkF4;
             const int jnv = issue_in_cur ? cur.nv : nxt.nv;
-            const float* jbody = issue_in_cur ? cur.row + cur.h : nxt.row + nxt.h;
+            const RowJob& jj = issue_in_cur ? cur : nxt;
+            const char* jbody = static_cast<const char*>(jj.row) + (static_cast<size_t>(jj.h) << (k16 ? 1 : 2));
             const int nf = min(kScanChunkF4, jnv - f0);
             if (lane == 0) {
                 const uint32_t bytes = static_cast<uint32_t>(nf) * 16u;
@@ -660,7 +696,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
         if (j.forced >= 0) {
             // Forced step: only the forced token is a candidate of this row.
             if (lane == 0) {
-                const float lp = j.row[j.forced];
+                const float lp = row_lp<k16>(j, j.forced, bf16);
                 const bool ok = isfinite(lp) && !(j.banned && j.banned[j.forced]) &&
                                 !(j.eos_blocked && j.forced == j.eos) && !(j.allow && !j.allow[j.forced]);
                 if (ok) out[0] = list_key(lp, j.forced);
@@ -702,7 +738,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             };
             {  // unaligned head, first in token order
                 const bool in = lane < j.h;
-                const float lp = in ? j.row[lane] : -INFINITY;
+                const float lp = in ? row_lp<k16>(j, lane, bf16) : -INFINITY;
                 consider(in, lane, lp);
             }
             for (int c = 0; c < j.chunks; ++c) {
@@ -719,58 +755,111 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                     in[u] = idx < nf;
                     q[u] = in[u] ? st[idx] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
                 }
-                if (c == 0 && C <= 32) {
-                    // threshold bootstrap: C-th largest lane maximum over
-                    // finite, allowed elements of the first chunk
-                    float mx = -INFINITY;
+                if constexpr (!k16) {
+                    if (c == 0 && C <= 32) {
+                        // threshold bootstrap: C-th largest lane maximum over
+                        // finite, allowed elements of the first chunk
+                        float mx = -INFINITY;
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        if (!in[u]) continue;
-                        const int v0 = j.h + 4 * (u * 32 + lane);
-                        if (isfinite(q[u].x) && allowed(v0 + 0, q[u].x)) mx = fmaxf(mx, q[u].x);
-                        if (isfinite(q[u].y) && allowed(v0 + 1, q[u].y)) mx = fmaxf(mx, q[u].y);
-                        if (isfinite(q[u].z) && allowed(v0 + 2, q[u].z)) mx = fmaxf(mx, q[u].z);
-                        if (isfinite(q[u].w) && allowed(v0 + 3, q[u].w)) mx = fmaxf(mx, q[u].w);
-                    }
-                    const float kth = warp_kth_largest(mx, C, lane);
-                    if (kth > thr) thr = kth;
-                }
-                // the stage is in registers: let lane 0 refill it
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                ++n_used;
-                issue_more();
-                const int tok0 = j.h + 4 * c * kScanChunkF4;
-                // Fast path: one max and one vote for the lane's 16 values;
-                // survivors are rare once the threshold has settled.
-                float m16 = -INFINITY;
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    m16 = fmaxf(m16, fmaxf(fmaxf(q[u].x, q[u].y), fmaxf(q[u].z, q[u].w)));
-                if (!__any_sync(FULL, m16 >= thr)) {
-                    rej = fmaxf(rej, m16);
-                } else {
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        // a 128-value group without a survivor only feeds the bound
-                        const float m4 = fmaxf(fmaxf(q[u].x, q[u].y), fmaxf(q[u].z, q[u].w));
-                        if (!__any_sync(FULL, m4 >= thr)) {
-                            rej = fmaxf(rej, m4);
-                            continue;
+                        for (int u = 0; u < 4; ++u) {
+                            if (!in[u]) continue;
+                            const int v0 = j.h + 4 * (u * 32 + lane);
+                            if (isfinite(q[u].x) && allowed(v0 + 0, q[u].x)) mx = fmaxf(mx, q[u].x);
+                            if (isfinite(q[u].y) && allowed(v0 + 1, q[u].y)) mx = fmaxf(mx, q[u].y);
+                            if (isfinite(q[u].z) && allowed(v0 + 2, q[u].z)) mx = fmaxf(mx, q[u].z);
+                            if (isfinite(q[u].w) && allowed(v0 + 3, q[u].w)) mx = fmaxf(mx, q[u].w);
                         }
-                        const int v0 = tok0 + 4 * (u * 32 + lane);
-                        consider(in[u], v0 + 0, q[u].x);
-                        consider(in[u], v0 + 1, q[u].y);
-                        consider(in[u], v0 + 2, q[u].z);
-                        consider(in[u], v0 + 3, q[u].w);
-                        if (cnt > capw - 128 - 8) compact();
+                        const float kth = warp_kth_largest(mx, C, lane);
+                        if (kth > thr) thr = kth;
+                    }
+                    // the stage is in registers: let lane 0 refill it
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    ++n_used;
+                    issue_more();
+                    const int tok0 = j.h + 4 * c * kScanChunkF4;
+                    // Fast path: one max and one vote for the lane's 16 values;
+                    // survivors are rare once the threshold has settled.
+                    float m16 = -INFINITY;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        m16 = fmaxf(m16, fmaxf(fmaxf(q[u].x, q[u].y), fmaxf(q[u].z, q[u].w)));
+                    if (!__any_sync(FULL, m16 >= thr)) {
+                        rej = fmaxf(rej, m16);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            // a 128-value group without a survivor only feeds the bound
+                            const float m4 = fmaxf(fmaxf(q[u].x, q[u].y), fmaxf(q[u].z, q[u].w));
+                            if (!__any_sync(FULL, m4 >= thr)) {
+                                rej = fmaxf(rej, m4);
+                                continue;
+                            }
+                            const int v0 = tok0 + 4 * (u * 32 + lane);
+                            consider(in[u], v0 + 0, q[u].x);
+                            consider(in[u], v0 + 1, q[u].y);
+                            consider(in[u], v0 + 2, q[u].z);
+                            consider(in[u], v0 + 3, q[u].w);
+                            if (cnt > capw - 128 - 8) compact();
+                        }
+                    }
+                } else {
+                    // 16-bit elements: the lane's 4 vectors hold 32 values,
+                    // vector w covering tokens tok0 + 8 * (w * 32 + lane) + 0..7
+                    const uint4* q16 = reinterpret_cast<const uint4*>(q);
+                    float m8[4];
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        float f[8];
+                        unpack8(q16[w], bf16, f);
+                        m8[w] = -INFINITY;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) m8[w] = fmaxf(m8[w], in[w] ? f[i] : -INFINITY);
+                    }
+                    if (c == 0 && C <= 32) {
+                        float mx = -INFINITY;
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            if (!in[w]) continue;
+                            float f[8];
+                            unpack8(q16[w], bf16, f);
+                            const int v0 = j.h + 8 * (w * 32 + lane);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                if (isfinite(f[i]) && allowed(v0 + i, f[i])) mx = fmaxf(mx, f[i]);
+                        }
+                        const float kth = warp_kth_largest(mx, C, lane);
+                        if (kth > thr) thr = kth;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    ++n_used;
+                    issue_more();
+                    const int tok0 = j.h + 8 * c * kScanChunkF4;
+                    const float m32 = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3]));
+                    if (!__any_sync(FULL, m32 >= thr)) {
+                        rej = fmaxf(rej, m32);
+                    } else {
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            if (!__any_sync(FULL, m8[w] >= thr)) {
+                                rej = fmaxf(rej, m8[w]);
+                                continue;
+                            }
+                            float f[8];
+                            unpack8(q16[w], bf16, f);
+                            const int v0 = tok0 + 8 * (w * 32 + lane);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) consider(in[w], v0 + i, f[i]);
+                            if (cnt > capw - 256 - 8) compact();
+                        }
                     }
                 }
             }
             {  // unaligned tail, last in token order
-                const int t0 = j.h + 4 * j.nv;
+                const int t0 = j.h + (k16 ? 8 : 4) * j.nv;
                 const bool in = lane < p.V - t0;
-                const float lp = in ? j.row[t0 + lane] : -INFINITY;
+                const float lp = in ? row_lp<k16>(j, t0 + lane, bf16) : -INFINITY;
                 consider(in, t0 + lane, lp);
             }
             __syncwarp();
@@ -788,7 +877,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         in4[c] = t0 + c < p.V;
-                        v4[c] = in4[c] ? j.row[t0 + c] : -INFINITY;
+                        v4[c] = in4[c] ? row_lp<k16>(j, t0 + c, bf16) : -INFINITY;
                     }
 #pragma unroll
                     for (int c = 0; c < 4; ++c) consider(in4[c], t0 + c, v4[c]);
@@ -820,7 +909,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             const int64_t rn = have_nxt ? nxt.r : claim();
             if (!have_nxt) {
                 if (rn >= p.total_rows) return;
-                nxt = make_job(p, rn, e_nxt);
+                nxt = make_job<k16>(p, rn, e_nxt);
             }
             cur = nxt;
             have_nxt = false;
@@ -1060,7 +1149,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                 if (tid == 0 && p.counters) atomicAdd(p.counters + 1, 1ull);
                 const float pr = s.prev_raw[k];
                 const float inv = p.inv_pen[s.prev_len[k] + 1];
-                const float* row = p.x + d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
+                const int64_t row = d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
                 const int cnt = s.row_cnt[k];
                 const uint64_t last = p.lists[d.list_offset + (row0 - d.row_begin + k) * C + (cnt - 1)];
                 const float m_lp = list_lp(last);
@@ -1084,7 +1173,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
                             const int v = v0 + u * NT;
-                            lv[u] = v < lim ? __ldg(row + v) : -INFINITY;
+                            lv[u] = v < lim ? lp_at(p, row + v) : -INFINITY;
                         }
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
@@ -1329,7 +1418,7 @@ __device__ void rank_merge_rescan(const DecodeParams& p, const ExampleDesc& d, i
             if (safe) continue;   // uniform: every thread reads the same staged top-N
         }
         if (tid == 0 && p.counters) atomicAdd(p.counters + 1, 1ull);
-        const float* row = p.x + d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
+        const int64_t row = d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
         const uint64_t last = L[k * C + cnt[k] - 1];
         const float m_lp = list_lp(last);
         const int m_tok = list_token(last);
@@ -1340,7 +1429,8 @@ __device__ void rank_merge_rescan(const DecodeParams& p, const ExampleDesc& d, i
                 if (forced >= 0 && v != forced) continue;
                 if (d.banned && d.banned[v]) continue;
                 if (eos_blocked && v == d.eos) continue;
-                const float lp = row[v];
+                if (p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v]) continue;
+                const float lp = lp_at(p, row + v);
                 if (!isfinite(lp)) continue;
                 const float lpc = __fadd_rn(lp, 0.0f);
                 if (lpc > m_lp || (lpc == m_lp && v <= m_tok)) continue;   // already listed
@@ -2224,10 +2314,14 @@ static size_t row_scan_smem(int capw) {
 cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream, int64_t rows) {
     if (rows < 0) rows = p.total_rows;
     if (rows <= 0) return cudaSuccess;
-    const int capw = row_scan_capw(max_C);
+    const bool k16 = p.x16 != nullptr;
+    // 16-bit rows append up to 256 values between compaction checks
+    const int capw = row_scan_capw(max_C) + (k16 ? 128 : 0);
+    const void* fn = k16 ? reinterpret_cast<const void*>(row_scan_kernel<true>)
+                         : reinterpret_cast<const void*>(row_scan_kernel<false>);
     const int threads = kScanWarpsPerCta * 32;
     const size_t smem = row_scan_smem(capw);
-    cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(row_scan_kernel), smem);
+    cudaError_t err = ensure_dynamic_smem(fn, smem);
     if (err != cudaSuccess) return err;
     int dev = 0;
     err = cudaGetDevice(&dev);
@@ -2236,13 +2330,13 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     {
         std::lock_guard<std::mutex> lock(g_attr_mu);
         for (auto& e : g_row_scan_occ)
-            if (std::get<0>(e) == dev && std::get<1>(e) == smem) per_sm = std::get<2>(e);
+            if (std::get<0>(e) == dev + (k16 ? 1 << 20 : 0) && std::get<1>(e) == smem) per_sm = std::get<2>(e);
     }
     if (per_sm < 0) {
-        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_scan_kernel, threads, smem);
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
         if (err != cudaSuccess) return err;
         std::lock_guard<std::mutex> lock(g_attr_mu);
-        g_row_scan_occ.emplace_back(dev, smem, per_sm);
+        g_row_scan_occ.emplace_back(dev + (k16 ? 1 << 20 : 0), smem, per_sm);
     }
     if (per_sm < 1) per_sm = 1;
     int64_t ctas = static_cast<int64_t>(num_sms) * per_sm;
@@ -2251,7 +2345,8 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     // The speculative threshold pays off over several rows per warp; with
     // few rows a failed guess (a second read of the row) only adds to the tail.
     const int speculate = (max_C > 32 && rows >= 4 * ctas * kScanWarpsPerCta) ? 1 : 0;
-    row_scan_kernel<<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw, speculate);
+    if (k16) row_scan_kernel<true><<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw, speculate);
+    else row_scan_kernel<false><<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw, speculate);
     return cudaGetLastError();
 }
 

@@ -539,6 +539,8 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     p.force_seq = ctl.force_seq ? 1 : 0;
 
     p.x = d_x;
+    p.x16 = ctl.x16;
+    p.x16_bf16 = ctl.x16_bf16 ? 1 : 0;
     p.V = V;
     p.B = B;
     p.total_rows = rows;

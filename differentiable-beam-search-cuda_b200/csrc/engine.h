@@ -142,6 +142,9 @@ struct DecodeControl {
     const uint8_t* row_allow = nullptr;
     bool force_seq = false;
     bool weights = true;
+    // 16-bit log-probs read natively (d_x is then unused)
+    const uint16_t* x16 = nullptr;
+    bool x16_bf16 = false;
 };
 
 // Host token filter of the reference's advanced constraints

@@ -306,6 +306,40 @@ def test_typed_decode_widening(libdbs, oracle_lib, dtype):
     assert_decode_equal(got, want, dtype)
 
 
+def _to16(x, dtype):
+    if dtype == "f16":
+        h = x.astype(np.float16)
+        return h.view(np.uint16), h.astype(np.float32), dc.DBS_DTYPE_F16
+    bits = (x.view(np.uint32) >> 16).astype(np.uint16)
+    return bits, (bits.astype(np.uint32) << 16).view(np.float32), dc.DBS_DTYPE_BF16
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("K,V,mult,B", [(8, 32003, 1, 5), (8, 32000, 8, 3), (4, 50257, 8, 2), (16, 4099, 4, 40)])
+def test_typed_batch_reads_16bit_natively(libdbs, oracle_lib, dtype, K, V, mult, B):
+    # vocab-sized rows with odd lengths (unaligned 16-bit heads and tails),
+    # short (C = K) and long (C = P > 32) row lists, and a batch large enough
+    # for the long-list speculation; compared with the oracle on the widened
+    # values, which are exact
+    rng = np.random.default_rng(V + K)
+    T = 6
+    bias = -1.1 * np.log(np.arange(V, dtype=np.float32) + 1.0)
+    x = log_softmax_np(2.0 * rng.standard_normal((B, T, K, V)).astype(np.float32) + bias)
+    bits, wide, code = _to16(x, dtype)
+    opts = dict(beam_size=K, relaxed_pool_multiplier=mult, eos_token=2, length_penalty_alpha=0.2)
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    br = ctypes.c_void_p()
+    rc = libdbs.dbs_decode_batch_typed(dec.h, np.ascontiguousarray(bits).ctypes.data_as(ctypes.c_void_p), code, B, T,
+                                       V, 0, ctypes.byref(br))
+    assert rc == 0, libdbs.dbs_last_error(dec.h)
+    for b in range(0, B, max(1, B // 4)):
+        want = _oracle_decode(oracle_lib, opts, np.ascontiguousarray(wide[b]), T, V, {})
+        got = dc.read_result(libdbs, libdbs.dbs_batch_result_at(br, b))
+        assert_decode_equal(got, want, f"{dtype} example {b}")
+    libdbs.dbs_free_batch_result(br)
+    dec.close()
+
+
 def test_model_step_decode(libdbs):
     # the reference's own model-step case (tests/dbs_tests.cpp:158-209)
     @dc.MODEL_STEP_FN
