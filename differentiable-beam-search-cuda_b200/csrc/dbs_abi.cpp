@@ -327,7 +327,8 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
                                         const std::vector<HostExample>& hx, const CallConstraints& cons,
                                         DBSDecoderHandle* stats_handle,
                                         const dbs_host::TokenFilter* filter = nullptr,
-                                        const uint16_t* x16 = nullptr, bool x16_bf16 = false) {
+                                        const uint16_t* x16 = nullptr, bool x16_bf16 = false,
+                                        const dbs_host::StepRows* rows = nullptr) {
     auto store = std::make_shared<ResultStore>();
     store->opt = opt;
     store->V = V;
@@ -371,7 +372,8 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
 
     CallStream cs(nullptr);
     cudaStream_t s = cs.s;
-    const bool x_dev = x16 != nullptr || is_device_pointer(x);   // 16-bit inputs arrive on the device
+    // 16-bit inputs arrive on the device; model-step rows are produced there
+    const bool x_dev = x16 != nullptr || rows != nullptr || is_device_pointer(x);
     const size_t budget = device_budget_bytes();
     int b0 = 0;
     while (b0 < B) {
@@ -468,7 +470,13 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
         o.final_scores = reinterpret_cast<float*>(take(nfin * 4));
         const float* dx = x_dev ? x : xs.as<float>();
         dbs_host::DecodeStats st;
-        if (filter) {
+        if (rows) {
+            // one example (dbs_decode_model_steps): rows arrive step by step
+            DeviceBuffer xr(static_cast<size_t>(spec[0].T) * spec[0].K * V * sizeof(float), s);
+            spec[0].x_offset = 0;
+            spec[0].k_stride = spec[0].K;
+            dbs_host::decode_model_steps(opt, xr.as<float>(), V, spec[0], o, CL, s, &st, *rows);
+        } else if (filter) {
             // one example (dbs_decode_constrained_ex): the host checks need the
             // constraint arrays in host memory
             const HostExample& e = hx[b0];
@@ -1055,36 +1063,45 @@ DBS_EXPORT int dbs_decode_model_steps_with_workspace(DBSDecoderHandle* handle, D
         std::lock_guard<std::mutex> lock(workspace->mutex);
         workspace->f32.assign(total, -std::numeric_limits<float>::infinity());
         workspace->i32.assign(static_cast<size_t>(K), -1);
-        std::vector<float> prev_scores(static_cast<size_t>(K), 0.0f);
+        std::vector<float> prev_scores_buf(static_cast<size_t>(K), 0.0f);
         const Options& opt = handle->options;
-        for (int t = 0; t < steps; ++t) {
+        // The callback fills step t's rows from the previous step's tokens
+        // and the final scores of the decode so far; the device decodes one
+        // step per launch and keeps the beams between launches, so the work
+        // grows linearly with the steps (the reference re-decodes every
+        // prefix).
+        dbs_host::StepRows rows = [&](int t, const int32_t* prev_tokens, const float* prev_scores, float* d_rows) {
             float* row = workspace->f32.data() + static_cast<size_t>(t) * row_count;
-            const int rc = step_fn(user_data, batch_index, t, workspace->i32.data(), prev_scores.data(), K,
+            for (int k = 0; k < K; ++k) {
+                workspace->i32[static_cast<size_t>(k)] = prev_tokens[k];
+                prev_scores_buf[static_cast<size_t>(k)] = prev_scores[k];
+            }
+            const int rc = step_fn(user_data, batch_index, t, workspace->i32.data(), prev_scores_buf.data(), K,
                                    vocab_size, row);
             if (rc != 0) throw std::runtime_error("model step callback returned non-zero status");
-            if (t + 1 < steps) {
-                HostExample e;
-                e.T = t + 1;
-                e.K = K;
-                e.k_stride = K;
-                e.eos = opt.eos_token;
-                e.min_length = opt.min_length;
-                check_example(opt, workspace->f32.data(), t + 1, vocab_size, K, opt.eos_token, nullptr);
-                auto part = run_decode(handle, opt, workspace->f32.data(), vocab_size, {e}, CallConstraints{}, handle);
-                for (int k = 0; k < K; ++k) {
-                    workspace->i32[static_cast<size_t>(k)] = part->tokens[static_cast<size_t>(t) * K + k];
-                    prev_scores[static_cast<size_t>(k)] = part->final_scores[static_cast<size_t>(k)];
+            if (opt.validate_inputs) {
+                // the reference validates every prefix it decodes (steps
+                // 0..t), sampling 1000 evenly spaced elements of each
+                // (validate_logprob_tensor, src/differentiable_beam.cpp:385-402)
+                const size_t count = static_cast<size_t>(t + 1) * row_count;
+                const size_t stride = count > 1000 ? count / 1000 : 1;
+                for (size_t i = 0; i < count; i += stride) {
+                    const float v = workspace->f32[i];
+                    if (std::isnan(v) || v == std::numeric_limits<float>::infinity())
+                        throw std::invalid_argument("log_probs contains NaN or +Inf");
                 }
             }
-        }
+            dbs_host::check_cuda(cudaMemcpy(d_rows, row, row_count * sizeof(float), cudaMemcpyHostToDevice),
+                                 "upload model step rows");
+        };
         HostExample e;
         e.T = steps;
         e.K = K;
         e.k_stride = K;
         e.eos = opt.eos_token;
         e.min_length = opt.min_length;
-        check_example(opt, workspace->f32.data(), steps, vocab_size, K, opt.eos_token, nullptr);
-        auto store = run_decode(handle, opt, workspace->f32.data(), vocab_size, {e}, CallConstraints{}, handle);
+        auto store = run_decode(handle, opt, nullptr, vocab_size, {e}, CallConstraints{}, handle, nullptr, nullptr,
+                                false, &rows);
         auto r = std::make_unique<DBSResultHandle>();
         r->store = store;
         record_decode(handle, store->ex[0], now_ns() - t0, 1, true);

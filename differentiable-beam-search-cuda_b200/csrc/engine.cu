@@ -907,4 +907,55 @@ void decode_filtered(const Options& opt, const float* d_x, int V, const ExampleS
     }
 }
 
+void decode_model_steps(const Options& opt, float* d_x, int V, const ExampleSpec& ex, const Outputs& out,
+                        const Layout& layout, cudaStream_t stream, DecodeStats* stats, const StepRows& rows) {
+    const int T = ex.T, K = ex.K;
+    const bool pool = out.pool_scores != nullptr;
+    const int C = list_capacity(opt, K, pool, true);
+    const int64_t nrows = static_cast<int64_t>(T) * K;
+    StepBuffer lists(static_cast<size_t>(nrows) * C * sizeof(uint64_t), stream);
+    StepBuffer counts(static_cast<size_t>(nrows) * sizeof(int32_t), stream);
+    StepBuffer bounds(static_cast<size_t>(nrows) * sizeof(float), stream);
+    StepBuffer state(static_cast<size_t>(4) * K * sizeof(float), stream);
+    StepBuffer seq(static_cast<size_t>(3) * K * T * sizeof(int32_t), stream);
+    std::vector<float> h_state(static_cast<size_t>(4) * K);
+    std::vector<int32_t> tokens(static_cast<size_t>(K), -1);
+    std::vector<float> scores(static_cast<size_t>(K) + 1, 0.0f);
+    for (int t = 0; t < T; ++t) {
+        if (t > 0) {
+            // tokens of step t-1 and the final scores of the decode so far
+            // (finalisation, src/differentiable_beam.cpp:1661-1667)
+            check_cuda(cudaMemcpyAsync(tokens.data(), out.tokens + static_cast<size_t>(t - 1) * K,
+                                       sizeof(int32_t) * K, cudaMemcpyDeviceToHost, stream), "read tokens");
+            check_cuda(cudaMemcpyAsync(h_state.data(), state.ptr, h_state.size() * sizeof(float),
+                                       cudaMemcpyDeviceToHost, stream), "read beam state");
+            check_cuda(cudaStreamSynchronize(stream), "model step");
+            for (int k = 0; k < K; ++k) {
+                int len = 0;
+                std::memcpy(&len, &h_state[K + k], sizeof(int));
+                scores[k] = h_state[k] / gnmt_host(opt.length_penalty_alpha, len < 1 ? 1 : len);
+            }
+        }
+        rows(t, tokens.data(), scores.data(), d_x + static_cast<size_t>(t) * K * V);
+        DecodeControl ctl;
+        ctl.synchronize = true;
+        ctl.lists = lists.as<uint64_t>();
+        ctl.list_count = counts.as<int32_t>();
+        ctl.list_bound = bounds.as<float>();
+        ctl.scan_begin = static_cast<int64_t>(t) * K;
+        ctl.scan_end = static_cast<int64_t>(t + 1) * K;
+        ctl.t_begin = t;
+        ctl.t_end = t + 1;
+        ctl.merge_state = state.as<float>();
+        ctl.seq_scratch = seq.as<int32_t>();
+        ctl.force_seq = true;   // the merge that keeps its state between launches
+        ctl.weights = t + 1 == T;
+        Options step_opt = opt;
+        step_opt.validate_inputs = 0;   // rows beyond step t are not written yet; the caller validates
+        decode(step_opt, d_x, V, {ex}, CallConstraints{}, out, layout, pool, out.weights != nullptr, stream, stats,
+               ctl);
+    }
+}
+
 }  // namespace dbs_host
+

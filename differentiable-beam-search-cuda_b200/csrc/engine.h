@@ -163,6 +163,20 @@ void decode_filtered(const Options& opt, const float* d_x, int V, const ExampleS
                      const int32_t* h_forced, const CallConstraints& cons, const Outputs& out, const Layout& layout,
                      cudaStream_t stream, DecodeStats* stats, const TokenFilter& filter);
 
+// Source of a model-driven decode's log-probs: fills step t's [K][V] rows at
+// d_rows (device) from the previous step's tokens and the final scores of the
+// decode so far (the reference's DBSModelStepFn contract).
+using StepRows = std::function<void(int step, const int32_t* prev_tokens, const float* prev_scores, float* d_rows)>;
+
+// Decode of one example whose rows arrive one step at a time (the model-step
+// API): each step's rows are produced after the previous step is merged, the
+// device scans and merges that step, and the beams carry over in device
+// memory, so the work is linear in the number of steps. d_x holds [T][K][V]
+// (row (t, k) at (t * K + k) * V) and is filled by `rows`; input validation
+// is the caller's (the rows exist on the host first). Synchronous.
+void decode_model_steps(const Options& opt, float* d_x, int V, const ExampleSpec& ex, const Outputs& out,
+                        const Layout& layout, cudaStream_t stream, DecodeStats* stats, const StepRows& rows);
+
 // Row-list capacity C of one example (the per-row candidate list length the
 // row scan keeps): N = P in pool mode else K, plus slack with sequence
 // constraints, cut to the merge's per-step capacity.

@@ -340,6 +340,62 @@ def test_typed_batch_reads_16bit_natively(libdbs, oracle_lib, dtype, K, V, mult,
     dec.close()
 
 
+@pytest.mark.parametrize("K,V,T,alpha", [(4, 300, 7, 0.0), (8, 2000, 12, 0.6)])
+def test_model_step_decode_matches_prefix_decodes(libdbs, oracle_lib, K, V, T, alpha):
+    # The reference fills step t from the tokens of step t-1 and the final
+    # scores of a decode of steps 0..t-1 (src/differentiable_beam.cpp:
+    # 3506-3586); the oracle side below does exactly that, the product decodes
+    # incrementally. Both the callbacks' arguments and the results must match.
+    rng = np.random.default_rng(K * V + T)
+    base = rng.standard_normal((T, K, V)).astype(np.float32)
+
+    def make_step(log):
+        @dc.MODEL_STEP_FN
+        def step(user, batch, t, prev_tokens, prev_scores, k_, v_, out):
+            toks = [prev_tokens[k] for k in range(K)]
+            scs = [prev_scores[k] for k in range(K)]
+            log.append((t, tuple(toks), tuple(np.float32(v) for v in scs)))
+            row = base[t].copy()
+            for k in range(K):
+                if toks[k] >= 0:
+                    row[k, (toks[k] * 7 + 3) % V] += 3.0
+                row[k] += np.float32(0.01) * np.float32(scs[k])
+            row = log_softmax_np(row)
+            ctypes.memmove(out, row.ctypes.data, row.nbytes)
+            return 0
+        return step
+
+    opts = dict(beam_size=K, eos_token=2, length_penalty_alpha=alpha, relaxed_pool_multiplier=2)
+    log_got = []
+    cb = make_step(log_got)
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    r = ctypes.c_void_p()
+    assert libdbs.dbs_decode_model_steps(dec.h, cb, None, 0, T, V, ctypes.byref(r)) == 0, libdbs.dbs_last_error(dec.h)
+    got = dc.read_result(libdbs, r)
+    libdbs.dbs_free_result(r)
+    dec.close()
+
+    # oracle: the reference's procedure, one prefix decode per step
+    log_want = []
+    fill = make_step(log_want)
+    x = np.zeros((T, K, V), dtype=np.float32)
+    toks = np.full(K, -1, np.int32)
+    scs = np.zeros(K, np.float32)
+    o = oracle_lib.options(**opts)
+    for t in range(T):
+        buf = (ctypes.c_float * (K * V))()
+        fill(None, 0, t, toks.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+             scs.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), K, V, buf)
+        x[t] = np.frombuffer(buf, dtype=np.float32).reshape(K, V)
+        if t + 1 < T:
+            part = oracle_lib.decode(o, np.ascontiguousarray(x[:t + 1]), t + 1, V)
+            toks = part["tokens"][t * K:(t + 1) * K].astype(np.int32).copy()
+            scs = part["final_scores"].astype(np.float32).copy()
+    want = oracle_lib.decode(o, x, T, V)
+    assert log_got == log_want
+    assert_decode_equal(got, want, "model steps")
+
+
 def test_model_step_decode(libdbs):
     # the reference's own model-step case (tests/dbs_tests.cpp:158-209)
     @dc.MODEL_STEP_FN
