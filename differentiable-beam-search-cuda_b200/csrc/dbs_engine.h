@@ -184,7 +184,6 @@ cudaError_t noalloc_prepare();
 
 // Limits of this implementation.
 constexpr int kMaxMergeCandidates = 8192;   // K * C per step handled by one CTA
-constexpr int kRowScanThreads = 256;
 constexpr int kMergeThreads = 512;
 
 }  // namespace dbs_dev
