@@ -246,18 +246,17 @@ def row_shards(rows: int, world: int):
 
 
 def decode_row_sharded(x4: torch.Tensor, options: DBSOptions, with_pool: bool = False, with_weights: bool = False,
-                       group=None, all_gather=None) -> DeviceTrace:
+                       group=None) -> DeviceTrace:
     """Decode a uniform batch whose log-probs every rank holds, with the row
-    scan split across the ranks of `group`: each rank scans its contiguous
-    share of the B*T*K rows, one all-gather assembles every row's candidate
-    list on every rank, and each rank runs the (sequential, small) step merge
-    itself. Every rank returns the trace dbs_device_decode_batch would
-    produce. `all_gather(out, inp)` defaults to
-    torch.distributed.all_gather_into_tensor on `group`."""
+    scan split across the ranks of `group` (NCCL): each rank scans its
+    contiguous share of the B*T*K rows, one all-gather assembles every row's
+    candidate list on every rank, and each rank runs the (sequential, small)
+    step merge itself. Every rank returns the trace dbs_device_decode_batch
+    would produce."""
     import torch.distributed as dist
     B, T, K, V = (int(s) for s in x4.shape)
-    world = dist.get_world_size(group) if all_gather is None else all_gather.world
-    rank = dist.get_rank(group) if all_gather is None else all_gather.rank
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
     lib = _library()
     h = _handle(options)
     cap = ctypes.c_int()
@@ -276,10 +275,8 @@ def decode_row_sharded(x4: torch.Tensor, options: DBSOptions, with_pool: bool = 
                                       _vp(bounds), stream)
     _check(rc, h, "dbs_decode")
     sl = slice(rank * per, (rank + 1) * per)
-    gather = all_gather if all_gather is not None else (
-        lambda out, inp: dist.all_gather_into_tensor(out, inp, group=group))
     for t in (lists, counts, bounds):
-        gather(t, t[sl].clone())
+        dist.all_gather_into_tensor(t, t[sl].clone(), group=group)
     P = max(K, K * options.relaxed_pool_multiplier)
     trace = DeviceTrace(B, T, K, dev, with_pool=with_pool, P=P, with_weights=with_weights)
     outs = trace.struct()
