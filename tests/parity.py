@@ -5,7 +5,7 @@ Gates (the reference's contract for this path):
   * raw / ranking / final scores: bit-exact (same IEEE float operations);
   * selected weights within 3e-3 and relaxed weights within 5e-3 (the
     reference's own scalar-vs-SIMD tolerances, src/differentiable_beam.cpp:
-    2545-2548), gradient values within 1e-5 relative (north-star gate) when
+    2545-2548), gradient values within 1e-5 relative (the required gate) when
     they depend only on grad_final, 8e-3 otherwise (:2551-2560).
 """
 from __future__ import annotations
