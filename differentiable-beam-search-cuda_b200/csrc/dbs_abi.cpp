@@ -22,10 +22,6 @@
 #include "dbs_device.h"
 #include "engine.h"
 
-namespace dbs_dev {
-cudaError_t launch_widen_16(const uint16_t* src, float* dst, int64_t count, int is_bf16, cudaStream_t stream);
-}
-
 using dbs_host::CallConstraints;
 using dbs_host::ExampleSpec;
 using dbs_host::InvalidArgument;

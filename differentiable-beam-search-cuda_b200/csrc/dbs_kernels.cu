@@ -2483,53 +2483,6 @@ cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_
     return cudaGetLastError();
 }
 
-}  // namespace dbs_dev
-
-namespace dbs_dev {
-
-// Exact widening of IEEE binary16 / bfloat16 bit patterns to fp32
-// (the reference converts on the host: src/differentiable_beam.cpp:3275-3305).
-__global__ void widen_16_kernel(const uint16_t* __restrict__ src, float* __restrict__ dst, int64_t count,
-                                int is_bf16) {
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
-        const uint32_t h = src[i];
-        uint32_t out;
-        if (is_bf16) {
-            out = h << 16;
-        } else {
-            const uint32_t sign = (h & 0x8000u) << 16;
-            const uint32_t exp = (h >> 10) & 0x1Fu;
-            const uint32_t mant = h & 0x3FFu;
-            if (exp == 0) {
-                if (mant == 0) {
-                    out = sign;
-                } else {
-                    // subnormal half: value = mant * 2^-24, renormalise
-                    const int shift = __clz(mant) - 21;      // leading zeros within 10 bits
-                    const uint32_t m = (mant << shift) & 0x3FFu;
-                    const uint32_t e = 113u - static_cast<uint32_t>(shift);
-                    out = sign | (e << 23) | (m << 13);
-                }
-            } else if (exp == 31) {
-                out = sign | 0x7F800000u | (mant << 13);
-            } else {
-                out = sign | ((exp + 112u) << 23) | (mant << 13);
-            }
-        }
-        dst[i] = __uint_as_float(out);
-    }
-}
-
-cudaError_t launch_widen_16(const uint16_t* src, float* dst, int64_t count, int is_bf16, cudaStream_t stream) {
-    if (count <= 0) return cudaSuccess;
-    int64_t blocks = (count + 255) / 256;
-    if (blocks > 65535) blocks = 65535;
-    cudaError_t err = prefer_shared(reinterpret_cast<const void*>(widen_16_kernel));
-    if (err != cudaSuccess) return err;
-    widen_16_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, count, is_bf16);
-    return cudaGetLastError();
-}
 
 // ---------------------------------------------------------------------------
 // Sparse backward that allocates nothing (dbs_device_backward_sparse_noalloc).

@@ -416,3 +416,46 @@ def test_model_step_decode(libdbs):
     assert dec.stats().used_model_step_callback == 1
     libdbs.dbs_free_result(r)
     dec.close()
+
+
+def test_concurrent_calls_on_one_handle(libdbs, oracle_lib):
+    """The reference's decoder is safe to share between threads; several host
+    threads decoding (and running the backward) on one handle at once must get
+    the results they get one at a time."""
+    import threading
+    rng = np.random.default_rng(8)
+    T, K, V = 5, 4, 3000
+    xs = [log_softmax_np(rng.standard_normal((T, K, V)).astype(np.float32) * 2) for _ in range(8)]
+    opts = dict(beam_size=K, eos_token=2, length_penalty_alpha=0.2, relaxed_pool_multiplier=4)
+    gf = np.ones(K, dtype=np.float32)
+    want = [dc.decode_and_read(libdbs, dc.Options(**opts), x, T, V, grad_final=gf) for x in xs]
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    got = [None] * (3 * len(xs))
+    errors = []
+
+    def work(tid):
+        try:
+            for rep in range(3):
+                i = (tid + rep * 4) % len(xs)
+                r = dec.decode(np.ascontiguousarray(xs[i]), T, V)
+                out = dc.read_result(libdbs, r)
+                b = dec.backward(r, None, None, gf, mode="sparse")
+                out["backward"] = dc.read_backward(libdbs, b, K=K)
+                libdbs.dbs_free_backward(b)
+                libdbs.dbs_free_result(r)
+                got[tid * 3 + rep] = (i, out)
+        except Exception as exc:   # surfaced by the main thread
+            errors.append(exc)
+
+    threads = [threading.Thread(target=work, args=(t,)) for t in range(8)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    dec.close()
+    assert not errors, errors
+    for entry in got:
+        i, out = entry
+        assert_decode_equal(out, want[i], f"thread result {i}")
+        assert np.array_equal(out["backward"]["indices"], want[i]["backward"]["indices"])
+        assert np.array_equal(out["backward"]["values"], want[i]["backward"]["values"])
