@@ -39,6 +39,13 @@ def test_reference_abi_symbol_set_and_version_node(libdbs):
     assert len(dc.ABI_FUNCTIONS) == 76
 
 
+def test_soname_matches_the_reference(libdbs):
+    # binaries linked against the reference look for libdbs.so.10
+    out = subprocess.run(["readelf", "-d", libdbs._name], capture_output=True, text=True, check=True)
+    assert "Library soname: [libdbs.so.10]" in out.stdout
+    assert os.path.exists(os.path.join(os.path.dirname(libdbs._name), "libdbs.so.10"))
+
+
 def test_version_and_stub_entry_points(libdbs):
     assert libdbs.dbs_abi_version() == 10
     assert libdbs.dbs_version_string() == b"1.0.0"
