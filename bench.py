@@ -19,6 +19,10 @@ Metric: log-prob elements per second, B*T*K*V / (forward + backward time).
   * cpu_baseline -- the reference's CPU library (compiled from its source into
               oracle/_ref) on the same workload, all host threads.
 
+Warm-up: at least --warmup steps and at least --warmup-seconds (5 s) of
+steps, since a freshly started GPU runs the first seconds measurably slower;
+the line's "warmup" is the number of warm-up steps run.
+
 `--impl reference` times only the reference CPU arm (rank 0).
 Multi-GPU (torchrun): every rank runs its own batch (weak scaling, no
 collective on the data path); value = all ranks' elements / max rank time.
@@ -54,6 +58,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--warmup-seconds", type=float, default=5.0,
+                    help="untimed warm-up lasts at least this long (and at least --warmup steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override B (profiling a smaller case only; bench lines use the default 64)")
@@ -299,9 +305,23 @@ def main():
         y = ext.final_scores(x, opts)
         y.sum().backward()
 
-    for _ in range(max(3, args.warmup)):
+    # at least W steps and at least a few seconds: a freshly started GPU runs
+    # the first seconds of this workload measurably slower
+    warm_steps = 0
+    t_warm = time.perf_counter()
+    while warm_steps < max(3, args.warmup) or time.perf_counter() - t_warm < args.warmup_seconds:
         step()
+        warm_steps += 1
+        if warm_steps % 50 == 0:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
+    if world > 1:   # every rank ran the same number of steps before the timed region
+        wt = torch.tensor([warm_steps], dtype=torch.int64, device=device)
+        dist.all_reduce(wt, op=dist.ReduceOp.MAX)
+        for _ in range(int(wt.item()) - warm_steps):
+            step()
+        warm_steps = int(wt.item())
+        torch.cuda.synchronize()
 
     uuid = str(torch.cuda.get_device_properties(device).uuid)
     sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
@@ -420,7 +440,7 @@ def main():
         return
     line = {
         "metric": METRIC, "value": value, "unit": "elem/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": warm_steps, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: 2*N(0,1) logits + Zipf bias -1.1*ln(v+1), log_softmax over V, seeded per example",
         "config": bench_config(B, T, K, V, world),
