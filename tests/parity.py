@@ -174,3 +174,35 @@ def logging_filter(log):
         return int((token * 7 + step * 3 + parent + last) % 5 != 0)
     return fn
 
+
+def degenerate_cases():
+    """Edge shapes and values: V=1, a single step and beam, rows entirely -inf,
+    log-probs near -FLT_MAX (parent + lp overflows), more beams than tokens with
+    all tokens but one banned, and a -0.0 / +0.0 tie."""
+    rng = np.random.default_rng(42)
+    cases = []
+    # one-token vocabulary, with and without EOS / min length
+    cases.append((dict(beam_size=3), np.zeros((4, 3, 1), np.float32), {}))
+    cases.append((dict(beam_size=2, eos_token=0, min_length=2), np.zeros((3, 2, 1), np.float32), {}))
+    # single step, single beam
+    cases.append((dict(beam_size=1), log_softmax_np(rng.standard_normal((1, 1, 50)).astype(np.float32)), {}))
+    # every log-prob -inf except one row
+    x = np.full((3, 4, 30), -np.inf, np.float32)
+    x[1, 0, 7] = -0.5
+    cases.append((dict(beam_size=4, relaxed_pool_multiplier=2), x, {}))
+    # values near -FLT_MAX: parent + lp overflows to -inf
+    x = np.full((4, 2, 20), -3.0e38, np.float32)
+    x[:, :, 3] = -1.0
+    x[2, 1, 5] = -2.0e38
+    cases.append((dict(beam_size=2, length_penalty_alpha=0.5), x, {}))
+    # more beams than tokens, all banned but one, forced steps
+    x = log_softmax_np(rng.standard_normal((3, 6, 4)).astype(np.float32))
+    banned = np.array([1, 1, 0, 1], np.uint8)
+    cases.append((dict(beam_size=6), x, dict(banned=banned, forced=np.array([-1, 2, -1], np.int32))))
+    # -0.0 and +0.0 log-probs tie
+    x = np.full((2, 2, 8), -5.0, np.float32)
+    x[:, :, 1] = -0.0
+    x[:, :, 6] = 0.0
+    cases.append((dict(beam_size=2, eos_token=6), x, {}))
+    return cases
+

@@ -105,3 +105,20 @@ def test_oracle_token_filter_matches_reference(oracle_lib):
         assert_decode_equal(got, want, f"filter case {i}")
         assert log_orc == log_ref, f"filter case {i}: call sequence differs"
 
+
+
+def test_oracle_degenerate_cases_match_reference(oracle_lib):
+    """Edge shapes and values (V=1, -inf rows, overflow near -FLT_MAX, K > V,
+    signed zeros) against oracle/_ref directly."""
+    import dbs_ctypes as dc
+    from oracle import reference_library_path
+    from parity import degenerate_cases
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+    ref = dc.load_library(path, device_api=False)
+    for i, (opts, x, cons) in enumerate(degenerate_cases()):
+        T, K, V = x.shape
+        want = dc.decode_and_read(ref, dc.Options(**opts), np.ascontiguousarray(x), T, V, **cons)
+        got = oracle_lib.decode(oracle_lib.options(**opts), x, T, V, **cons)
+        assert_decode_equal(got, want, f"degenerate {i}")

@@ -6,8 +6,8 @@ import numpy as np
 import pytest
 
 import dbs_ctypes as dc
-from parity import (assert_close_rel, assert_decode_equal, assert_sparse_equal, log_softmax_np,
-                    random_case)
+from parity import (assert_close_rel, assert_decode_equal, assert_sparse_equal, degenerate_cases,
+                    log_softmax_np, random_case)
 
 pytestmark = pytest.mark.gpu
 
@@ -459,3 +459,12 @@ def test_concurrent_calls_on_one_handle(libdbs, oracle_lib):
         assert_decode_equal(out, want[i], f"thread result {i}")
         assert np.array_equal(out["backward"]["indices"], want[i]["backward"]["indices"])
         assert np.array_equal(out["backward"]["values"], want[i]["backward"]["values"])
+
+
+@pytest.mark.parametrize("idx", range(len(degenerate_cases())))
+def test_degenerate_shapes_and_values(libdbs, oracle_lib, idx):
+    opts, x, cons = degenerate_cases()[idx]
+    T, K, V = x.shape
+    want = _oracle_decode(oracle_lib, opts, x, T, V, cons)
+    got = _product_decode(libdbs, opts, np.ascontiguousarray(x), T, V, cons)
+    assert_decode_equal(got, want, f"degenerate case {idx}")
