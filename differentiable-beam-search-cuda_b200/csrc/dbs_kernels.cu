@@ -354,9 +354,19 @@ __global__ void validate_kernel(DecodeParams p) {
 constexpr int kScanStages = 4;
 constexpr int kScanChunkF4 = 128;       // 2 KB per chunk: 4 float4 per lane
 constexpr int kScanWarpsPerCta = 4;
-// Lists longer than 32 entries (buffer capacity above 2*32 + 136) compact by
-// radix selection, which needs a 256-bin histogram per warp.
-__host__ __device__ constexpr int row_scan_hist_ints(int capw) { return capw > 2 * 32 + 136 ? 256 : 0; }
+// Lists longer than 32 entries (buffer capacity above 2*32 + 136, plus 128
+// for 16-bit rows) compact by radix selection, which needs a 256-bin
+// histogram per warp.
+__host__ __device__ constexpr int row_scan_hist_ints(int capw, bool k16) {
+    return capw - (k16 ? 128 : 0) > 2 * 32 + 136 ? 256 : 0;
+}
+// Per-warp shared memory: chunk ring | mbarriers | survivor buffer | radix
+// histogram, 128-byte aligned.
+__host__ __device__ constexpr size_t row_scan_warp_bytes(int capw, bool k16) {
+    return ((static_cast<size_t>(kScanStages) * kScanChunkF4 * 16 + kScanStages * sizeof(uint64_t) +
+             static_cast<size_t>(capw) * sizeof(uint64_t) +
+             static_cast<size_t>(row_scan_hist_ints(capw, k16)) * sizeof(int)) + 127) & ~static_cast<size_t>(127);
+}
 
 __device__ __forceinline__ void warp_sort_desc_u64(uint64_t* a, int n, int lane) {
     if (n <= 1) { __syncwarp(); return; }
@@ -606,10 +616,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // per-warp region: ring | barriers | survivor buffer
     const size_t ring_bytes = static_cast<size_t>(kScanStages) * kScanChunkF4 * 16;
-    const int hist_ints = row_scan_hist_ints(capw);
-    const size_t warp_bytes = ring_bytes + kScanStages * sizeof(uint64_t) + static_cast<size_t>(capw) * sizeof(uint64_t) +
-                              static_cast<size_t>(hist_ints) * sizeof(int);
-    unsigned char* base = smem_raw + warp * ((warp_bytes + 127) & ~static_cast<size_t>(127));
+    const int hist_ints = row_scan_hist_ints(capw, k16);
+    unsigned char* base = smem_raw + warp * row_scan_warp_bytes(capw, k16);
     float4* ring = reinterpret_cast<float4*>(base);
     uint64_t* full = reinterpret_cast<uint64_t*>(base + ring_bytes);
     uint64_t* buf = full + kScanStages;
@@ -682,11 +690,12 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     };
 
     // Lists longer than 32 (when each warp scans many rows): the warp starts
-    // a row at a speculative threshold, the (3C/2)-th largest lp of the
-    // previous row it scanned. If fewer than C entries reach it the row is
-    // scanned again from global memory without a threshold, so the list
-    // stays exact; otherwise far fewer elements take the slow path than with
-    // a threshold that starts at -FLT_MAX.
+    // a row at a speculative threshold, the (C + 4 sqrt(C))-th largest lp of
+    // the previous row it scanned (the rank of a row's C-th value varies by
+    // about sqrt(C) between rows of one distribution). If fewer than C
+    // entries reach it the row is scanned again from global memory, so the
+    // list stays exact; otherwise far fewer elements take the slow path than
+    // with a threshold that starts at -FLT_MAX.
     float spec = -FLT_MAX;
     while (true) {
         issue_more();
@@ -725,7 +734,9 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 __syncwarp();
                 if (C > 32 && hist_ints) {
                     cnt = warp_compact_select(buf, cnt, C, lane, hist, thr, evict);
-                    if (cnt <= capw - 128 - 8 - 32) return;
+                    // room for one more group of appends (128 values, 256
+                    // for 16-bit rows) plus the 32-value tail
+                    if (cnt <= capw - (k16 ? 256 : 128) - 8 - 32) return;
                     // the C-th lp value repeats too often to free room: cut exactly
                 }
                 warp_sort_desc_u64(buf, cnt, lane);
@@ -863,11 +874,26 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 consider(in, t0 + lane, lp);
             }
             __syncwarp();
-            if (spec_used && cnt < C) {
-                // the speculative threshold dropped part of the best C: scan
-                // the row again (global memory, token order) without one
+            const int k_spec = C + static_cast<int>(4.0f * sqrtf(static_cast<float>(C)));
+            const bool missed = spec_used && cnt < C;
+            if (missed) {
+                // The speculative threshold dropped part of the best C: scan
+                // the row again (global memory, token order). No compaction
+                // ran, so the buffer holds every candidate at or above the
+                // threshold and each lane's `rej` is the largest element it
+                // rejected. Without constraints on the row those 32 maxima
+                // are distinct candidates, so the m-th largest of them, for
+                // C - cnt <= m <= 32, has at least C candidates at or above
+                // it: a safe threshold for the second pass, taken with m up
+                // to k_spec - cnt so the next row's threshold can come from it.
+                float boot = -FLT_MAX;
+                if (C - cnt <= 32 && !j.banned && !j.eos_blocked && !j.allow) {
+                    const int m = min(32, k_spec - cnt);
+                    const float kth = warp_kth_largest(rej, m, lane);
+                    if (kth > boot) boot = kth;   // -inf when fewer than m lanes rejected a finite value
+                }
                 cnt = 0;
-                thr = -FLT_MAX;
+                thr = boot;
                 rej = -INFINITY;
                 evict = -INFINITY;
                 for (int base = 0; base < p.V; base += 128) {
@@ -879,19 +905,26 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                         in4[c] = t0 + c < p.V;
                         v4[c] = in4[c] ? row_lp<k16>(j, t0 + c, bf16) : -INFINITY;
                     }
+                    const float m4 = fmaxf(fmaxf(v4[0], v4[1]), fmaxf(v4[2], v4[3]));
+                    if (!__any_sync(FULL, m4 >= thr)) {
+                        rej = fmaxf(rej, m4);
+                        continue;
+                    }
 #pragma unroll
                     for (int c = 0; c < 4; ++c) consider(in4[c], t0 + c, v4[c]);
                     if (cnt > capw - 128 - 8) compact();
                 }
                 __syncwarp();
             }
-            // long lists: cut to about 3C/2 (the next row's speculative
+            // long lists: cut to k_spec entries (the next row's speculative
             // threshold comes from there) before the one full sort of the row
-            const int k_spec = C + C / 2;
             if (C > 32 && hist_ints && cnt > k_spec + 32)
                 cnt = warp_compact_select(buf, cnt, k_spec, lane, hist, thr, evict);
             warp_sort_desc_u64(buf, cnt, lane);
-            if (C > 32 && hist_ints && cnt >= k_spec) spec = list_lp(buf[k_spec - 1]);
+            if (C > 32 && hist_ints) {
+                if (cnt >= k_spec) spec = list_lp(buf[k_spec - 1]);
+                else if (missed) spec = cnt > 0 ? list_lp(buf[cnt - 1]) : -FLT_MAX;   // lower it after a miss
+            }
             const int keep = cnt < C ? cnt : C;
             for (int i = lane; i < keep; i += 32) out[i] = buf[i];
             rej = warp_max(rej);
@@ -2304,11 +2337,8 @@ cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream) {
 // per 16.
 static int row_scan_capw(int max_C) { return max_C + (max_C > 16 ? max_C : 16) + 128 + 8; }
 
-static size_t row_scan_smem(int capw) {
-    const size_t warp_bytes = static_cast<size_t>(kScanStages) * kScanChunkF4 * 16 + kScanStages * sizeof(uint64_t) +
-                              static_cast<size_t>(capw) * sizeof(uint64_t) +
-                              static_cast<size_t>(row_scan_hist_ints(capw)) * sizeof(int);
-    return static_cast<size_t>(kScanWarpsPerCta) * ((warp_bytes + 127) & ~static_cast<size_t>(127));
+static size_t row_scan_smem(int capw, bool k16) {
+    return static_cast<size_t>(kScanWarpsPerCta) * row_scan_warp_bytes(capw, k16);
 }
 
 cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream, int64_t rows) {
@@ -2316,27 +2346,44 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     if (rows <= 0) return cudaSuccess;
     const bool k16 = p.x16 != nullptr;
     // 16-bit rows append up to 256 values between compaction checks
-    const int capw = row_scan_capw(max_C) + (k16 ? 128 : 0);
+    int capw = row_scan_capw(max_C) + (k16 ? 128 : 0);
     const void* fn = k16 ? reinterpret_cast<const void*>(row_scan_kernel<true>)
                          : reinterpret_cast<const void*>(row_scan_kernel<false>);
-    const int threads = kScanWarpsPerCta * 32;
-    const size_t smem = row_scan_smem(capw);
-    cudaError_t err = ensure_dynamic_smem(fn, smem);
-    if (err != cudaSuccess) return err;
     int dev = 0;
-    err = cudaGetDevice(&dev);
+    cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
+    if (max_C > 32) {
+        // Long lists: shrink the survivor buffer so that the 4 CTAs per SM
+        // the launch bounds plan for fit in shared memory (more compactions,
+        // but a third more warps than 3 CTAs at C = 256), when that leaves
+        // room for one append group plus 32 entries above C.
+        int per_sm_smem = 0, reserved = 0;
+        err = cudaDeviceGetAttribute(&per_sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        if (err != cudaSuccess) return err;
+        err = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+        if (err != cudaSuccess) return err;
+        const int per_warp = ((per_sm_smem / 4 - reserved) / kScanWarpsPerCta) & ~127;
+        const int fixed = kScanStages * kScanChunkF4 * 16 + kScanStages * 8 + 256 * 4;
+        const int fit = (per_warp - fixed) / 8;
+        const int lowest = max_C + (k16 ? 256 : 128) + 8 + 32;
+        if (fit >= lowest && fit < capw) capw = fit;
+    }
+    const int threads = kScanWarpsPerCta * 32;
+    const size_t smem = row_scan_smem(capw, k16);
+    err = ensure_dynamic_smem(fn, smem);
+    if (err != cudaSuccess) return err;
+    const int key = dev + (k16 ? 1 << 20 : 0);
     int per_sm = -1;
     {
         std::lock_guard<std::mutex> lock(g_attr_mu);
         for (auto& e : g_row_scan_occ)
-            if (std::get<0>(e) == dev + (k16 ? 1 << 20 : 0) && std::get<1>(e) == smem) per_sm = std::get<2>(e);
+            if (std::get<0>(e) == key && std::get<1>(e) == smem) per_sm = std::get<2>(e);
     }
     if (per_sm < 0) {
         err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem);
         if (err != cudaSuccess) return err;
         std::lock_guard<std::mutex> lock(g_attr_mu);
-        g_row_scan_occ.emplace_back(dev + (k16 ? 1 << 20 : 0), smem, per_sm);
+        g_row_scan_occ.emplace_back(key, smem, per_sm);
     }
     if (per_sm < 1) per_sm = 1;
     int64_t ctas = static_cast<int64_t>(num_sms) * per_sm;
@@ -2345,8 +2392,9 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     // The speculative threshold pays off over several rows per warp; with
     // few rows a failed guess (a second read of the row) only adds to the tail.
     const int speculate = (max_C > 32 && rows >= 4 * ctas * kScanWarpsPerCta) ? 1 : 0;
-    if (k16) row_scan_kernel<true><<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw, speculate);
-    else row_scan_kernel<false><<<static_cast<unsigned>(ctas), threads, smem, stream>>>(p, capw, speculate);
+    const dim3 grid(static_cast<unsigned>(ctas));
+    if (k16) row_scan_kernel<true><<<grid, threads, smem, stream>>>(p, capw, speculate);
+    else row_scan_kernel<false><<<grid, threads, smem, stream>>>(p, capw, speculate);
     return cudaGetLastError();
 }
 

@@ -186,6 +186,44 @@ def test_rows_of_very_different_sharpness(libdbs, oracle_lib, mult):
     dec.close()
 
 
+
+@pytest.mark.parametrize("K,mult,flat,cons", [
+    (8, 8, 0.75, False), (8, 16, 0.65, False), (8, 8, 0.75, True), (32, 8, 0.8, False),
+])
+def test_speculative_threshold_small_misses(libdbs, oracle_lib, K, mult, flat, cons):
+    # Rows alternate between scale 1 and a slightly flatter scale, so a row
+    # that follows a scale-1 row usually misses its speculative threshold by
+    # a few entries (fewer than 32): the second pass then starts from the
+    # lane maxima of what the first pass rejected. With bans and a minimum
+    # length on the example the second pass starts from scratch instead.
+    rng = np.random.default_rng(100 + mult + K)
+    # 9600 rows: every warp scans several (lists of 256 entries at K = 32)
+    B, T, V = (40, 30, 2000) if K == 8 else (10, 30, 4000)
+    scale = np.where(np.arange(K) % 2 == 0, 1.0, flat).astype(np.float32)
+    xb = log_softmax_np(rng.standard_normal((B, T, K, V)).astype(np.float32) * scale[None, None, :, None])
+    # a few rows with most values -inf: some lanes reject nothing finite
+    xb[3, 4, 1, 40:] = -np.inf
+    xb[7, 9, :, :V - 500] = -np.inf
+    opts = dict(beam_size=K, relaxed_pool_multiplier=mult, eos_token=2)
+    kw = {}
+    if cons:
+        opts["min_length"] = 6
+        banned = (rng.random(V) < 0.02).astype(np.uint8)
+        kw = dict(banned=banned, min_length=6)
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    if cons:
+        br = dec.decode_batch_variable(np.ascontiguousarray(xb), B, T, K, V, steps=np.full(B, T, np.int32),
+                                       beams=np.full(B, K, np.int32), eos=np.full(B, 2, np.int32),
+                                       min_lengths=np.full(B, 6, np.int32),
+                                       banned=np.ascontiguousarray(np.tile(kw["banned"], (B, 1))), threads=4)
+    else:
+        br = dec.decode_batch(np.ascontiguousarray(xb), B, T, V, 4)
+    for b in sorted(set(range(0, B, 4)) | {3, 7}):
+        w = _oracle_decode(oracle_lib, opts, xb[b], T, V, kw)
+        assert_decode_equal(dc.read_result(libdbs, libdbs.dbs_batch_result_at(br, b)), w, f"example {b}")
+    libdbs.dbs_free_batch_result(br)
+    dec.close()
+
 def test_massive_ties_with_large_beam(libdbs, oracle_lib):
     # constant rows: thousands of candidates share one key prefix, so the
     # merge's radix selection cannot narrow them and sorts them all
@@ -305,6 +343,41 @@ def test_typed_decode_widening(libdbs, oracle_lib, dtype):
     dec.close()
     assert_decode_equal(got, want, dtype)
 
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_typed_long_lists_with_ties_at_the_cut(libdbs, oracle_lib, dtype):
+    # 16-bit rows, 64-entry lists: the first 256 values hold 150 copies of
+    # one value, so the compaction after them keeps more than 2C entries
+    # tied at the C-th value and must cut exactly before the next 256-value
+    # group (all above the cut) is appended.
+    T, K, V = 2, 8, 4096
+    x = np.full((T, K, V), -10.0, dtype=np.float32)
+    first = np.where(np.arange(256) % 256 < 150, -6.0, -9.0).astype(np.float32)
+    np.random.default_rng(4).shuffle(first)
+    x[:, :, :256] = first
+    x[:, :, 256:512] = -5.0 + 0.03125 * (np.arange(256) % 32)
+    x[1, 3, 700] = -1.0
+    if dtype == "f16":
+        bits = x.astype(np.float16).view(np.uint16)
+        wide = bits.view(np.float16).astype(np.float32)
+        code = dc.DBS_DTYPE_F16
+    else:
+        bits = (x.view(np.uint32) >> 16).astype(np.uint16)
+        wide = (bits.astype(np.uint32) << 16).view(np.float32)
+        code = dc.DBS_DTYPE_BF16
+    assert np.array_equal(wide, x)   # every value is exact in both formats
+    opts = dict(beam_size=K, relaxed_pool_multiplier=8)
+    want = _oracle_decode(oracle_lib, opts, wide, T, V, {})
+    dec = dc.Decoder(libdbs, dc.Options(**opts))
+    r = ctypes.c_void_p()
+    rc = libdbs.dbs_decode_typed(dec.h, np.ascontiguousarray(bits).ctypes.data_as(ctypes.c_void_p), code, T, V,
+                                 ctypes.byref(r))
+    assert rc == 0, libdbs.dbs_last_error(dec.h)
+    got = dc.read_result(libdbs, r)
+    libdbs.dbs_free_result(r)
+    dec.close()
+    assert_decode_equal(got, want, dtype)
 
 def _to16(x, dtype):
     if dtype == "f16":
