@@ -66,6 +66,11 @@ def parse_args():
     ap.add_argument("--pool-decode", type=int, default=None, metavar="MULT",
                     help="profiling only: run the relaxed-pool device decode (relaxed_pool_multiplier MULT) "
                          "--steps times on the workload and print no bench line")
+    ap.add_argument("--shape", default=None, metavar="T,K,V",
+                    help="profiling only (--pool-decode): steps, beams and vocabulary instead of the workload's")
+    ap.add_argument("--rows", choices=("zipf", "normal"), default="zipf",
+                    help="profiling only (--pool-decode): the workload's Zipf-biased rows, or "
+                         "log_softmax(N(0,1)) rows as in the 256-example V=50257 configuration")
     return ap.parse_args()
 
 
@@ -76,8 +81,19 @@ def pool_decode_loop(args):
     import torch_dbs_extension as ext
     B, T, K, V = (WORKLOAD[k] for k in "BTKV")
     B = args.batch or B
-    x = make_inputs(torch, B, T, K, V, 0, torch.device("cuda", 0))
-    opts = ext.DBSOptions(**dict(OPTIONS, relaxed_pool_multiplier=args.pool_decode))
+    if args.shape:
+        T, K, V = (int(v) for v in args.shape.split(","))
+    device = torch.device("cuda", 0)
+    if args.rows == "zipf":
+        x = make_inputs(torch, B, T, K, V, 0, device)
+    else:
+        x = torch.empty((B, T, K, V), dtype=torch.float32, device=device)
+        g = torch.Generator(device=device)
+        for b in range(B):
+            g.manual_seed(SEED * 1_000_003 + b)
+            x[b].normal_(generator=g)
+            x[b] = torch.log_softmax(x[b], dim=-1)
+    opts = ext.DBSOptions(**dict(OPTIONS, beam_size=K, relaxed_pool_multiplier=args.pool_decode))
     for _ in range(args.steps):
         ext.device_decode(x, opts, with_pool=True, with_weights=True)
     torch.cuda.synchronize()

@@ -649,18 +649,27 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     e_nxt = e_cur;
     RowJob nxt = cur;
     bool have_nxt = false;
-    // issue cursor
-    bool issue_in_cur = true;  // issuing chunks of cur (else of nxt)
-    int ic = 0;                // next chunk to issue within its row
+    // Issue cursor: the next chunk to copy, the chunks of its row still to
+    // copy and the bytes of that row's last chunk; `inxt` once the cursor has
+    // moved on to the prefetched row.
+    const float4* ip = nullptr;
+    int ileft = 0;
+    uint32_t ilast = 0;
+    bool inxt = false;
+    auto cursor_to = [&](const RowJob& jr) {
+        ip = reinterpret_cast<const float4*>(static_cast<const char*>(jr.row) +
+                                             (static_cast<size_t>(jr.h) << (k16 ? 1 : 2)));
+        ileft = jr.chunks;
+        ilast = static_cast<uint32_t>(jr.nv - (jr.chunks - 1) * kScanChunkF4) * 16u;
+    };
+    cursor_to(cur);
     uint32_t n_issued = 0, n_used = 0;
 
     auto issue_more = [&]() {
         // lane 0 keeps up to kScanStages chunks in flight, crossing into nxt
         while (n_issued < n_used + kScanStages) {
-            if (!issue_in_cur && !have_nxt) break;
-            const int jchunks = issue_in_cur ? cur.chunks : nxt.chunks;
-            if (ic >= jchunks) {
-                if (!issue_in_cur) break;  // at most one row ahead
+            if (ileft == 0) {
+                if (inxt) break;  // at most one row ahead
                 // move the issue cursor to the next claimed row
                 if (!have_nxt) {
                     const int64_t rn = claim();
@@ -668,23 +677,18 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                     nxt = make_job<k16>(p, rn, e_nxt);
                     have_nxt = true;
                 }
-                issue_in_cur = false;
-                ic = 0;
+                inxt = true;
+                cursor_to(nxt);
                 continue;
             }
-            const int s = static_cast<int>(n_issued % kScanStages);
-            const int f0 = ic * kScanChunkF4;
-            const int jnv = issue_in_cur ? cur.nv : nxt.nv;
-            const RowJob& jj = issue_in_cur ? cur : nxt;
-            const char* jbody = static_cast<const char*>(jj.row) + (static_cast<size_t>(jj.h) << (k16 ? 1 : 2));
-            const int nf = min(kScanChunkF4, jnv - f0);
+            const uint32_t s = n_issued % kScanStages;
             if (lane == 0) {
-                const uint32_t bytes = static_cast<uint32_t>(nf) * 16u;
+                const uint32_t bytes = ileft == 1 ? ilast : kScanChunkF4 * 16u;
                 mbar_arrive_expect_tx(full + s, bytes);
-                bulk_copy_g2s(ring + static_cast<size_t>(s) * kScanChunkF4,
-                              reinterpret_cast<const float4*>(jbody) + f0, bytes, full + s);
+                bulk_copy_g2s(ring + s * kScanChunkF4, ip, bytes, full + s);
             }
-            ++ic;
+            ip += kScanChunkF4;
+            --ileft;
             ++n_issued;
         }
     };
@@ -730,6 +734,18 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 if (keep) buf[cnt + __popc(b & lt_mask)] = list_key(lp, v);
                 cnt += __popc(b);
             };
+            // Rows without banned tokens, EOS block or host verdicts (the
+            // common case) only exclude +inf: no per-value branches. Padding
+            // values are -inf, which is never kept and leaves rej unchanged.
+            const bool plain = !j.banned && !j.eos_blocked && !j.allow;
+            auto consider_plain = [&](int v, float lp) {
+                const bool pass = lp >= thr;
+                if (!pass) rej = fmaxf(rej, lp);
+                const bool keep = pass && lp != INFINITY;
+                const unsigned b = __ballot_sync(FULL, keep);
+                if (keep) buf[cnt + __popc(b & lt_mask)] = list_key(lp, v);
+                cnt += __popc(b);
+            };
             auto compact = [&]() {
                 __syncwarp();
                 if (C > 32 && hist_ints) {
@@ -753,18 +769,21 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 consider(in, lane, lp);
             }
             for (int c = 0; c < j.chunks; ++c) {
-                const int s = static_cast<int>(n_used % kScanStages);
+                const uint32_t s = n_used % kScanStages;
                 const uint32_t parity = (n_used / kScanStages) & 1u;
                 if (!mbar_wait(full + s, parity, err)) return;
-                const int nf = min(kScanChunkF4, j.nv - c * kScanChunkF4);
-                const float4* st = ring + static_cast<size_t>(s) * kScanChunkF4;
+                const float4* st = ring + s * kScanChunkF4;
                 float4 q[4];
-                bool in[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int idx = u * 32 + lane;
-                    in[u] = idx < nf;
-                    q[u] = in[u] ? st[idx] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                for (int u = 0; u < 4; ++u) q[u] = st[u * 32 + lane];
+                const int nf = j.nv - c * kScanChunkF4;
+                if (nf < kScanChunkF4) {
+                    // the row's last chunk is partial: the rest of the slot
+                    // is stale, read as -inf in the element format
+                    const float pad = k16 ? __uint_as_float(bf16 ? 0xFF80FF80u : 0xFC00FC00u) : -INFINITY;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (u * 32 + lane >= nf) q[u] = make_float4(pad, pad, pad, pad);
                 }
                 if constexpr (!k16) {
                     if (c == 0 && C <= 32) {
@@ -773,7 +792,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                         float mx = -INFINITY;
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
-                            if (!in[u]) continue;
+                            // padding is -inf: not finite, never counted
                             const int v0 = j.h + 4 * (u * 32 + lane);
                             if (isfinite(q[u].x) && allowed(v0 + 0, q[u].x)) mx = fmaxf(mx, q[u].x);
                             if (isfinite(q[u].y) && allowed(v0 + 1, q[u].y)) mx = fmaxf(mx, q[u].y);
@@ -807,10 +826,17 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                                 continue;
                             }
                             const int v0 = tok0 + 4 * (u * 32 + lane);
-                            consider(in[u], v0 + 0, q[u].x);
-                            consider(in[u], v0 + 1, q[u].y);
-                            consider(in[u], v0 + 2, q[u].z);
-                            consider(in[u], v0 + 3, q[u].w);
+                            if (plain) {
+                                consider_plain(v0 + 0, q[u].x);
+                                consider_plain(v0 + 1, q[u].y);
+                                consider_plain(v0 + 2, q[u].z);
+                                consider_plain(v0 + 3, q[u].w);
+                            } else {
+                                consider(true, v0 + 0, q[u].x);
+                                consider(true, v0 + 1, q[u].y);
+                                consider(true, v0 + 2, q[u].z);
+                                consider(true, v0 + 3, q[u].w);
+                            }
                             if (cnt > capw - 128 - 8) compact();
                         }
                     }
@@ -825,13 +851,12 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                         unpack8(q16[w], bf16, f);
                         m8[w] = -INFINITY;
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) m8[w] = fmaxf(m8[w], in[w] ? f[i] : -INFINITY);
+                        for (int i = 0; i < 8; ++i) m8[w] = fmaxf(m8[w], f[i]);
                     }
                     if (c == 0 && C <= 32) {
                         float mx = -INFINITY;
 #pragma unroll
                         for (int w = 0; w < 4; ++w) {
-                            if (!in[w]) continue;
                             float f[8];
                             unpack8(q16[w], bf16, f);
                             const int v0 = j.h + 8 * (w * 32 + lane);
@@ -861,7 +886,10 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                             unpack8(q16[w], bf16, f);
                             const int v0 = tok0 + 8 * (w * 32 + lane);
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) consider(in[w], v0 + i, f[i]);
+                            for (int i = 0; i < 8; ++i) {
+                                if (plain) consider_plain(v0 + i, f[i]);
+                                else consider(true, v0 + i, f[i]);
+                            }
                             if (cnt > capw - 256 - 8) compact();
                         }
                     }
@@ -911,7 +939,10 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                         continue;
                     }
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) consider(in4[c], t0 + c, v4[c]);
+                    for (int c = 0; c < 4; ++c) {
+                        if (plain) consider_plain(t0 + c, v4[c]);
+                        else consider(in4[c], t0 + c, v4[c]);
+                    }
                     if (cnt > capw - 128 - 8) compact();
                 }
                 __syncwarp();
@@ -937,21 +968,16 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             __syncwarp();
         }
         // advance to the next claimed row
-        if (issue_in_cur) {
-            // nothing of the next row was issued yet
-            const int64_t rn = have_nxt ? nxt.r : claim();
-            if (!have_nxt) {
-                if (rn >= p.total_rows) return;
-                nxt = make_job<k16>(p, rn, e_nxt);
-            }
-            cur = nxt;
-            have_nxt = false;
-            ic = 0;
-        } else {
-            cur = nxt;
-            have_nxt = false;
-            issue_in_cur = true;
+        if (!inxt) {
+            // nothing of the next row was issued yet (nor claimed)
+            const int64_t rn = claim();
+            if (rn >= p.total_rows) return;
+            nxt = make_job<k16>(p, rn, e_nxt);
+            cursor_to(nxt);
         }
+        cur = nxt;
+        have_nxt = false;
+        inxt = false;
         e_cur = e_nxt;
     }
 }
