@@ -182,6 +182,105 @@ __device__ __forceinline__ int find_example(const int64_t* prefix, int B, int64_
 // `tmp_cap` of them remain; those are gathered into tmp_hi/tmp_lo, sorted and
 // copied back. Keys tied on hi beyond that capacity fall back to a full sort.
 // Must be called by all threads of the block; ends with a barrier.
+// Top n_out keys of nr runs, each sorted descending by (hi, lo) with unique
+// keys: run r holds meta_a[r] & 0xFFFF keys at offset meta_a[r] >> 16 of
+// (ahi, alo). Rounds of pairwise merges halve the run count; output j of a
+// pair comes from a merge-path binary search (how many of the first j come
+// from the first run), so a round needs no barrier inside and only the top
+// n_out keys of each pair are formed. Rounds ping-pong between (ahi, alo) and
+// (bhi, blo); the result is the run at offset 0 of the returned buffer (0 =
+// a, 1 = b), *n_res keys. meta_b holds (nr + 1) / 2 words of scratch.
+// Called by all threads of the block.
+__device__ __noinline__ int block_merge_runs(uint64_t* ahi, uint64_t* alo, uint64_t* bhi, uint64_t* blo,
+                                             uint32_t* meta_a, uint32_t* meta_b, int nr, int n_out, int* n_res) {
+    __shared__ int sh_total;
+    uint64_t *shi = ahi, *slo = alo, *dhi = bhi, *dlo = blo;
+    uint32_t *mcur = meta_a, *mnext = meta_b;
+    int which = 0;
+    while (nr > 1) {
+        const int np = (nr + 1) >> 1;
+        if (threadIdx.x < 32) {
+            // pair lengths (capped at n_out) and their offsets, one warp
+            const int lane = threadIdx.x;
+            const int per = (np + 31) >> 5;
+            const int p0 = lane * per;
+            const int p1 = p0 + per < np ? p0 + per : np;
+            auto pair_len = [&](int q) {
+                int len = static_cast<int>(mcur[2 * q] & 0xFFFFu);
+                if (2 * q + 1 < nr) len += static_cast<int>(mcur[2 * q + 1] & 0xFFFFu);
+                return len < n_out ? len : n_out;
+            };
+            int sum = 0;
+            for (int q = p0; q < p1; ++q) sum += pair_len(q);
+            int incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            int run = incl - sum;
+            for (int q = p0; q < p1; ++q) {
+                const int len = pair_len(q);
+                mnext[q] = (static_cast<uint32_t>(run) << 16) | static_cast<uint32_t>(len);
+                run += len;
+            }
+            if (lane == 31) sh_total = incl;
+        }
+        __syncthreads();
+        const int total = sh_total;
+        for (int g = threadIdx.x; g < total; g += blockDim.x) {
+            // the pair holding output g: the last one starting at or before g
+            int lo = 0, hi = np - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (static_cast<int>(mnext[mid] >> 16) <= g) lo = mid; else hi = mid - 1;
+            }
+            const int q = lo;
+            const int dst = static_cast<int>(mnext[q] >> 16);
+            const int j = g - dst;
+            const uint32_t ma = mcur[2 * q];
+            const int aoff = static_cast<int>(ma >> 16), a = static_cast<int>(ma & 0xFFFFu);
+            int boff = 0, b = 0;
+            if (2 * q + 1 < nr) {
+                const uint32_t mb = mcur[2 * q + 1];
+                boff = static_cast<int>(mb >> 16);
+                b = static_cast<int>(mb & 0xFFFFu);
+            }
+            // i = keys of the first run among the pair's first j outputs
+            int l2 = j - b > 0 ? j - b : 0;
+            int h2 = j < a ? j : a;
+            // x before y: larger high word, or equal high words and larger
+            // low word (read only then: high words rarely tie)
+            auto before = [&](int x, int y) {
+                const uint64_t hx = shi[x], hy = shi[y];
+                return hx > hy || (hx == hy && slo[x] > slo[y]);
+            };
+            while (l2 < h2) {
+                const int mid = (l2 + h2) >> 1;
+                if (before(aoff + mid, boff + j - 1 - mid)) l2 = mid + 1;
+                else h2 = mid;
+            }
+            const int i = l2;
+            bool take_a;
+            if (i >= a) take_a = false;
+            else if (j - i >= b) take_a = true;
+            else take_a = before(aoff + i, boff + j - i);
+            const int src = take_a ? aoff + i : boff + j - i;
+            dhi[dst + j] = shi[src];
+            dlo[dst + j] = slo[src];
+        }
+        __syncthreads();
+        uint64_t* th = shi; shi = dhi; dhi = th;
+        uint64_t* tl = slo; slo = dlo; dlo = tl;
+        uint32_t* tm = mcur; mcur = mnext; mnext = tm;
+        which ^= 1;
+        nr = np;
+    }
+    const int len = nr > 0 ? static_cast<int>(mcur[0] & 0xFFFFu) : 0;
+    *n_res = len < n_out ? len : n_out;
+    return which;
+}
+
 __device__ __noinline__ void block_top_n_u128(uint64_t* hi, uint64_t* lo, int m, int n_top, uint64_t* tmp_hi, uint64_t* tmp_lo,
                                  int tmp_cap) {
     __shared__ int hist[256];
@@ -1040,6 +1139,10 @@ __device__ __forceinline__ bool in_list(const int32_t* a, int n, int v) {
     return false;
 }
 
+// kRuns: the instance for up to 1024 candidates per step, which merges the
+// sorted row runs when no sequence constraint is active (the larger-step
+// instance leaves that code out: it costs registers on the selection path).
+template <bool kRuns>
 __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodeParams p, int cand_cap,
                                                                    int seq_T, int seq_K, int sel_cap) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -1130,7 +1233,24 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         // Candidate generation: slot k*C + i holds entry i of row k; an
         // ended parent's carry candidate takes slot k*C.
         const int M = K * C;
-        for (int idx = tid; idx < M; idx += NT) {
+        for (int idx0 = tid; idx0 < M; idx0 += 4 * NT) {
+            // four list loads in flight per thread before any is used
+            uint64_t lk[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int idx = idx0 + u * NT;
+                lk[u] = 0;
+                if (idx < M) {
+                    const int k = idx / C;
+                    const int i = idx - k * C;
+                    if (i < s.row_cnt[k] && isfinite(s.prev_raw[k]) && !(d.eos >= 0 && s.ended[k]))
+                        lk[u] = p.lists[d.list_offset + (row0 - d.row_begin + k) * C + i];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+            const int idx = idx0 + u * NT;
+            if (idx >= M) continue;
             const int k = idx / C;
             const int i = idx - k * C;
             uint64_t h = 0, l = 0;
@@ -1144,7 +1264,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                         l = cand_lo(k, d.eos);
                     }
                 } else if (i < s.row_cnt[k]) {
-                    const uint64_t key = p.lists[d.list_offset + (row0 - d.row_begin + k) * C + i];
+                    const uint64_t key = lk[u];
                     float lp = list_lp(key);
                     const int v = list_token(key);
                     bool ok = true;
@@ -1170,10 +1290,51 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
             }
             chi[idx] = h;
             clo[idx] = l;
+            }
         }
         __syncthreads();
-        if (M > 1024) block_top_n_u128(chi, clo, M, N, sel_hi, sel_lo, sel_cap);
-        else block_sort_desc_u128(chi, clo, M);
+        bool merged = false;
+        if (kRuns && !need_seq && M <= 1024) {   // (the first round then fits the selection buffer)
+            // Without per-beam changes to the log-probs each row's candidates
+            // come sorted: the list is in (lp desc, token asc) order, and
+            // raw = pr + lp and rank = raw * inv only round monotonically.
+            // The exception is two lp values rounding to one (rank, raw) with
+            // their tokens out of order; a step with such a pair sorts.
+            // Otherwise the top N is a merge of K sorted runs.
+            uint32_t* meta_a = reinterpret_cast<uint32_t*>(seq_len_a);
+            uint32_t* meta_b = reinterpret_cast<uint32_t*>(seq_len_b);
+            for (int k = tid; k < K; k += NT) {
+                int lo = 0, hi = C;   // empty slots (key 0) only trail a run
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if (chi[k * C + mid] != 0) lo = mid + 1; else hi = mid;
+                }
+                meta_a[k] = (static_cast<uint32_t>(k * C) << 16) | static_cast<uint32_t>(lo);
+            }
+            int bad = 0;   // any pair of neighbours out of order (or a gap before a key)
+            for (int idx = tid; idx < M; idx += NT) {
+                if (idx % C == C - 1) continue;
+                const uint64_t h0 = chi[idx], h1 = chi[idx + 1];
+                if (h1 > h0 || (h0 != 0 && h0 == h1 && clo[idx] < clo[idx + 1])) bad = 1;
+            }
+            if (!__syncthreads_or(bad)) {
+                int n_res = 0;
+                const int w = block_merge_runs(chi, clo, sel_hi, sel_lo, meta_a, meta_b, K, N, &n_res);
+                const int lim = N < M ? N : M;
+                for (int i = tid; i < lim; i += NT) {
+                    const uint64_t h = i < n_res ? (w ? sel_hi[i] : chi[i]) : 0;
+                    const uint64_t l = i < n_res ? (w ? sel_lo[i] : clo[i]) : 0;
+                    chi[i] = h;
+                    clo[i] = l;
+                }
+                __syncthreads();
+                merged = true;
+            }
+        }
+        if (!merged) {
+            if (M > 1024) block_top_n_u128(chi, clo, M, N, sel_hi, sel_lo, sel_cap);
+            else block_sort_desc_u128(chi, clo, M);
+        }
 
         // Exactness proof per truncated row: every entry the scan dropped has
         // lp <= bound, so its candidate is at most U = (rank(bound),
@@ -2470,12 +2631,18 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
                         static_cast<size_t>(max_K) * 3 * sizeof(float) +
                         static_cast<size_t>(max_K) * 7 * sizeof(int) + 64 +
                         16 + static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t);
+    // about two candidates per thread (the run merges of a step are bound by
+    // shared-memory latency, so more warps help)
     int threads = 64;
-    while (threads < kMergeThreads && threads * 2 <= (M + 1) / 2) threads <<= 1;
+    while (threads < kMergeThreads && threads * 2 <= M) threads <<= 1;
     if (threads < 128 && max_K > 64) threads = 128;
-    cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(step_merge_kernel), smem);
+    const bool runs = !need_sequences && M <= 1024;
+    const void* fn = runs ? reinterpret_cast<const void*>(step_merge_kernel<true>)
+                          : reinterpret_cast<const void*>(step_merge_kernel<false>);
+    cudaError_t err = ensure_dynamic_smem(fn, smem);
     if (err != cudaSuccess) return err;
-    step_merge_kernel<<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap);
+    if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap);
+    else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap);
     return cudaGetLastError();
 }
 

@@ -224,6 +224,25 @@ def test_speculative_threshold_small_misses(libdbs, oracle_lib, K, mult, flat, c
     libdbs.dbs_free_batch_result(br)
     dec.close()
 
+
+def test_rounding_collisions_in_merged_rows(libdbs, oracle_lib):
+    # Parent scores near -1000 (float spacing 6e-5) make log-probs 1e-5
+    # apart round to one raw score; with their tokens in reverse order a
+    # row's candidates are not in key order, so the step merge must not
+    # merge the rows as sorted runs (64-entry lists, 8 beams).
+    T, K, V = 3, 8, 120
+    x = np.full((T, K, V), -50.0, dtype=np.float32)
+    x[0] = -1000.0 - 0.001 * np.arange(V, dtype=np.float32)
+    for t in (1, 2):
+        x[t, :, 10] = -1.00001
+        x[t, :, 5] = -1.00002
+        for i in range(20):
+            x[t, :, 60 - i] = np.float32(-2.0 - 1e-6 * i)
+    opts = dict(beam_size=K, relaxed_pool_multiplier=8)
+    want = _oracle_decode(oracle_lib, opts, x, T, V, {})
+    got = _product_decode(libdbs, opts, x, T, V, {})
+    assert_decode_equal(got, want, "rounding collisions")
+
 def test_massive_ties_with_large_beam(libdbs, oracle_lib):
     # constant rows: thousands of candidates share one key prefix, so the
     # merge's radix selection cannot narrow them and sorts them all
