@@ -1380,30 +1380,48 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                 // in whenever the staging room could overflow (and at the end
                 // of the row); G only improves, so it is re-read per chunk.
                 const int stage_room = cand_cap - N;
-                // chunks of 2048: staged candidates are merged only when the
-                // room could overflow, so G stays fresh without extra merges
-                constexpr int chunk = 2048;
-                for (int base = 0; base < V; base += chunk) {
+                // Sub-batches of 4 values per thread (4 NT <= 2048 <= the
+                // room); four sub-batches (16 loads per thread) are in flight
+                // before the first is used. After each sub-batch the staged
+                // candidates are merged if the room could overflow, and G is
+                // re-read (it only improves).
+                const int sub = 4 * NT;
+                for (int base = 0; base < V; base += 4 * sub) {
+                    float lv[16];
+#pragma unroll
+                    for (int r = 0; r < 16; ++r) {
+                        const int v = base + (r >> 2) * sub + (r & 3) * NT + tid;
+                        lv[r] = v < V ? lp_at(p, row + v) : -INFINITY;
+                    }
+#pragma unroll
+                    for (int sb = 0; sb < 4; ++sb) {
+                    const int sbase = base + sb * sub;
+                    if (sbase >= V) break;
                     const uint64_t gh = (N - 1 < M) ? chi[N - 1] : 0;
                     const uint64_t gl = (N - 1 < M) ? clo[N - 1] : 0;
-                    const int lim = base + chunk < V ? base + chunk : V;
-                    // four loads in flight per thread before any of them is used
-                    for (int v0 = base + tid; v0 < lim; v0 += 4 * NT) {
-                        float lv[4];
+                    // lp floor: a value f whose candidate, formed with the same
+                    // roundings, has a high word below G's; rounding is
+                    // monotone, so no lp <= f can beat G (a penalised lp is
+                    // lower still). -inf when that cannot be shown.
+                    float floor_lp = -INFINITY;
+                    if (gh != 0) {
+                        const float rg = cand_rank(gh);
+                        float f = __fsub_rn(__fdiv_rn(rg, inv), pr);
+                        f = __fsub_rn(f, (fabsf(f) + fabsf(pr) + 1.0f) * 1e-3f);
+                        const float rawf = __fadd_rn(pr, f);
+                        const float rankf = __fmul_rn(rawf, inv);
+                        if (isfinite(f) && isfinite(rawf) && isfinite(rankf) && cand_hi(rankf, rawf) < gh) floor_lp = f;
+                    }
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int v = v0 + u * NT;
-                            lv[u] = v < lim ? lp_at(p, row + v) : -INFINITY;
-                        }
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                        const int v = v0 + u * NT;
-                        if (v >= lim) continue;
+                    for (int u = 0; u < 4; ++u) {
+                        const int v = sbase + u * NT + tid;
+                        if (v >= V) continue;
+                        float lp = lv[sb * 4 + u];
+                        if (lp <= floor_lp) continue;   // (NaN falls through to the check below)
                         if (forced >= 0 && v != forced) continue;
                         if (d.banned && d.banned[v]) continue;
                         if (eos_blocked && v == d.eos) continue;
                         if (p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v]) continue;
-                        float lp = lv[u];
                         if (!isfinite(lp)) continue;
                         const float lpc = __fadd_rn(lp, 0.0f);
                         if (lpc > m_lp || (lpc == m_lp && v <= m_tok)) continue;  // already listed
@@ -1426,19 +1444,54 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                             chi[N + pos] = h;
                             clo[N + pos] = l;
                         }
-                        }
                     }
                     __syncthreads();
                     const int staged = sh_stage;
-                    __syncthreads();   // every thread holds the count before the next chunk stages
-                    const bool last_chunk = lim >= V;
-                    if (staged > 0 && (last_chunk || staged > stage_room - chunk)) {
-                        if (N + staged > 1024) block_top_n_u128(chi, clo, N + staged, N, sel_hi, sel_lo, sel_cap);
-                        else block_sort_desc_u128(chi, clo, N + staged);
+                    __syncthreads();   // every thread holds the count before the next sub-batch stages
+                    const bool last_sub = sbase + sub >= V;
+                    if (staged > 0 && (last_sub || staged > stage_room - sub)) {
+                        if (staged <= 64) {
+                            // A few staged keys (the usual case): the final
+                            // position of a key of the sorted top N is its
+                            // index plus the staged keys above it; that of a
+                            // staged key is the top-N keys above it (binary
+                            // search) plus the staged keys above it. Keys are
+                            // unique, so the positions below N are distinct.
+                            for (int i = tid; i < N + staged; i += NT) {
+                                const uint64_t h = chi[i], l = clo[i];
+                                int pos = 0;
+                                if (i < N) {
+                                    pos = i;
+                                    for (int q = N; q < N + staged; ++q) pos += key2_less(h, l, chi[q], clo[q]) ? 1 : 0;
+                                } else {
+                                    int lo = 0, hi = N;   // top-N keys above (h, l)
+                                    while (lo < hi) {
+                                        const int mid = (lo + hi) >> 1;
+                                        if (key2_less(h, l, chi[mid], clo[mid])) lo = mid + 1; else hi = mid;
+                                    }
+                                    pos = lo;
+                                    for (int q = N; q < N + staged; ++q) pos += key2_less(h, l, chi[q], clo[q]) ? 1 : 0;
+                                }
+                                if (pos < N) {
+                                    sel_hi[pos] = h;
+                                    sel_lo[pos] = l;
+                                }
+                            }
+                            __syncthreads();
+                            for (int i = tid; i < N; i += NT) {
+                                chi[i] = sel_hi[i];
+                                clo[i] = sel_lo[i];
+                            }
+                        } else if (N + staged > 1024) {
+                            block_top_n_u128(chi, clo, N + staged, N, sel_hi, sel_lo, sel_cap);
+                        } else {
+                            block_sort_desc_u128(chi, clo, N + staged);
+                        }
                         for (int i = N + tid; i < N + staged; i += NT) { chi[i] = 0; clo[i] = 0; }
                         __syncthreads();
                         if (tid == 0) sh_stage = 0;
                         __syncthreads();
+                    }
                     }
                 }
             }
