@@ -349,6 +349,7 @@ struct Helper {
     cudaStream_t side = nullptr;
     cudaEvent_t before = nullptr;
     cudaEvent_t after = nullptr;
+    std::vector<cudaEvent_t> seg;   // end of each row-scan segment of a pipelined decode
 };
 std::mutex g_helper_mu;
 std::vector<Helper> g_helpers;
@@ -478,15 +479,33 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     // counters] [lists | counts | bounds | prefixes]. The header is staged in
     // pinned memory (status and counters zeroed there) and uploaded with one
     // asynchronous copy.
+    const bool ext_lists = ctl.lists != nullptr;
+    const int64_t scan_begin = std::max<int64_t>(0, ctl.scan_begin);
+    const int64_t scan_end = ctl.scan_end < 0 ? rows : std::min<int64_t>(rows, ctl.scan_end);
+    // One example whose merge is the selection merge (one CTA, T dependent
+    // steps, the slow half of such a decode): the row scan runs in segments
+    // of steps on the helper stream, and each segment's merge starts as soon
+    // as its rows are listed, beside the scan of the next segment; the beam
+    // state passes between the merge launches in the workspace.
+    int seg_steps = 0, n_seg = 0;
+    if (B == 1 && ctl.scan && ctl.merge && !ext_lists && scan_begin == 0 && scan_end == rows &&
+        ctl.t_begin <= 0 && ctl.t_end >= max_T && !ctl.merge_state && !ctl.row_allow && max_T >= 32 &&
+        (dynamic || static_cast<int64_t>(max_K) * max_C > 256)) {
+        // about 512 rows per segment (at least 16 steps): the first merge
+        // starts after one short scan, and a segment's scan (each warp near
+        // its own streaming limit) stays ahead of its merge
+        seg_steps = std::max(16, std::min(max_T, 512 / std::max(1, max_K)));
+        n_seg = (max_T + seg_steps - 1) / seg_steps;
+        if (n_seg < 2) n_seg = 0;
+    }
+    const bool pipeline = n_seg > 0;
     size_t hdr = 0;
     hdr += bytes_of<dbs_dev::ExampleDesc>(B);
     hdr += bytes_of<int64_t>(B + 1);
     hdr += 2 * bytes_of<float>(lmax + 1);
     hdr += bytes_of<int32_t>(B);
     hdr += bytes_of<unsigned long long>(4);
-    const bool ext_lists = ctl.lists != nullptr;
-    const int64_t scan_begin = std::max<int64_t>(0, ctl.scan_begin);
-    const int64_t scan_end = ctl.scan_end < 0 ? rows : std::min<int64_t>(rows, ctl.scan_end);
+    if (pipeline) hdr += bytes_of<unsigned long long>(n_seg);   // first row of each scan segment
     if (ext_lists && (!ctl.list_count || !ctl.list_bound)) throw InvalidArgument("row lists need counts and bounds");
     if (!ext_lists && !(ctl.scan && ctl.merge)) throw InvalidArgument("a split decode needs caller row lists");
     size_t ws = hdr;
@@ -496,6 +515,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         ws += bytes_of<float>(static_cast<size_t>(rows));
     }
     if (dynamic && !ctl.seq_scratch) ws += bytes_of<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
+    if (pipeline) ws += bytes_of<float>(static_cast<size_t>(4) * max_K);   // merge state between segments
     trace.mark("prepared");
     Lease lease(ws, hdr, stream);
     trace.mark("slot");
@@ -518,6 +538,13 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     std::memset(h_status, 0, sizeof(int32_t) * B);
     std::memset(h_counters, 0, sizeof(unsigned long long) * 4);
     h_counters[2] = static_cast<unsigned long long>(scan_begin);   // first row the scan claims
+    unsigned long long* h_seeds = nullptr;
+    if (pipeline) {
+        cv.take<unsigned long long>(n_seg);
+        h_seeds = hv.take<unsigned long long>(n_seg);
+        for (int i = 0; i < n_seg; ++i)
+            h_seeds[i] = static_cast<unsigned long long>(i) * seg_steps * desc[0].K;
+    }
     check_cuda(cudaMemcpyAsync(lease.s->dev, lease.s->pinned, cv.off, cudaMemcpyHostToDevice, stream),
                "upload decode metadata");
     if (ext_lists) {
@@ -532,6 +559,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     p.seq_scratch = !dynamic ? nullptr
                   : ctl.seq_scratch ? ctl.seq_scratch
                                     : cv.take<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
+    float* d_state = pipeline ? cv.take<float>(static_cast<size_t>(4) * max_K) : nullptr;
     p.t_begin = ctl.t_begin;
     p.t_end = ctl.t_end;
     p.merge_state = ctl.merge_state;
@@ -595,54 +623,128 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
                    "read status");
         check_cuda(cudaEventRecord(lease.s->validated, hp.side), "cudaEventRecord");
     }
-    if (ctl.scan && scan_end > scan_begin) {
-        ProfileScope ps(kRowScan, stream);
-        dbs_dev::DecodeParams ps_p = p;
-        ps_p.total_rows = scan_end;   // rows are claimed from scan_begin up to here
-        check_cuda(dbs_dev::launch_row_scan(ps_p, max_C, device_sm_count(), stream, scan_end - scan_begin),
-                   "row scan kernel");
-    }
-    trace.mark("row scan queued");
-    if (validate) {
-        // The reference rejects NaN / +Inf before decoding. The row scan is
-        // already queued (it only writes this call's workspace and tolerates
-        // any value), so the GPU keeps streaming while the host waits for the
-        // small validation kernel; nothing that writes an output is queued
-        // before the verdict.
-        check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
-        trace.mark("validate synced");
-        for (int b = 0; b < B; ++b)
-            if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
-    }
-    if (!ctl.merge) {
-        // scan-only call: read the counters back for the timeout check
-    } else if (ctl.zero_fill && ctl.zero_fill_count > 0) {
-        // zero the gradient buffer on the helper stream while the (latency
-        // bound, few-CTA) step merge runs; `stream` waits for it afterwards
-        // The merge is queued first; the fill is one 32-thread CTA per SM
-        // issuing bulk stores, so merge CTAs always fit beside it and keep
-        // the load/store pipe to themselves.
-        std::lock_guard<std::mutex> lock(g_helper_mu);
-        Helper& hp = helper_locked();
-        check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
+    if (pipeline) {
+        // Segments of steps: the helper stream seeds the row-claim counter
+        // and scans each segment's rows after the validation kernel; the
+        // merge of segment i (on `stream`) waits only for scan i, so it runs
+        // beside the scans of later segments.
+        // seg_done[n_seg]: the helper stream's part of this call is over
+        std::vector<cudaEvent_t> seg_done(n_seg + 1, nullptr);
+        struct EventsGuard {
+            std::vector<cudaEvent_t>& v;
+            ~EventsGuard() {
+                for (cudaEvent_t e : v)
+                    if (e) cudaEventDestroy(e);   // released once the queued waits are done
+            }
+        } events_guard{seg_done};
+        for (cudaEvent_t& ev : seg_done)
+            check_cuda(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "cudaEventCreate");
+        const int K0 = desc[0].K;
         {
+            std::lock_guard<std::mutex> lock(g_helper_mu);
+            Helper& hp = helper_locked();
+            if (!validate) {   // the metadata upload and the caller's earlier work come first
+                check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
+                check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
+            }
+            for (int i = 0; i < n_seg; ++i) {
+                const int64_t r0 = static_cast<int64_t>(i) * seg_steps * K0;
+                const int64_t r1 = std::min<int64_t>(rows, r0 + static_cast<int64_t>(seg_steps) * K0);
+                check_cuda(cudaMemcpyAsync(p.counters + 2, h_seeds + i, sizeof(unsigned long long),
+                                           cudaMemcpyHostToDevice, hp.side),
+                           "seed row claims");
+                {
+                    ProfileScope ps(kRowScan, hp.side);
+                    dbs_dev::DecodeParams ps_p = p;
+                    ps_p.total_rows = r1;
+                    check_cuda(dbs_dev::launch_row_scan(ps_p, max_C, device_sm_count(), hp.side, r1 - r0),
+                               "row scan kernel");
+                }
+                check_cuda(cudaEventRecord(seg_done[i], hp.side), "cudaEventRecord");
+            }
+            if (ctl.zero_fill && ctl.zero_fill_count > 0) {
+                // after the scans, beside the remaining merges
+                ProfileScope ps(kFillZero, hp.side);
+                check_cuda(dbs_dev::launch_fill_zero_bulk(ctl.zero_fill, ctl.zero_fill_count, device_sm_count(),
+                                                          hp.side),
+                           "zero fill kernel");
+            }
+            check_cuda(cudaEventRecord(seg_done[n_seg], hp.side), "cudaEventRecord");
+        }
+        trace.mark("row scan queued");
+        if (validate) {
+            check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
+            trace.mark("validate synced");
+            for (int b = 0; b < B; ++b) {
+                if (h_status[b]) {
+                    // the workspace is released on `stream`: it must cover the scans
+                    check_cuda(cudaStreamWaitEvent(stream, seg_done[n_seg], 0), "cudaStreamWaitEvent");
+                    throw InvalidArgument("log_probs contains NaN or +Inf");
+                }
+            }
+        }
+        for (int i = 0; i < n_seg; ++i) {
+            check_cuda(cudaStreamWaitEvent(stream, seg_done[i], 0), "cudaStreamWaitEvent");
+            dbs_dev::DecodeParams mp = p;
+            mp.t_begin = i * seg_steps;
+            mp.t_end = std::min(max_T, (i + 1) * seg_steps);
+            mp.merge_state = d_state;
             ProfileScope ps(kStepMerge, stream);
-            check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream),
+            check_cuda(dbs_dev::launch_step_merge(mp, max_K, max_C, max_T, max_N, dynamic, stream),
                        "step merge kernel");
         }
         trace.mark("merge queued");
-        check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
-        {
-            ProfileScope ps(kFillZero, hp.side);
-            check_cuda(dbs_dev::launch_fill_zero_bulk(ctl.zero_fill, ctl.zero_fill_count, device_sm_count(), hp.side),
-                       "zero fill kernel");
-        }
-        check_cuda(cudaEventRecord(hp.after, hp.side), "cudaEventRecord");
-        trace.mark("fill queued");
-        check_cuda(cudaStreamWaitEvent(stream, hp.after, 0), "cudaStreamWaitEvent");
+        check_cuda(cudaStreamWaitEvent(stream, seg_done[n_seg], 0), "cudaStreamWaitEvent");
     } else {
-        ProfileScope ps(kStepMerge, stream);
-        check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream), "step merge kernel");
+        if (ctl.scan && scan_end > scan_begin) {
+            ProfileScope ps(kRowScan, stream);
+            dbs_dev::DecodeParams ps_p = p;
+            ps_p.total_rows = scan_end;   // rows are claimed from scan_begin up to here
+            check_cuda(dbs_dev::launch_row_scan(ps_p, max_C, device_sm_count(), stream, scan_end - scan_begin),
+                       "row scan kernel");
+        }
+        trace.mark("row scan queued");
+        if (validate) {
+            // The reference rejects NaN / +Inf before decoding. The row scan is
+            // already queued (it only writes this call's workspace and tolerates
+            // any value), so the GPU keeps streaming while the host waits for the
+            // small validation kernel; nothing that writes an output is queued
+            // before the verdict.
+            check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
+            trace.mark("validate synced");
+            for (int b = 0; b < B; ++b)
+                if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
+        }
+        if (!ctl.merge) {
+            // scan-only call: read the counters back for the timeout check
+        } else if (ctl.zero_fill && ctl.zero_fill_count > 0) {
+            // zero the gradient buffer on the helper stream while the (latency
+            // bound, few-CTA) step merge runs; `stream` waits for it afterwards
+            // The merge is queued first; the fill is one 32-thread CTA per SM
+            // issuing bulk stores, so merge CTAs always fit beside it and keep
+            // the load/store pipe to themselves.
+            std::lock_guard<std::mutex> lock(g_helper_mu);
+            Helper& hp = helper_locked();
+            check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
+            {
+                ProfileScope ps(kStepMerge, stream);
+                check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream),
+                           "step merge kernel");
+            }
+            trace.mark("merge queued");
+            check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
+            {
+                ProfileScope ps(kFillZero, hp.side);
+                check_cuda(dbs_dev::launch_fill_zero_bulk(ctl.zero_fill, ctl.zero_fill_count, device_sm_count(), hp.side),
+                           "zero fill kernel");
+            }
+            check_cuda(cudaEventRecord(hp.after, hp.side), "cudaEventRecord");
+            trace.mark("fill queued");
+            check_cuda(cudaStreamWaitEvent(stream, hp.after, 0), "cudaStreamWaitEvent");
+        } else {
+            ProfileScope ps(kStepMerge, stream);
+            check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream), "step merge kernel");
+        }
     }
     const bool want_w = (p.weights && p.scores) || (p.relaxed_weights && p.pool_scores);
     if (want_w && ctl.merge && ctl.weights) {
