@@ -15,7 +15,9 @@ Metric: log-prob elements per second, B*T*K*V / (forward + backward time).
               every step and the loss read back.
   * roofline -- the row scan kernel (the pass that streams every log-prob
               once) timed live with CUDA events around its launches; its
-              algorithmic bytes are 4*B*T*K*V per launch.
+              algorithmic bytes are 4*B*(T*K - (K-1))*V per launch (every
+              row but those of beams 1..K-1 at step 0, which no live beam
+              extends).
   * cpu_baseline -- the reference's CPU library (compiled from its source into
               oracle/_ref) on the same workload, all host threads.
 
@@ -398,14 +400,15 @@ def main():
     rs = rs_live
     peak, peak_kind = measured_peaks()
     rs_ms = rs["total_ms"] / max(1, rs["launches"])
-    alg_bytes = 4.0 * elems
+    # every row but the K-1 rows of step 0 that no live beam extends
+    alg_bytes = 4.0 * B * (T * K - (K - 1)) * V
     achieved = alg_bytes / (rs_ms / 1e3) / 1e9 if rs_ms > 0 else None
     traffic = ncu_traffic_per_launch()
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": (achieved / peak) if achieved else None, "traffic": traffic,
                 "peak_kind": peak_kind, "kernel": "row_scan_kernel",
                 "algorithmic_bytes_per_launch": alg_bytes, "avg_launch_ms": rs_ms}
-    step_bytes = 8.0 * elems  # log-prob read + dense gradient write
+    step_bytes = alg_bytes + 4.0 * elems  # log-prob read + dense gradient write
     whole = {"achieved_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
              "frac": step_bytes / (ms_per_step / 1e3) / 1e9 / peak}
 

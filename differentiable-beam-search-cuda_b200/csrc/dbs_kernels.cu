@@ -665,6 +665,7 @@ struct RowJob {
     int forced;
     int eos;
     bool eos_blocked;
+    bool dead;   // never read: no live parent can extend it
     const uint8_t* banned;
     const uint8_t* allow;   // host filter verdicts of this row, or nullptr
     int h;       // unaligned head elements
@@ -693,6 +694,10 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     j.list_at = d.list_offset + lr * d.C;
     j.C = d.C;
     j.forced = d.forced ? d.forced[t] : -1;
+    // A decode starts from beam 0 alone (the other beams score -inf), so the
+    // rows of the other beams at step 0 can never yield a candidate; like
+    // the reference, which scans live parents only, they are not read.
+    j.dead = t == 0 && k > 0;
     j.eos = d.eos;
     j.eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
     j.banned = d.banned;
@@ -704,7 +709,7 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     if (h > p.V) h = p.V;
     j.h = h;
     j.nv = (p.V - h) >> (4 - kShift);
-    j.chunks = j.forced >= 0 ? 0 : (j.nv + kScanChunkF4 - 1) / kScanChunkF4;
+    j.chunks = (j.forced >= 0 || j.dead) ? 0 : (j.nv + kScanChunkF4 - 1) / kScanChunkF4;
     return j;
 }
 
@@ -805,7 +810,12 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
         const RowJob& j = cur;
         const int C = j.C;
         uint64_t* out = p.lists + j.list_at;
-        if (j.forced >= 0) {
+        if (j.dead) {
+            if (lane == 0) {
+                p.list_count[j.r] = 0;
+                p.list_bound[j.r] = -INFINITY;
+            }
+        } else if (j.forced >= 0) {
             // Forced step: only the forced token is a candidate of this row.
             if (lane == 0) {
                 const float lp = row_lp<k16>(j, j.forced, bf16);
