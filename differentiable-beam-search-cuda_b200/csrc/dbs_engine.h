@@ -48,7 +48,7 @@ struct ExampleDesc {
     int32_t k_stride;        // rows per step in the input layout
     int32_t P;               // relaxed pool size (output width of the pool)
     int32_t N;               // candidates selected per step (P or K)
-    int32_t C;               // row list capacity (>= N)
+    int32_t C;               // row list capacity (at most N; shorter lists are proven per step)
     int32_t sel_stride;      // K-dimension stride of [T,K] outputs
     int32_t pool_stride;     // P-dimension stride of [T,P] outputs
     int32_t sel_t_stride;    // T-dimension stride (elements) of selected outputs
@@ -92,6 +92,14 @@ struct DecodeParams {
     float* merge_state;            // [B][4][max K]: raw, len, ended, prefix length
     const uint8_t* row_allow;
     int32_t force_seq;
+    // Short row lists (many-example relaxed-pool decodes): the one live row
+    // of step 0, (t=0, k=0), gets a list of up to min(N, K*C) entries in the
+    // list space of step 0's K rows (the other K-1 rows of step 0 are never
+    // extended). The main row scan skips that row; a second launch with
+    // first_rows_only = 1 scans exactly those rows (claim i -> row_prefix[i]);
+    // the step merge reads step 0 as that one list.
+    int32_t first_row_apart;
+    int32_t first_rows_only;
     // workspace
     uint64_t* lists;              // row lists, key = ord(lp)<<32 | ~token
     int32_t* list_count;          // [total_rows]

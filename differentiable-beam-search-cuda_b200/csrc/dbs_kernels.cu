@@ -666,6 +666,7 @@ struct RowJob {
     int eos;
     bool eos_blocked;
     bool dead;   // never read: no live parent can extend it
+    bool apart;  // scanned by the launch for the step-0 rows
     const uint8_t* banned;
     const uint8_t* allow;   // host filter verdicts of this row, or nullptr
     int h;       // unaligned head elements
@@ -692,12 +693,15 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     else j.row = p.x + elem;
     j.r = r;
     j.list_at = d.list_offset + lr * d.C;
-    j.C = d.C;
+    // the live step-0 row of a short-list decode keeps a long list in the
+    // list space of step 0's K rows
+    j.C = p.first_rows_only ? min(d.N, d.K * d.C) : d.C;
     j.forced = d.forced ? d.forced[t] : -1;
     // A decode starts from beam 0 alone (the other beams score -inf), so the
     // rows of the other beams at step 0 can never yield a candidate; like
     // the reference, which scans live parents only, they are not read.
     j.dead = t == 0 && k > 0;
+    j.apart = p.first_row_apart && !p.first_rows_only && t == 0 && k == 0;
     j.eos = d.eos;
     j.eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
     j.banned = d.banned;
@@ -709,7 +713,7 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     if (h > p.V) h = p.V;
     j.h = h;
     j.nv = (p.V - h) >> (4 - kShift);
-    j.chunks = (j.forced >= 0 || j.dead) ? 0 : (j.nv + kScanChunkF4 - 1) / kScanChunkF4;
+    j.chunks = (j.forced >= 0 || j.dead || j.apart) ? 0 : (j.nv + kScanChunkF4 - 1) / kScanChunkF4;
     return j;
 }
 
@@ -741,6 +745,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
         unsigned long long r = 0;
         if (lane == 0) r = atomicAdd(next_row, 1ull);
         r = __shfl_sync(FULL, r, 0);
+        if (p.first_rows_only)   // claim i: the first row of example i
+            return r < static_cast<unsigned long long>(p.B) ? p.row_prefix[r] : INT64_MAX;
         return static_cast<int64_t>(r);
     };
 
@@ -810,7 +816,9 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
         const RowJob& j = cur;
         const int C = j.C;
         uint64_t* out = p.lists + j.list_at;
-        if (j.dead) {
+        if (j.apart) {
+            // listed by the step-0 launch
+        } else if (j.dead) {
             if (lane == 0) {
                 p.list_count[j.r] = 0;
                 p.list_bound[j.r] = -INFINITY;
@@ -1241,8 +1249,11 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         __syncthreads();
 
         // Candidate generation: slot k*C + i holds entry i of row k; an
-        // ended parent's carry candidate takes slot k*C.
+        // ended parent's carry candidate takes slot k*C. Step 0 of a
+        // short-list decode has one live row whose list fills all K*C slots
+        // (slot i holds its entry i: the runs of C slots stay sorted).
         const int M = K * C;
+        const bool long0 = p.first_row_apart && t == 0;
         for (int idx0 = tid; idx0 < M; idx0 += 4 * NT) {
             // four list loads in flight per thread before any is used
             uint64_t lk[4];
@@ -1251,7 +1262,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                 const int idx = idx0 + u * NT;
                 lk[u] = 0;
                 if (idx < M) {
-                    const int k = idx / C;
+                    const int k = long0 ? 0 : idx / C;
                     const int i = idx - k * C;
                     if (i < s.row_cnt[k] && isfinite(s.prev_raw[k]) && !(d.eos >= 0 && s.ended[k]))
                         lk[u] = p.lists[d.list_offset + (row0 - d.row_begin + k) * C + i];
@@ -1261,7 +1272,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
             for (int u = 0; u < 4; ++u) {
             const int idx = idx0 + u * NT;
             if (idx >= M) continue;
-            const int k = idx / C;
+            const int k = long0 ? 0 : idx / C;
             const int i = idx - k * C;
             uint64_t h = 0, l = 0;
             const float pr = s.prev_raw[k];
@@ -1309,8 +1320,10 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
             // come sorted: the list is in (lp desc, token asc) order, and
             // raw = pr + lp and rank = raw * inv only round monotonically.
             // The exception is two lp values rounding to one (rank, raw) with
-            // their tokens out of order; a step with such a pair sorts.
-            // Otherwise the top N is a merge of K sorted runs.
+            // their tokens out of order: such neighbours are swapped (rounds
+            // of odd-even transposition restricted to equal high words, so
+            // nothing else moves) before the top N is merged from the K
+            // sorted runs; a step whose runs stay unsorted sorts.
             uint32_t* meta_a = reinterpret_cast<uint32_t*>(seq_len_a);
             uint32_t* meta_b = reinterpret_cast<uint32_t*>(seq_len_b);
             for (int k = tid; k < K; k += NT) {
@@ -1321,13 +1334,35 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                 }
                 meta_a[k] = (static_cast<uint32_t>(k * C) << 16) | static_cast<uint32_t>(lo);
             }
-            int bad = 0;   // any pair of neighbours out of order (or a gap before a key)
+            int bad = 0;    // neighbours whose high words are out of order (or a gap before a key)
+            int ties = 0;   // neighbours with one high word whose tokens are out of order
             for (int idx = tid; idx < M; idx += NT) {
                 if (idx % C == C - 1) continue;
                 const uint64_t h0 = chi[idx], h1 = chi[idx + 1];
-                if (h1 > h0 || (h0 != 0 && h0 == h1 && clo[idx] < clo[idx + 1])) bad = 1;
+                if (h1 > h0) bad = 1;
+                else if (h0 != 0 && h0 == h1 && clo[idx] < clo[idx + 1]) ties = 1;
             }
-            if (!__syncthreads_or(bad)) {
+            bad = __syncthreads_or(bad);
+            ties = __syncthreads_or(ties);
+            // a group of r equal high words is in order after r rounds; two
+            // quiet rounds in a row (one of each parity) mean every group is
+            int quiet = 0;
+            for (int round = 0; !bad && ties && quiet < 2 && round < 16; ++round) {
+                int swapped = 0;
+                for (int j = tid; 2 * j + (round & 1) + 1 < M; j += NT) {
+                    const int idx = 2 * j + (round & 1);
+                    if (idx % C == C - 1) continue;
+                    if (chi[idx] != 0 && chi[idx] == chi[idx + 1] && clo[idx] < clo[idx + 1]) {
+                        const uint64_t l0 = clo[idx];
+                        clo[idx] = clo[idx + 1];
+                        clo[idx + 1] = l0;
+                        swapped = 1;
+                    }
+                }
+                quiet = __syncthreads_or(swapped) ? 0 : quiet + 1;
+            }
+            if (ties && quiet < 2) bad = 1;   // still unsorted after 16 rounds: sort the step
+            if (!bad) {
                 int n_res = 0;
                 const int w = block_merge_runs(chi, clo, sel_hi, sel_lo, meta_a, meta_b, K, N, &n_res);
                 const int lim = N < M ? N : M;
@@ -1374,6 +1409,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         if (sh_any_unsafe) {
             // Rescan the unproven rows from HBM and merge in every dropped
             // candidate that beats the current N-th (rare path).
+            const int stage_room = cand_cap - N;
             for (int k = 0; k < K; ++k) {
                 if (!s.unsafe[k]) continue;
                 if (tid == 0 && p.counters) atomicAdd(p.counters + 1, 1ull);
@@ -1386,10 +1422,136 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                 const int m_tok = list_token(last);
                 const int32_t* pre = need_seq ? seq_a + static_cast<int64_t>(k) * seq_T : nullptr;
                 const int plen = need_seq ? sl_prev[k] : 0;
-                // Candidates that beat G are staged behind the top N and merged
-                // in whenever the staging room could overflow (and at the end
-                // of the row); G only improves, so it is re-read per chunk.
-                const int stage_room = cand_cap - N;
+                // lp floor for the N-th candidate G = (gh, .): a value f whose
+                // candidate, formed with the same roundings, has a high word
+                // below G's; rounding is monotone, so no lp <= f can beat G (a
+                // penalised lp is lower still). -inf when that cannot be shown.
+                auto floor_of = [&](uint64_t gh) {
+                    float floor_lp = -INFINITY;
+                    if (gh != 0) {
+                        const float rg = cand_rank(gh);
+                        float f = __fsub_rn(__fdiv_rn(rg, inv), pr);
+                        f = __fsub_rn(f, (fabsf(f) + fabsf(pr) + 1.0f) * 1e-3f);
+                        const float rawf = __fadd_rn(pr, f);
+                        const float rankf = __fmul_rn(rawf, inv);
+                        if (isfinite(f) && isfinite(rawf) && isfinite(rankf) && cand_hi(rankf, rawf) < gh) floor_lp = f;
+                    }
+                    return floor_lp;
+                };
+                // The candidate of token v when the scan dropped it and it
+                // beats G = (gh, gl); false otherwise.
+                auto dropped_winner = [&](int v, float lp, float floor_lp, uint64_t gh, uint64_t gl, uint64_t& h,
+                                          uint64_t& l) -> bool {
+                    if (lp <= floor_lp) return false;   // (NaN falls through to the check below)
+                    if (forced >= 0 && v != forced) return false;
+                    if (d.banned && d.banned[v]) return false;
+                    if (eos_blocked && v == d.eos) return false;
+                    if (p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v]) return false;
+                    if (!isfinite(lp)) return false;
+                    const float lpc = __fadd_rn(lp, 0.0f);
+                    if (lpc > m_lp || (lpc == m_lp && v <= m_tok)) return false;  // already listed
+                    if (need_seq) {
+                        if (use_ngram) {
+                            const bool bl = (p.no_repeat_ngram == 1)
+                                                ? in_list(pre, plen, v)
+                                                : in_list(blk + static_cast<int64_t>(k) * seq_T, s.blocked_n[k], v);
+                            if (bl) return false;
+                        }
+                        if (use_rep && in_list(pre, plen, v)) lp = __fsub_rn(lp, p.log_repetition_penalty);
+                    }
+                    const float raw = __fadd_rn(pr, lp);
+                    if (raw == -INFINITY) return false;
+                    const float rank = __fmul_rn(raw, inv);
+                    h = cand_hi(rank, raw);
+                    l = cand_lo(k, v);
+                    return key2_less(gh, gl, h, l);
+                };
+                // Merges the `staged` keys behind the top N into it; leaves
+                // the stage empty. Called by all threads.
+                auto merge_staged = [&](int staged) {
+                    if (staged <= 64) {
+                        // A few staged keys (the usual case): the final
+                        // position of a key of the sorted top N is its
+                        // index plus the staged keys above it; that of a
+                        // staged key is the top-N keys above it (binary
+                        // search) plus the staged keys above it. Keys are
+                        // unique, so the positions below N are distinct.
+                        for (int i = tid; i < N + staged; i += NT) {
+                            const uint64_t h = chi[i], l = clo[i];
+                            int pos = 0;
+                            if (i < N) {
+                                pos = i;
+                                for (int q = N; q < N + staged; ++q) pos += key2_less(h, l, chi[q], clo[q]) ? 1 : 0;
+                            } else {
+                                int lo = 0, hi = N;   // top-N keys above (h, l)
+                                while (lo < hi) {
+                                    const int mid = (lo + hi) >> 1;
+                                    if (key2_less(h, l, chi[mid], clo[mid])) lo = mid + 1; else hi = mid;
+                                }
+                                pos = lo;
+                                for (int q = N; q < N + staged; ++q) pos += key2_less(h, l, chi[q], clo[q]) ? 1 : 0;
+                            }
+                            if (pos < N) {
+                                sel_hi[pos] = h;
+                                sel_lo[pos] = l;
+                            }
+                        }
+                        __syncthreads();
+                        for (int i = tid; i < N; i += NT) {
+                            chi[i] = sel_hi[i];
+                            clo[i] = sel_lo[i];
+                        }
+                    } else if (N + staged > 1024) {
+                        block_top_n_u128(chi, clo, N + staged, N, sel_hi, sel_lo, sel_cap);
+                    } else {
+                        block_sort_desc_u128(chi, clo, N + staged);
+                    }
+                    for (int i = N + tid; i < N + staged; i += NT) { chi[i] = 0; clo[i] = 0; }
+                    __syncthreads();
+                    if (tid == 0) sh_stage = 0;
+                    __syncthreads();
+                };
+
+                // One sweep against the G of the row's start: 16 loads per
+                // thread in flight, no barrier until the row ends, winners
+                // staged through a shared counter and merged once. If more
+                // winners than the staging room holds turn up (G far from
+                // settled), the row is swept again in batches that merge as
+                // they go.
+                {
+                    const uint64_t gh = (N - 1 < M) ? chi[N - 1] : 0;
+                    const uint64_t gl = (N - 1 < M) ? clo[N - 1] : 0;
+                    const float floor_lp = floor_of(gh);
+                    for (int base = 0; base < V; base += 16 * NT) {
+                        float lv[16];
+#pragma unroll
+                        for (int r = 0; r < 16; ++r) {
+                            const int v = base + r * NT + tid;
+                            lv[r] = v < V ? lp_at(p, row + v) : -INFINITY;
+                        }
+#pragma unroll
+                        for (int r = 0; r < 16; ++r) {
+                            const int v = base + r * NT + tid;
+                            uint64_t h, l;
+                            if (v < V && dropped_winner(v, lv[r], floor_lp, gh, gl, h, l)) {
+                                const int pos = atomicAdd(&sh_stage, 1);
+                                if (pos < stage_room) {
+                                    chi[N + pos] = h;
+                                    clo[N + pos] = l;
+                                }
+                            }
+                        }
+                    }
+                }
+                __syncthreads();
+                const int swept = sh_stage;
+                __syncthreads();
+                if (swept <= stage_room) {
+                    if (swept > 0) merge_staged(swept);
+                    continue;
+                }
+                if (tid == 0) sh_stage = 0;
+                __syncthreads();
                 // Sub-batches of 4 values per thread (4 NT <= 2048 <= the
                 // room); four sub-batches (16 loads per thread) are in flight
                 // before the first is used. After each sub-batch the staged
@@ -1405,103 +1567,26 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                     }
 #pragma unroll
                     for (int sb = 0; sb < 4; ++sb) {
-                    const int sbase = base + sb * sub;
-                    if (sbase >= V) break;
-                    const uint64_t gh = (N - 1 < M) ? chi[N - 1] : 0;
-                    const uint64_t gl = (N - 1 < M) ? clo[N - 1] : 0;
-                    // lp floor: a value f whose candidate, formed with the same
-                    // roundings, has a high word below G's; rounding is
-                    // monotone, so no lp <= f can beat G (a penalised lp is
-                    // lower still). -inf when that cannot be shown.
-                    float floor_lp = -INFINITY;
-                    if (gh != 0) {
-                        const float rg = cand_rank(gh);
-                        float f = __fsub_rn(__fdiv_rn(rg, inv), pr);
-                        f = __fsub_rn(f, (fabsf(f) + fabsf(pr) + 1.0f) * 1e-3f);
-                        const float rawf = __fadd_rn(pr, f);
-                        const float rankf = __fmul_rn(rawf, inv);
-                        if (isfinite(f) && isfinite(rawf) && isfinite(rankf) && cand_hi(rankf, rawf) < gh) floor_lp = f;
-                    }
+                        const int sbase = base + sb * sub;
+                        if (sbase >= V) break;
+                        const uint64_t gh = (N - 1 < M) ? chi[N - 1] : 0;
+                        const uint64_t gl = (N - 1 < M) ? clo[N - 1] : 0;
+                        const float floor_lp = floor_of(gh);
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int v = sbase + u * NT + tid;
-                        if (v >= V) continue;
-                        float lp = lv[sb * 4 + u];
-                        if (lp <= floor_lp) continue;   // (NaN falls through to the check below)
-                        if (forced >= 0 && v != forced) continue;
-                        if (d.banned && d.banned[v]) continue;
-                        if (eos_blocked && v == d.eos) continue;
-                        if (p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v]) continue;
-                        if (!isfinite(lp)) continue;
-                        const float lpc = __fadd_rn(lp, 0.0f);
-                        if (lpc > m_lp || (lpc == m_lp && v <= m_tok)) continue;  // already listed
-                        if (need_seq) {
-                            if (use_ngram) {
-                                const bool bl = (p.no_repeat_ngram == 1)
-                                                    ? in_list(pre, plen, v)
-                                                    : in_list(blk + static_cast<int64_t>(k) * seq_T, s.blocked_n[k], v);
-                                if (bl) continue;
+                        for (int u = 0; u < 4; ++u) {
+                            const int v = sbase + u * NT + tid;
+                            uint64_t h, l;
+                            if (v < V && dropped_winner(v, lv[sb * 4 + u], floor_lp, gh, gl, h, l)) {
+                                const int pos = atomicAdd(&sh_stage, 1);
+                                chi[N + pos] = h;
+                                clo[N + pos] = l;
                             }
-                            if (use_rep && in_list(pre, plen, v)) lp = __fsub_rn(lp, p.log_repetition_penalty);
                         }
-                        const float raw = __fadd_rn(pr, lp);
-                        if (raw == -INFINITY) continue;
-                        const float rank = __fmul_rn(raw, inv);
-                        const uint64_t h = cand_hi(rank, raw);
-                        const uint64_t l = cand_lo(k, v);
-                        if (key2_less(gh, gl, h, l)) {
-                            const int pos = atomicAdd(&sh_stage, 1);
-                            chi[N + pos] = h;
-                            clo[N + pos] = l;
-                        }
-                    }
-                    __syncthreads();
-                    const int staged = sh_stage;
-                    __syncthreads();   // every thread holds the count before the next sub-batch stages
-                    const bool last_sub = sbase + sub >= V;
-                    if (staged > 0 && (last_sub || staged > stage_room - sub)) {
-                        if (staged <= 64) {
-                            // A few staged keys (the usual case): the final
-                            // position of a key of the sorted top N is its
-                            // index plus the staged keys above it; that of a
-                            // staged key is the top-N keys above it (binary
-                            // search) plus the staged keys above it. Keys are
-                            // unique, so the positions below N are distinct.
-                            for (int i = tid; i < N + staged; i += NT) {
-                                const uint64_t h = chi[i], l = clo[i];
-                                int pos = 0;
-                                if (i < N) {
-                                    pos = i;
-                                    for (int q = N; q < N + staged; ++q) pos += key2_less(h, l, chi[q], clo[q]) ? 1 : 0;
-                                } else {
-                                    int lo = 0, hi = N;   // top-N keys above (h, l)
-                                    while (lo < hi) {
-                                        const int mid = (lo + hi) >> 1;
-                                        if (key2_less(h, l, chi[mid], clo[mid])) lo = mid + 1; else hi = mid;
-                                    }
-                                    pos = lo;
-                                    for (int q = N; q < N + staged; ++q) pos += key2_less(h, l, chi[q], clo[q]) ? 1 : 0;
-                                }
-                                if (pos < N) {
-                                    sel_hi[pos] = h;
-                                    sel_lo[pos] = l;
-                                }
-                            }
-                            __syncthreads();
-                            for (int i = tid; i < N; i += NT) {
-                                chi[i] = sel_hi[i];
-                                clo[i] = sel_lo[i];
-                            }
-                        } else if (N + staged > 1024) {
-                            block_top_n_u128(chi, clo, N + staged, N, sel_hi, sel_lo, sel_cap);
-                        } else {
-                            block_sort_desc_u128(chi, clo, N + staged);
-                        }
-                        for (int i = N + tid; i < N + staged; i += NT) { chi[i] = 0; clo[i] = 0; }
                         __syncthreads();
-                        if (tid == 0) sh_stage = 0;
-                        __syncthreads();
-                    }
+                        const int staged = sh_stage;
+                        __syncthreads();   // every thread holds the count before the next sub-batch stages
+                        const bool last_sub = sbase + sub >= V;
+                        if (staged > 0 && (last_sub || staged > stage_room - sub)) merge_staged(staged);
                     }
                 }
             }
@@ -2664,7 +2749,8 @@ constexpr size_t kMergeRankSmemBudget = 200 * 1024;
 
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T, int max_N,
                               bool need_sequences, cudaStream_t stream) {
-    if (!need_sequences && static_cast<int64_t>(max_K) * max_C <= 256) {
+    // (the ranking merge reads every row as one list of at most C entries)
+    if (!need_sequences && !p.first_row_apart && static_cast<int64_t>(max_K) * max_C <= 256) {
         const int tab_n = (p.Lmax + 1 <= 4096) ? p.Lmax + 1 : 0;
         int ring = max_T < kMergeRingMax ? max_T : kMergeRingMax;
         if (ring < 2) ring = 2;

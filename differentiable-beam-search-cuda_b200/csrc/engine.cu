@@ -418,6 +418,26 @@ int list_capacity(const Options& opt, int K, bool pool, bool dynamic) {
     return list_capacity_for(pool ? P : K, K, dynamic);
 }
 
+// Short row lists for relaxed-pool decodes of many examples. A step's pool
+// (P = 8K by default) is spread over the beams' rows: on log_softmax(N(0,1))
+// rows of 50257 tokens a row holds more than 64 of a step's pool entries
+// about 0.3 times per step at K = 32 (0.8 at K = 64, 1.8 at K = 128). Lists
+// of 64 entries keep the row scan near the copy rate (5.4 TB/s against
+// 3.5 TB/s with 256-entry lists); the merge proves every other row per step
+// and rescans the few that could hold more from HBM, so the selection stays
+// exact. Step 0 has one live row, which holds the whole pool: it gets a list
+// of up to K*64 entries in the list space of step 0's rows (the other beams'
+// rows at step 0 are never extended). The saving grows with the rows a
+// call scans (the speculative scan needs many rows per warp) while the
+// rescans cost each example's merge a fixed time, and the merges of many
+// examples run side by side; so short lists need at least 32 examples and
+// 64K rows (measured with T = 64: K = 32, 256 examples 33.5 -> 22.2 ms and
+// 32 examples 5.8 -> 4.9 ms; K = 64, 128 examples 25.8 -> 22.5 ms; but
+// K = 16 with 32 examples, 32K rows, 2.73 -> 2.88 ms).
+constexpr int kShortListEntries = 64;
+constexpr int kShortListMinExamples = 32;
+constexpr int64_t kShortListMinRows = 65536;
+
 void decode(const Options& opt, const float* d_x, int V, const std::vector<ExampleSpec>& ex,
             const CallConstraints& cons, const Outputs& out, const Layout& layout, bool pool,
             bool weights, cudaStream_t stream, DecodeStats* stats, const DecodeControl& ctl) {
@@ -426,15 +446,33 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     HostTrace trace("decode");
     const bool dynamic = cons.repetition_penalty > 1.0f || cons.no_repeat_ngram > 0 || ctl.force_seq;
 
+    const bool ext_lists = ctl.lists != nullptr;
+    bool short_lists = false;
+    if (pool && !dynamic && !ext_lists && B >= kShortListMinExamples && ctl.scan && ctl.merge &&
+        ctl.t_begin <= 0 && !ctl.merge_state && !ctl.row_allow) {
+        int kmax = 0;
+        int64_t nrows = 0;
+        bool cut = false;   // some example's full list would be longer
+        for (const ExampleSpec& e : ex) {
+            kmax = std::max(kmax, e.K);
+            nrows += static_cast<int64_t>(e.T) * e.K;
+            const int N = std::max(e.K, e.K * opt.relaxed_pool_multiplier);
+            cut = cut || list_capacity_for(N, e.K, false) > kShortListEntries;
+        }
+        // (calls whose merge would be the ranking merge keep full lists)
+        short_lists = cut && nrows >= kShortListMinRows && static_cast<int64_t>(kmax) * kShortListEntries > 256;
+    }
+
     std::vector<dbs_dev::ExampleDesc> desc(B);
     std::vector<int64_t> row_prefix(B + 1, 0);
-    int max_T = 0, max_K = 0, max_C = 0, max_N = 0, max_P = 0;
+    int max_T = 0, max_K = 0, max_C = 0, max_N = 0, max_P = 0, max_C0 = 0;
     int64_t rows = 0, list_entries = 0;
     for (int b = 0; b < B; ++b) {
         const ExampleSpec& e = ex[b];
         const int P = layout.P[b];
         const int N = pool ? P : e.K;
-        const int C = list_capacity_for(N, e.K, dynamic);
+        int C = list_capacity_for(N, e.K, dynamic);
+        if (short_lists && C > kShortListEntries) C = kShortListEntries;
         if (e.K > 1024) throw LengthError("beam_size above 1024 is not supported by the device decoder");
         dbs_dev::ExampleDesc& d = desc[b];
         d.x_offset = e.x_offset;
@@ -465,6 +503,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         max_T = std::max(max_T, e.T);
         max_K = std::max(max_K, e.K);
         max_C = std::max(max_C, C);
+        max_C0 = std::max(max_C0, std::min(N, e.K * C));   // step-0 list of a short-list decode
         max_N = std::max(max_N, N);
         max_P = std::max(max_P, P);
     }
@@ -479,7 +518,6 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     // counters] [lists | counts | bounds | prefixes]. The header is staged in
     // pinned memory (status and counters zeroed there) and uploaded with one
     // asynchronous copy.
-    const bool ext_lists = ctl.lists != nullptr;
     const int64_t scan_begin = std::max<int64_t>(0, ctl.scan_begin);
     const int64_t scan_end = ctl.scan_end < 0 ? rows : std::min<int64_t>(rows, ctl.scan_end);
     // One example whose merge is the selection merge (one CTA, T dependent
@@ -565,6 +603,8 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     p.merge_state = ctl.merge_state;
     p.row_allow = ctl.row_allow;
     p.force_seq = ctl.force_seq ? 1 : 0;
+    p.first_row_apart = short_lists ? 1 : 0;
+    p.first_rows_only = 0;
 
     p.x = d_x;
     p.x16 = ctl.x16;
@@ -702,6 +742,15 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
             ps_p.total_rows = scan_end;   // rows are claimed from scan_begin up to here
             check_cuda(dbs_dev::launch_row_scan(ps_p, max_C, device_sm_count(), stream, scan_end - scan_begin),
                        "row scan kernel");
+            if (short_lists) {
+                // the live step-0 row of every example, with its long list
+                // (claims restart at 0: claim i is example i's first row)
+                check_cuda(cudaMemsetAsync(p.counters + 2, 0, sizeof(unsigned long long), stream),
+                           "row claim reset");
+                ps_p.first_rows_only = 1;
+                check_cuda(dbs_dev::launch_row_scan(ps_p, max_C0, device_sm_count(), stream, B),
+                           "row scan kernel (step 0)");
+            }
         }
         trace.mark("row scan queued");
         if (validate) {
