@@ -459,12 +459,16 @@ constexpr int kScanWarpsPerCta = 4;
 __host__ __device__ constexpr int row_scan_hist_ints(int capw, bool k16) {
     return capw - (k16 ? 128 : 0) > 2 * 32 + 136 ? 256 : 0;
 }
+// Speculative thresholds a warp remembers, one per list length (rows of
+// one call can have different list lengths, e.g. per-example beam sizes).
+constexpr int kSpecSlots = 4;
 // Per-warp shared memory: chunk ring | mbarriers | survivor buffer | radix
-// histogram, 128-byte aligned.
+// histogram | speculation slots (threshold, list length), 128-byte aligned.
 __host__ __device__ constexpr size_t row_scan_warp_bytes(int capw, bool k16) {
     return ((static_cast<size_t>(kScanStages) * kScanChunkF4 * 16 + kScanStages * sizeof(uint64_t) +
              static_cast<size_t>(capw) * sizeof(uint64_t) +
-             static_cast<size_t>(row_scan_hist_ints(capw, k16)) * sizeof(int)) + 127) & ~static_cast<size_t>(127);
+             static_cast<size_t>(row_scan_hist_ints(capw, k16)) * sizeof(int) + kSpecSlots * 8) + 127) &
+           ~static_cast<size_t>(127);
 }
 
 __device__ __forceinline__ void warp_sort_desc_u64(uint64_t* a, int n, int lane) {
@@ -730,6 +734,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     uint64_t* full = reinterpret_cast<uint64_t*>(base + ring_bytes);
     uint64_t* buf = full + kScanStages;
     int* hist = reinterpret_cast<int*>(buf + capw);
+    float* spec_lp = reinterpret_cast<float*>(hist + hist_ints);   // [kSpecSlots]
+    int* spec_len = reinterpret_cast<int*>(spec_lp + kSpecSlots);   // [kSpecSlots], 0 = empty
     unsigned long long* err = p.counters ? p.counters + 3 : nullptr;
     unsigned long long* next_row = p.counters + 2;
     const bool bf16 = p.x16_bf16 != 0;
@@ -738,6 +744,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     if (lane == 0) {
         for (int s = 0; s < kScanStages; ++s) mbar_init(full + s, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int s = 0; s < kSpecSlots; ++s) spec_len[s] = 0;
     }
     __syncwarp();
 
@@ -805,12 +812,15 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
 
     // Lists longer than 32 (when each warp scans many rows): the warp starts
     // a row at a speculative threshold, the (C + 4 sqrt(C))-th largest lp of
-    // the previous row it scanned (the rank of a row's C-th value varies by
-    // about sqrt(C) between rows of one distribution). If fewer than C
-    // entries reach it the row is scanned again from global memory, so the
-    // list stays exact; otherwise far fewer elements take the slow path than
-    // with a threshold that starts at -FLT_MAX.
-    float spec = -FLT_MAX;
+    // the last row with the same list length C it scanned (the rank of a
+    // row's C-th value varies by about sqrt(C) between rows of one
+    // distribution). If fewer than C entries reach it the row is scanned
+    // again from global memory, so the list stays exact; otherwise far fewer
+    // elements take the slow path than with a threshold that starts at
+    // -FLT_MAX. The guesses are kept per list length (a few slots, by a hash
+    // of C): consecutive rows of a warp come from different examples, whose
+    // beam sizes may differ.
+    auto spec_slot = [](int c) { return static_cast<int>((static_cast<uint32_t>(c) * 2654435761u) >> 30); };
     while (true) {
         issue_more();
         const RowJob& j = cur;
@@ -835,6 +845,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             }
         } else {
             int cnt = 0;
+            const int slot = spec_slot(C);
+            const float spec = spec_len[slot] == C ? spec_lp[slot] : -FLT_MAX;
             const bool spec_used = speculate && C > 32 && hist_ints && spec > -FLT_MAX;
             float thr = spec_used ? spec : -FLT_MAX;
             float rej = -INFINITY;
@@ -1070,8 +1082,15 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 cnt = warp_compact_select(buf, cnt, k_spec, lane, hist, thr, evict);
             warp_sort_desc_u64(buf, cnt, lane);
             if (C > 32 && hist_ints) {
-                if (cnt >= k_spec) spec = list_lp(buf[k_spec - 1]);
-                else if (missed) spec = cnt > 0 ? list_lp(buf[cnt - 1]) : -FLT_MAX;   // lower it after a miss
+                float next = spec;
+                if (cnt >= k_spec) next = list_lp(buf[k_spec - 1]);
+                else if (missed) next = cnt > 0 ? list_lp(buf[cnt - 1]) : -FLT_MAX;   // lower it after a miss
+                __syncwarp();
+                if (lane == 0) {
+                    spec_lp[slot] = next;
+                    spec_len[slot] = C;
+                }
+                __syncwarp();
             }
             const int keep = cnt < C ? cnt : C;
             for (int i = lane; i < keep; i += 32) out[i] = buf[i];
@@ -2698,7 +2717,7 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
         err = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
         if (err != cudaSuccess) return err;
         const int per_warp = ((per_sm_smem / 4 - reserved) / kScanWarpsPerCta) & ~127;
-        const int fixed = kScanStages * kScanChunkF4 * 16 + kScanStages * 8 + 256 * 4;
+        const int fixed = kScanStages * kScanChunkF4 * 16 + kScanStages * 8 + 256 * 4 + kSpecSlots * 8;
         const int fit = (per_warp - fixed) / 8;
         const int lowest = max_C + (k16 ? 256 : 128) + 8 + 32;
         if (fit >= lowest && fit < capw) capw = fit;
