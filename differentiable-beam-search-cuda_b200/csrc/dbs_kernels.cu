@@ -863,10 +863,35 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 if (keep) buf[cnt + __popc(b & lt_mask)] = list_key(lp, v);
                 cnt += __popc(b);
             };
-            // Rows without banned tokens, EOS block or host verdicts (the
-            // common case) only exclude +inf: no per-value branches. Padding
-            // values are -inf, which is never kept and leaves rej unchanged.
-            const bool plain = !j.banned && !j.eos_blocked && !j.allow;
+            // Rows without host verdicts append survivors without per-value
+            // branches (only +inf is excluded; padding values are -inf, never
+            // kept, leaving rej unchanged). Banned tokens and a blocked EOS,
+            // which a row has few of, are removed from the survivor buffer
+            // afterwards, before each compaction and at the end of the row:
+            // a threshold only ever comes from allowed entries.
+            const bool plain = !j.allow;
+            const bool deferred = j.banned || j.eos_blocked;
+            const int eos_cut = j.eos_blocked ? j.eos : -1;
+            auto drop_disallowed = [&]() {
+                if (!deferred) return;
+                __syncwarp();
+                int w = 0;   // order-preserving, in place (writes stay below the next reads)
+                for (int base = 0; base < cnt; base += 32) {
+                    const int i = base + lane;
+                    const uint64_t key = i < cnt ? buf[i] : 0;
+                    bool ok = false;
+                    if (i < cnt) {
+                        const int v = list_token(key);
+                        ok = v != eos_cut && !(j.banned && j.banned[v]);
+                    }
+                    const unsigned b = __ballot_sync(FULL, ok);
+                    __syncwarp();
+                    if (ok) buf[w + __popc(b & lt_mask)] = key;
+                    w += __popc(b);
+                    __syncwarp();
+                }
+                cnt = w;
+            };
             auto consider_plain = [&](int v, float lp) {
                 const bool pass = lp >= thr;
                 if (!pass) rej = fmaxf(rej, lp);
@@ -876,6 +901,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 cnt += __popc(b);
             };
             auto compact = [&]() {
+                drop_disallowed();
                 __syncwarp();
                 if (C > 32 && hist_ints) {
                     cnt = warp_compact_select(buf, cnt, C, lane, hist, thr, evict);
@@ -1031,6 +1057,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 consider(in, t0 + lane, lp);
             }
             __syncwarp();
+            drop_disallowed();
             const int k_spec = C + static_cast<int>(4.0f * sqrtf(static_cast<float>(C)));
             const bool missed = spec_used && cnt < C;
             if (missed) {
@@ -1075,6 +1102,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                     if (cnt > capw - 128 - 8) compact();
                 }
                 __syncwarp();
+                drop_disallowed();
             }
             // long lists: cut to k_spec entries (the next row's speculative
             // threshold comes from there) before the one full sort of the row
@@ -1154,22 +1182,6 @@ __device__ __forceinline__ int cand_token(uint64_t lo) {
 __device__ __forceinline__ float cand_rank(uint64_t hi) { return unord_f32(static_cast<uint32_t>(hi >> 32)); }
 __device__ __forceinline__ float cand_raw(uint64_t hi) { return unord_f32(static_cast<uint32_t>(hi)); }
 
-// would_repeat_ngram (src/differentiable_beam.cpp:305-325) for n >= 2 turned
-// into the set of tokens it rejects for one prefix.
-__device__ int ngram_blocked_set(const int32_t* pre, int plen, int n, int32_t* out) {
-    int cnt = 0;
-    if (plen + 1 < n) return 0;
-    const int suffix = plen - (n - 1);
-    for (int i = 0; i + n <= plen; ++i) {
-        bool same = true;
-        for (int j = 0; j < n - 1; ++j) {
-            if (pre[i + j] != pre[suffix + j]) { same = false; break; }
-        }
-        if (same) out[cnt++] = pre[i + n - 1];
-    }
-    return cnt;
-}
-
 __device__ __forceinline__ bool in_list(const int32_t* a, int n, int v) {
     for (int i = 0; i < n; ++i)
         if (a[i] == v) return true;
@@ -1179,9 +1191,16 @@ __device__ __forceinline__ bool in_list(const int32_t* a, int n, int v) {
 // kRuns: the instance for up to 1024 candidates per step, which merges the
 // sorted row runs when no sequence constraint is active (the larger-step
 // instance leaves that code out: it costs registers on the selection path).
+// Per-beam prefix filters of the step merge (repetition penalty, 1-gram
+// blocking): 1024 bits, two bits per token; a token whose two bits are not
+// both set is not in the prefix, and only the others scan it.
+constexpr int kBloomWords = 32;
+__device__ __forceinline__ uint32_t bloom_h1(int v) { return static_cast<uint32_t>(v) & 1023u; }
+__device__ __forceinline__ uint32_t bloom_h2(int v) { return (static_cast<uint32_t>(v) * 2654435761u) >> 22; }
+
 template <bool kRuns>
 __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodeParams p, int cand_cap,
-                                                                   int seq_T, int seq_K, int sel_cap) {
+                                                                   int seq_T, int seq_K, int sel_cap, int bloom_on) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     const ExampleDesc d = p.desc[e];
@@ -1246,22 +1265,70 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
     if (need_seq && (t_first & 1)) {   // the prefix buffers swap once per step
         int32_t* tmp = seq_a; seq_a = seq_b; seq_b = tmp;
     }
+    // prefix filters (with the prefixes of an earlier launch, if any)
+    const bool use_bloom = need_seq && bloom_on;
+    uint32_t* bloom_a = use_bloom ? reinterpret_cast<uint32_t*>(sel_lo + sel_cap) : nullptr;
+    uint32_t* bloom_b = use_bloom ? bloom_a + seq_K * kBloomWords : nullptr;
+    if (use_bloom) {
+        for (int i = tid; i < K * kBloomWords; i += NT) bloom_a[i] = 0;
+    }
     __syncthreads();
+    if (use_bloom && t_first > 0) {
+        for (int idx = tid; idx < K * seq_T; idx += NT) {
+            const int k = idx / seq_T;
+            const int i = idx - k * seq_T;
+            if (i < sl_prev[k]) {
+                const int v = seq_a[static_cast<int64_t>(k) * seq_T + i];
+                atomicOr(bloom_a + k * kBloomWords + (bloom_h1(v) >> 5), 1u << (bloom_h1(v) & 31));
+                atomicOr(bloom_a + k * kBloomWords + (bloom_h2(v) >> 5), 1u << (bloom_h2(v) & 31));
+            }
+        }
+    }
+    __syncthreads();
+    // token v in beam k's prefix
+    auto in_prefix = [&](int k, int v) {
+        if (use_bloom) {
+            const uint32_t* bl = bloom_a + k * kBloomWords;
+            const uint32_t a = bloom_h1(v), b = bloom_h2(v);
+            if (!((bl[a >> 5] >> (a & 31)) & (bl[b >> 5] >> (b & 31)) & 1u)) return false;
+        }
+        return in_list(seq_a + static_cast<int64_t>(k) * seq_T, sl_prev[k], v);
+    };
 
     for (int t = t_first; t < t_stop; ++t) {
         const int64_t row0 = d.row_begin + static_cast<int64_t>(t) * K;
         const int forced = d.forced ? d.forced[t] : -1;
         const bool eos_blocked = d.eos >= 0 && (t + 1) < d.min_length;
+        const bool ngram_sets = use_ngram && p.no_repeat_ngram >= 2;
         for (int k = tid; k < K; k += NT) {
             s.row_cnt[k] = p.list_count[row0 + k];
             s.row_bound[k] = p.list_bound[row0 + k];
             s.unsafe[k] = 0;
-            if (use_ngram && p.no_repeat_ngram >= 2 && isfinite(s.prev_raw[k]) &&
-                !(d.eos >= 0 && s.ended[k])) {
-                s.blocked_n[k] = ngram_blocked_set(seq_a + static_cast<int64_t>(k) * seq_T, sl_prev[k],
-                                                   p.no_repeat_ngram, blk + static_cast<int64_t>(k) * seq_T);
-            } else if (k < K) {
-                s.blocked_n[k] = 0;
+            if (!ngram_sets) s.blocked_n[k] = 0;
+        }
+        if (ngram_sets) {
+            // would_repeat_ngram (src/differentiable_beam.cpp:305-325) as the
+            // set of tokens it rejects after each live beam's prefix: one
+            // warp per beam, lane i testing the n-gram that starts at i
+            const int n = p.no_repeat_ngram;
+            const int lane = tid & 31;
+            for (int k = tid >> 5; k < K; k += NT >> 5) {
+                int cnt = 0;
+                const int plen = sl_prev[k];
+                if (isfinite(s.prev_raw[k]) && !(d.eos >= 0 && s.ended[k]) && plen + 1 >= n) {
+                    const int32_t* pre = seq_a + static_cast<int64_t>(k) * seq_T;
+                    int32_t* out = blk + static_cast<int64_t>(k) * seq_T;
+                    const int suffix = plen - (n - 1);
+                    for (int base = 0; base + n <= plen; base += 32) {
+                        const int i = base + lane;
+                        bool same = i + n <= plen;
+                        for (int q = 0; q < n - 1 && same; ++q) same = pre[i + q] == pre[suffix + q];
+                        const unsigned b = __ballot_sync(0xFFFFFFFFu, same);
+                        if (same) out[cnt + __popc(b & ((1u << lane) - 1u))] = pre[i + n - 1];
+                        cnt += __popc(b);
+                    }
+                }
+                if (lane == 0) s.blocked_n[k] = cnt;
             }
         }
         if (tid == 0) { sh_any_unsafe = 0; sh_stage = 0; }
@@ -1309,13 +1376,11 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                     const int v = list_token(key);
                     bool ok = true;
                     if (need_seq) {
-                        const int32_t* pre = seq_a + static_cast<int64_t>(k) * seq_T;
-                        const int plen = sl_prev[k];
                         if (use_ngram) {
-                            if (p.no_repeat_ngram == 1) ok = !in_list(pre, plen, v);
+                            if (p.no_repeat_ngram == 1) ok = !in_prefix(k, v);
                             else ok = !in_list(blk + static_cast<int64_t>(k) * seq_T, s.blocked_n[k], v);
                         }
-                        if (ok && use_rep && in_list(pre, plen, v))
+                        if (ok && use_rep && in_prefix(k, v))
                             lp = __fsub_rn(lp, p.log_repetition_penalty);
                     }
                     if (ok) {
@@ -1439,8 +1504,6 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                 const uint64_t last = p.lists[d.list_offset + (row0 - d.row_begin + k) * C + (cnt - 1)];
                 const float m_lp = list_lp(last);
                 const int m_tok = list_token(last);
-                const int32_t* pre = need_seq ? seq_a + static_cast<int64_t>(k) * seq_T : nullptr;
-                const int plen = need_seq ? sl_prev[k] : 0;
                 // lp floor for the N-th candidate G = (gh, .): a value f whose
                 // candidate, formed with the same roundings, has a high word
                 // below G's; rounding is monotone, so no lp <= f can beat G (a
@@ -1472,11 +1535,11 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                     if (need_seq) {
                         if (use_ngram) {
                             const bool bl = (p.no_repeat_ngram == 1)
-                                                ? in_list(pre, plen, v)
+                                                ? in_prefix(k, v)
                                                 : in_list(blk + static_cast<int64_t>(k) * seq_T, s.blocked_n[k], v);
                             if (bl) return false;
                         }
-                        if (use_rep && in_list(pre, plen, v)) lp = __fsub_rn(lp, p.log_repetition_penalty);
+                        if (use_rep && in_prefix(k, v)) lp = __fsub_rn(lp, p.log_repetition_penalty);
                     }
                     const float raw = __fadd_rn(pr, lp);
                     if (raw == -INFINITY) return false;
@@ -1677,6 +1740,27 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
                     seq_b[static_cast<int64_t>(j) * seq_T + i] = cand_token(l);
             }
         }
+        if (use_bloom) {
+            // filter[j] = filter[parent_j] + token_j (when from a log-prob)
+            for (int idx = tid; idx < K * kBloomWords; idx += NT) {
+                const int j = idx / kBloomWords;
+                const int w = idx - j * kBloomWords;
+                const uint64_t h = (j < M) ? chi[j] : 0;
+                uint32_t bits = 0;
+                if (h != 0) {
+                    const uint64_t l = clo[j];
+                    const int parent = cand_parent(l);
+                    bits = bloom_a[parent * kBloomWords + w];
+                    if (!(d.eos >= 0 && s.ended[parent])) {
+                        const int v = cand_token(l);
+                        const uint32_t a = bloom_h1(v), b = bloom_h2(v);
+                        if (static_cast<int>(a >> 5) == w) bits |= 1u << (a & 31);
+                        if (static_cast<int>(b >> 5) == w) bits |= 1u << (b & 31);
+                    }
+                }
+                bloom_b[idx] = bits;
+            }
+        }
         __syncthreads();
         for (int k = tid; k < K; k += NT) {
             s.prev_raw[k] = s.next_raw[k];
@@ -1686,6 +1770,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         if (need_seq) {
             int32_t* tmp = seq_a; seq_a = seq_b; seq_b = tmp;
             int* tl = sl_prev; sl_prev = sl_next; sl_next = tl;
+            uint32_t* tb = bloom_a; bloom_a = bloom_b; bloom_b = tb;
         }
         __syncthreads();
     }
@@ -2795,10 +2880,13 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     int cand_cap = M;
     if (cand_cap < max_N + 2048) cand_cap = max_N + 2048;
     const int sel_cap = max_N + 2048;
+    // prefix filters of the sequence constraints: two buffers of K filters
+    const int bloom_on = (need_sequences && max_K <= 64) ? 1 : 0;
     const size_t smem = static_cast<size_t>(cand_cap) * 2 * sizeof(uint64_t) +
                         static_cast<size_t>(max_K) * 3 * sizeof(float) +
                         static_cast<size_t>(max_K) * 7 * sizeof(int) + 64 +
-                        16 + static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t);
+                        16 + static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t) +
+                        (bloom_on ? static_cast<size_t>(2) * max_K * kBloomWords * sizeof(uint32_t) : 0);
     // about two candidates per thread (the run merges of a step are bound by
     // shared-memory latency, so more warps help)
     int threads = 64;
@@ -2809,8 +2897,8 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
                           : reinterpret_cast<const void*>(step_merge_kernel<false>);
     cudaError_t err = ensure_dynamic_smem(fn, smem);
     if (err != cudaSuccess) return err;
-    if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap);
-    else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap);
+    if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_on);
+    else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_on);
     return cudaGetLastError();
 }
 
