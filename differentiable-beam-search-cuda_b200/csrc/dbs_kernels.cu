@@ -1182,8 +1182,20 @@ __device__ __forceinline__ int cand_token(uint64_t lo) {
 __device__ __forceinline__ float cand_rank(uint64_t hi) { return unord_f32(static_cast<uint32_t>(hi >> 32)); }
 __device__ __forceinline__ float cand_raw(uint64_t hi) { return unord_f32(static_cast<uint32_t>(hi)); }
 
+// Membership in a short list in global memory: eight independent loads per
+// round instead of one dependent load per entry.
 __device__ __forceinline__ bool in_list(const int32_t* a, int n, int v) {
-    for (int i = 0; i < n; ++i)
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        int32_t w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) w[u] = a[i + u];
+        bool hit = false;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) hit |= w[u] == v;
+        if (hit) return true;
+    }
+    for (; i < n; ++i)
         if (a[i] == v) return true;
     return false;
 }
@@ -1192,15 +1204,17 @@ __device__ __forceinline__ bool in_list(const int32_t* a, int n, int v) {
 // sorted row runs when no sequence constraint is active (the larger-step
 // instance leaves that code out: it costs registers on the selection path).
 // Per-beam prefix filters of the step merge (repetition penalty, 1-gram
-// blocking): 1024 bits, two bits per token; a token whose two bits are not
-// both set is not in the prefix, and only the others scan it.
-constexpr int kBloomWords = 32;
-__device__ __forceinline__ uint32_t bloom_h1(int v) { return static_cast<uint32_t>(v) & 1023u; }
-__device__ __forceinline__ uint32_t bloom_h2(int v) { return (static_cast<uint32_t>(v) * 2654435761u) >> 22; }
+// blocking): 2^bloom_log2 bits (2048 for up to 32 beams, else 1024), two
+// bits per token; a token whose two bits are not both set is not in the
+// prefix, and only the others scan it.
+__device__ __forceinline__ uint32_t bloom_h1(int v, int lg) { return static_cast<uint32_t>(v) & ((1u << lg) - 1u); }
+__device__ __forceinline__ uint32_t bloom_h2(int v, int lg) {
+    return (static_cast<uint32_t>(v) * 2654435761u) >> (32 - lg);
+}
 
 template <bool kRuns>
 __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodeParams p, int cand_cap,
-                                                                   int seq_T, int seq_K, int sel_cap, int bloom_on) {
+                                                                   int seq_T, int seq_K, int sel_cap, int bloom_log2) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     const ExampleDesc d = p.desc[e];
@@ -1266,11 +1280,13 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         int32_t* tmp = seq_a; seq_a = seq_b; seq_b = tmp;
     }
     // prefix filters (with the prefixes of an earlier launch, if any)
-    const bool use_bloom = need_seq && bloom_on;
+    const bool use_bloom = need_seq && bloom_log2 > 0;
+    const int bl_lg = bloom_log2;
+    const int bl_words = use_bloom ? 1 << (bloom_log2 - 5) : 0;
     uint32_t* bloom_a = use_bloom ? reinterpret_cast<uint32_t*>(sel_lo + sel_cap) : nullptr;
-    uint32_t* bloom_b = use_bloom ? bloom_a + seq_K * kBloomWords : nullptr;
+    uint32_t* bloom_b = use_bloom ? bloom_a + seq_K * bl_words : nullptr;
     if (use_bloom) {
-        for (int i = tid; i < K * kBloomWords; i += NT) bloom_a[i] = 0;
+        for (int i = tid; i < K * bl_words; i += NT) bloom_a[i] = 0;
     }
     __syncthreads();
     if (use_bloom && t_first > 0) {
@@ -1279,8 +1295,9 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
             const int i = idx - k * seq_T;
             if (i < sl_prev[k]) {
                 const int v = seq_a[static_cast<int64_t>(k) * seq_T + i];
-                atomicOr(bloom_a + k * kBloomWords + (bloom_h1(v) >> 5), 1u << (bloom_h1(v) & 31));
-                atomicOr(bloom_a + k * kBloomWords + (bloom_h2(v) >> 5), 1u << (bloom_h2(v) & 31));
+                const uint32_t a = bloom_h1(v, bl_lg), b = bloom_h2(v, bl_lg);
+                atomicOr(bloom_a + k * bl_words + (a >> 5), 1u << (a & 31));
+                atomicOr(bloom_a + k * bl_words + (b >> 5), 1u << (b & 31));
             }
         }
     }
@@ -1288,8 +1305,8 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
     // token v in beam k's prefix
     auto in_prefix = [&](int k, int v) {
         if (use_bloom) {
-            const uint32_t* bl = bloom_a + k * kBloomWords;
-            const uint32_t a = bloom_h1(v), b = bloom_h2(v);
+            const uint32_t* bl = bloom_a + k * bl_words;
+            const uint32_t a = bloom_h1(v, bl_lg), b = bloom_h2(v, bl_lg);
             if (!((bl[a >> 5] >> (a & 31)) & (bl[b >> 5] >> (b & 31)) & 1u)) return false;
         }
         return in_list(seq_a + static_cast<int64_t>(k) * seq_T, sl_prev[k], v);
@@ -1742,18 +1759,18 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         }
         if (use_bloom) {
             // filter[j] = filter[parent_j] + token_j (when from a log-prob)
-            for (int idx = tid; idx < K * kBloomWords; idx += NT) {
-                const int j = idx / kBloomWords;
-                const int w = idx - j * kBloomWords;
+            for (int idx = tid; idx < K * bl_words; idx += NT) {
+                const int j = idx / bl_words;
+                const int w = idx - j * bl_words;
                 const uint64_t h = (j < M) ? chi[j] : 0;
                 uint32_t bits = 0;
                 if (h != 0) {
                     const uint64_t l = clo[j];
                     const int parent = cand_parent(l);
-                    bits = bloom_a[parent * kBloomWords + w];
+                    bits = bloom_a[parent * bl_words + w];
                     if (!(d.eos >= 0 && s.ended[parent])) {
                         const int v = cand_token(l);
-                        const uint32_t a = bloom_h1(v), b = bloom_h2(v);
+                        const uint32_t a = bloom_h1(v, bl_lg), b = bloom_h2(v, bl_lg);
                         if (static_cast<int>(a >> 5) == w) bits |= 1u << (a & 31);
                         if (static_cast<int>(b >> 5) == w) bits |= 1u << (b & 31);
                     }
@@ -2881,12 +2898,13 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     if (cand_cap < max_N + 2048) cand_cap = max_N + 2048;
     const int sel_cap = max_N + 2048;
     // prefix filters of the sequence constraints: two buffers of K filters
-    const int bloom_on = (need_sequences && max_K <= 64) ? 1 : 0;
+    const int bloom_log2 = !need_sequences ? 0 : (max_K <= 32 ? 11 : (max_K <= 64 ? 10 : 0));
+    const int bloom_words = bloom_log2 ? 1 << (bloom_log2 - 5) : 0;
     const size_t smem = static_cast<size_t>(cand_cap) * 2 * sizeof(uint64_t) +
                         static_cast<size_t>(max_K) * 3 * sizeof(float) +
                         static_cast<size_t>(max_K) * 7 * sizeof(int) + 64 +
                         16 + static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t) +
-                        (bloom_on ? static_cast<size_t>(2) * max_K * kBloomWords * sizeof(uint32_t) : 0);
+                        static_cast<size_t>(2) * max_K * bloom_words * sizeof(uint32_t);
     // about two candidates per thread (the run merges of a step are bound by
     // shared-memory latency, so more warps help)
     int threads = 64;
@@ -2897,8 +2915,8 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
                           : reinterpret_cast<const void*>(step_merge_kernel<false>);
     cudaError_t err = ensure_dynamic_smem(fn, smem);
     if (err != cudaSuccess) return err;
-    if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_on);
-    else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_on);
+    if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2);
+    else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2);
     return cudaGetLastError();
 }
 
