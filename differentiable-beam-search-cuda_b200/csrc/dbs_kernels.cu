@@ -661,6 +661,31 @@ __device__ __noinline__ int warp_compact_select(uint64_t* buf, int cnt, int C, i
     return w;
 }
 
+// Removes banned tokens and the blocked EOS (eos_cut, -1 for none) from a
+// warp's survivor buffer, keeping the order; returns the new count. Kept
+// out of line: the row scan's hot loop stays as small as without it.
+__device__ __noinline__ int warp_drop_disallowed(uint64_t* buf, int cnt, const uint8_t* banned, int eos_cut, int lane) {
+    constexpr unsigned FULL = 0xFFFFFFFFu;
+    const unsigned lt = (1u << lane) - 1u;
+    __syncwarp();
+    int w = 0;   // in place: writes stay below the next reads
+    for (int base = 0; base < cnt; base += 32) {
+        const int i = base + lane;
+        const uint64_t key = i < cnt ? buf[i] : 0;
+        bool ok = false;
+        if (i < cnt) {
+            const int v = list_token(key);
+            ok = v != eos_cut && !(banned && banned[v]);
+        }
+        const unsigned b = __ballot_sync(FULL, ok);
+        __syncwarp();
+        if (ok) buf[w + __popc(b & lt)] = key;
+        w += __popc(b);
+        __syncwarp();
+    }
+    return w;
+}
+
 struct RowJob {
     const void* row;    // first element of the row (fp32 or 16-bit)
     int64_t r;
@@ -871,26 +896,8 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             // a threshold only ever comes from allowed entries.
             const bool plain = !j.allow;
             const bool deferred = j.banned || j.eos_blocked;
-            const int eos_cut = j.eos_blocked ? j.eos : -1;
             auto drop_disallowed = [&]() {
-                if (!deferred) return;
-                __syncwarp();
-                int w = 0;   // order-preserving, in place (writes stay below the next reads)
-                for (int base = 0; base < cnt; base += 32) {
-                    const int i = base + lane;
-                    const uint64_t key = i < cnt ? buf[i] : 0;
-                    bool ok = false;
-                    if (i < cnt) {
-                        const int v = list_token(key);
-                        ok = v != eos_cut && !(j.banned && j.banned[v]);
-                    }
-                    const unsigned b = __ballot_sync(FULL, ok);
-                    __syncwarp();
-                    if (ok) buf[w + __popc(b & lt_mask)] = key;
-                    w += __popc(b);
-                    __syncwarp();
-                }
-                cnt = w;
+                if (deferred) cnt = warp_drop_disallowed(buf, cnt, j.banned, j.eos_blocked ? j.eos : -1, lane);
             };
             auto consider_plain = [&](int v, float lp) {
                 const bool pass = lp >= thr;
@@ -2910,6 +2917,13 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     int threads = 64;
     while (threads < kMergeThreads && threads * 2 <= M) threads <<= 1;
     if (threads < 128 && max_K > 64) threads = 128;
+    // More examples than SMs: 256-thread CTAs, two per SM (a 512-thread CTA
+    // holds an SM's registers), so the examples run in one wave, not two.
+    int dev = 0, sms = 0;
+    cudaError_t aerr = cudaGetDevice(&dev);
+    if (aerr == cudaSuccess) aerr = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (aerr != cudaSuccess) return aerr;
+    if (p.B > sms && threads > 256) threads = 256;
     const bool runs = !need_sequences && M <= 1024;
     const void* fn = runs ? reinterpret_cast<const void*>(step_merge_kernel<true>)
                           : reinterpret_cast<const void*>(step_merge_kernel<false>);
