@@ -1221,7 +1221,8 @@ __device__ __forceinline__ uint32_t bloom_h2(int v, int lg) {
 
 template <bool kRuns>
 __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodeParams p, int cand_cap,
-                                                                   int seq_T, int seq_K, int sel_cap, int bloom_log2) {
+                                                                   int seq_T, int seq_K, int sel_cap, int bloom_log2,
+                                                                   int seq_smem) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     const ExampleDesc d = p.desc[e];
@@ -1294,6 +1295,22 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
     uint32_t* bloom_b = use_bloom ? bloom_a + seq_K * bl_words : nullptr;
     if (use_bloom) {
         for (int i = tid; i < K * bl_words; i += NT) bloom_a[i] = 0;
+    }
+    // Prefixes and n-gram sets in shared memory when they fit: the launch
+    // works on its own copy, loaded from the global scratch when an earlier
+    // launch left prefixes there and stored back when a later one continues.
+    const bool seq_local = need_seq && seq_smem;
+    int32_t* const g_seq = need_seq ? p.seq_scratch + static_cast<int64_t>(e) * 3 * seq_K * seq_T : nullptr;
+    if (seq_local) {
+        int32_t* sq = reinterpret_cast<int32_t*>(sel_lo + sel_cap) + 2 * seq_K * bl_words;
+        __syncthreads();   // prefix lengths of the state loop
+        if (t_first > 0) {
+            for (int idx = tid; idx < K * seq_T; idx += NT)
+                if (idx - (idx / seq_T) * seq_T < sl_prev[idx / seq_T]) sq[idx] = seq_a[idx];
+        }
+        seq_a = sq;
+        seq_b = sq + static_cast<int64_t>(K) * seq_T;
+        blk = seq_b + static_cast<int64_t>(K) * seq_T;
     }
     __syncthreads();
     if (use_bloom && t_first > 0) {
@@ -1799,6 +1816,12 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         __syncthreads();
     }
     if (t_stop < T) {   // more steps follow in a later launch: keep the state
+        if (seq_local) {
+            // the later launch starts from the buffer its step's parity names
+            int32_t* g_cur = g_seq + ((t_stop & 1) ? static_cast<int64_t>(K) * seq_T : 0);
+            for (int idx = tid; idx < K * seq_T; idx += NT)
+                if (idx - (idx / seq_T) * seq_T < sl_prev[idx / seq_T]) g_cur[idx] = seq_a[idx];
+        }
         if (state) {
             for (int k = tid; k < K; k += NT) {
                 state[k] = s.prev_raw[k];
@@ -2907,11 +2930,15 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     // prefix filters of the sequence constraints: two buffers of K filters
     const int bloom_log2 = !need_sequences ? 0 : (max_K <= 32 ? 11 : (max_K <= 64 ? 10 : 0));
     const int bloom_words = bloom_log2 ? 1 << (bloom_log2 - 5) : 0;
-    const size_t smem = static_cast<size_t>(cand_cap) * 2 * sizeof(uint64_t) +
-                        static_cast<size_t>(max_K) * 3 * sizeof(float) +
-                        static_cast<size_t>(max_K) * 7 * sizeof(int) + 64 +
-                        16 + static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t) +
-                        static_cast<size_t>(2) * max_K * bloom_words * sizeof(uint32_t);
+    size_t smem = static_cast<size_t>(cand_cap) * 2 * sizeof(uint64_t) +
+                  static_cast<size_t>(max_K) * 3 * sizeof(float) +
+                  static_cast<size_t>(max_K) * 7 * sizeof(int) + 64 +
+                  16 + static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t) +
+                  static_cast<size_t>(2) * max_K * bloom_words * sizeof(uint32_t);
+    // prefixes (two buffers) and n-gram sets in shared memory when they fit
+    const size_t seq_bytes = static_cast<size_t>(3) * max_K * max_T * sizeof(int32_t);
+    const int seq_smem = (need_sequences && smem + seq_bytes <= 200 * 1024) ? 1 : 0;
+    if (seq_smem) smem += seq_bytes;
     // about two candidates per thread (the run merges of a step are bound by
     // shared-memory latency, so more warps help)
     int threads = 64;
@@ -2929,8 +2956,8 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
                           : reinterpret_cast<const void*>(step_merge_kernel<false>);
     cudaError_t err = ensure_dynamic_smem(fn, smem);
     if (err != cudaSuccess) return err;
-    if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2);
-    else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2);
+    if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2, seq_smem);
+    else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2, seq_smem);
     return cudaGetLastError();
 }
 
