@@ -2556,7 +2556,7 @@ __global__ void backward_kernel(BackwardParams p, int sparse, int max_K, int max
 //     with atomicAdd into the zeroed buffer, which is exact in either order.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) backward_sweep_kernel(BackwardParams p, int max_T, int max_K, int max_P,
-                                                             int with_pool) {
+                                                             int with_pool, int sparse) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     const ExampleDesc d = p.desc[e];
@@ -2657,42 +2657,115 @@ __global__ void __launch_bounds__(256) backward_sweep_kernel(BackwardParams p, i
         }
     }
     __syncthreads();
-    if (tid >= 32) return;
-    // the recursion: one warp, lane k = beam k
-    const int lane = tid;
-    float g = 0.0f;
-    for (int t = T - 1; t >= 0; --t) {
-        float draw = 0.0f;
-        int sp = -1;
-        if (lane < K) {
-            const int idx = t * K + lane;
-            const int parent = par[idx];
-            if (parent >= 0) {
-                draw = __fadd_rn(g, own[idx]);
-                const int tk = tok[idx];
-                if (draw != 0.0f && tk >= 0) {
-                    const int64_t gi = (static_cast<int64_t>(t) * K + parent) * V + tk;
-                    if (with_pool && relax[t]) atomicAdd(p.grad_dense + d.grad_offset + gi, draw);
-                    else p.grad_dense[d.grad_offset + gi] = draw;
+    if (tid < 32) {
+        // the recursion: one warp, lane k = beam k
+        const int lane = tid;
+        float g = 0.0f;
+        for (int t = T - 1; t >= 0; --t) {
+            float draw = 0.0f;
+            int sp = -1;
+            if (lane < K) {
+                const int idx = t * K + lane;
+                const int parent = par[idx];
+                if (parent >= 0) {
+                    draw = __fadd_rn(g, own[idx]);
+                    const int tk = tok[idx];
+                    if (sparse) {
+                        // keep the entry for the sparse output below
+                        own[idx] = draw;
+                        if (draw == 0.0f) tok[idx] = -1;
+                    } else if (draw != 0.0f && tk >= 0) {
+                        const int64_t gi = (static_cast<int64_t>(t) * K + parent) * V + tk;
+                        if (with_pool && relax[t]) atomicAdd(p.grad_dense + d.grad_offset + gi, draw);
+                        else p.grad_dense[d.grad_offset + gi] = draw;
+                    }
+                    if (draw != 0.0f) sp = parent;
                 }
-                if (draw != 0.0f) sp = parent;
+            }
+            float acc = 0.0f;
+            for (int k = 0; k < K; ++k) {
+                const int pk = __shfl_sync(0xFFFFFFFFu, sp, k);
+                const float dk = __shfl_sync(0xFFFFFFFFu, draw, k);
+                if (pk == lane) acc = __fadd_rn(acc, dk);
+            }
+            if (with_pool && relax[t]) {
+                const int* pq = ppar + t * P;
+                const float* dq = pdraw + t * P;
+                for (int q = 0; q < P; ++q)
+                    if (pq[q] == lane) acc = __fadd_rn(acc, dq[q]);
+            }
+            g = acc;
+        }
+        if (lane < K && p.grad_initial) p.grad_initial[d.final_offset + lane] = g;
+    }
+    if (!sparse) return;
+    // Sparse output without a relaxed-pool gradient: a step's entries are
+    // its selected slots, whose (parent, token) pairs are distinct, so the
+    // sorted unique indices (finalize_sparse_entries,
+    // src/differentiable_beam.cpp:1908-1941) are each step's entries sorted
+    // by (parent, token), steps in order. One warp sorts a step in
+    // registers; one scan of the per-step counts places the steps.
+    __syncthreads();
+    int* step_n = relax;                           // [T] entries of step t
+    int* step_off = reinterpret_cast<int*>(dot);   // [T] their first output slot
+    const int lane = tid & 31;
+    for (int t = tid >> 5; t < T; t += NT >> 5) {
+        const int idx = t * K + lane;
+        const int pa = lane < K ? par[idx] : -1;
+        const int tk = lane < K ? tok[idx] : -1;
+        const bool ok = pa >= 0 && tk >= 0;
+        uint64_t key = ok ? (static_cast<uint64_t>(pa) << 32) | static_cast<uint32_t>(tk) : ~0ull;
+        float val = lane < K ? own[idx] : 0.0f;
+#pragma unroll
+        for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+            for (int st = size >> 1; st > 0; st >>= 1) {
+                const uint64_t ok2 = __shfl_xor_sync(0xFFFFFFFFu, key, st);
+                const float ov = __shfl_xor_sync(0xFFFFFFFFu, val, st);
+                const bool lower = (lane & st) == 0;
+                const bool asc = (lane & size) == 0;
+                if (lower == asc ? ok2 < key : ok2 > key) {
+                    key = ok2;
+                    val = ov;
+                }
             }
         }
-        float acc = 0.0f;
-        for (int k = 0; k < K; ++k) {
-            const int pk = __shfl_sync(0xFFFFFFFFu, sp, k);
-            const float dk = __shfl_sync(0xFFFFFFFFu, draw, k);
-            if (pk == lane) acc = __fadd_rn(acc, dk);
+        const int n = __popc(__ballot_sync(0xFFFFFFFFu, ok));
+        __syncwarp();
+        if (lane < n) {
+            par[idx] = static_cast<int>(key >> 32);
+            tok[idx] = static_cast<int>(key & 0xFFFFFFFFu);
+            own[idx] = val;
         }
-        if (with_pool && relax[t]) {
-            const int* pq = ppar + t * P;
-            const float* dq = pdraw + t * P;
-            for (int q = 0; q < P; ++q)
-                if (pq[q] == lane) acc = __fadd_rn(acc, dq[q]);
-        }
-        g = acc;
+        if (lane == 0) step_n[t] = n;
     }
-    if (lane < K && p.grad_initial) p.grad_initial[d.final_offset + lane] = g;
+    __syncthreads();
+    if (tid < 32) {
+        int base = 0;
+        for (int t0 = 0; t0 < T; t0 += 32) {
+            const int t = t0 + tid;
+            const int n = t < T ? step_n[t] : 0;
+            int incl = n;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (tid >= o) incl += v;
+            }
+            if (t < T) step_off[t] = base + incl - n;
+            base += __shfl_sync(0xFFFFFFFFu, incl, 31);
+        }
+        if (tid == 0) p.sparse_counts[e] = base;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < T * K; idx += NT) {
+        const int t = idx / K;
+        const int j = idx - t * K;
+        if (j < step_n[t]) {
+            const int64_t o = d.sparse_offset + step_off[t] + j;
+            p.sparse_indices[o] = (static_cast<int64_t>(t) * K + par[idx]) * V + tok[idx];
+            p.sparse_values[o] = own[idx];
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -2995,13 +3068,15 @@ static size_t backward_smem_bytes(int max_K, int max_P) {
 }
 
 cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool sparse, cudaStream_t stream) {
-    if (!sparse && max_K <= 32 && p.grad_dense) {
-        const bool with_pool = p.grad_relaxed != nullptr;
+    // the sweep: dense output, or sparse output without a relaxed-pool gradient
+    if (max_K <= 32 && (sparse ? p.grad_relaxed == nullptr : p.grad_dense != nullptr)) {
+        const bool with_pool = !sparse && p.grad_relaxed != nullptr;
         const size_t smem = backward_sweep_smem(p.max_T, max_K, max_P, with_pool);
         if (smem <= kBackwardSweepSmemBudget) {
             cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(backward_sweep_kernel), smem);
             if (err != cudaSuccess) return err;
-            backward_sweep_kernel<<<p.B, 256, smem, stream>>>(p, p.max_T, max_K, max_P, with_pool ? 1 : 0);
+            backward_sweep_kernel<<<p.B, 256, smem, stream>>>(p, p.max_T, max_K, max_P, with_pool ? 1 : 0,
+                                                              sparse ? 1 : 0);
             return cudaGetLastError();
         }
     }
