@@ -560,3 +560,70 @@ def test_degenerate_shapes_and_values(libdbs, oracle_lib, idx):
     want = _oracle_decode(oracle_lib, opts, x, T, V, cons)
     got = _product_decode(libdbs, opts, np.ascontiguousarray(x), T, V, cons)
     assert_decode_equal(got, want, f"degenerate case {idx}")
+
+
+def test_more_examples_than_sms_with_sequence_constraints(libdbs, oracle_lib):
+    # 200 examples (more than the GPU's SMs, so the step merge runs two
+    # 256-thread CTAs per SM) with repetition penalty, 2-gram blocking,
+    # banned and forced tokens, mixed steps and beams: every example against
+    # the oracle
+    rng = np.random.default_rng(31)
+    B, maxT, maxK, V = 200, 7, 6, 90
+    x = log_softmax_np(1.5 * rng.standard_normal((B, maxT, maxK, V)).astype(np.float32))
+    x[:, :, :, :5] += 1.0   # a few favoured tokens, so that repeats and blocked 2-grams occur
+    x = log_softmax_np(x)
+    steps = rng.integers(2, maxT + 1, B).astype(np.int32)
+    beams = rng.integers(1, maxK + 1, B).astype(np.int32)
+    banned = (rng.random((B, V)) < 0.05).astype(np.uint8)
+    forced = np.where(rng.random((B, maxT)) < 0.1, rng.integers(0, V, (B, maxT)), -1).astype(np.int32)
+    base = dict(beam_size=3, eos_token=4, relaxed_pool_multiplier=3)
+    results = []
+    for b in range(B):
+        T, K = int(steps[b]), int(beams[b])
+        cons = dict(banned=banned[b], forced=forced[b, :T].copy(), repetition_penalty=1.3, no_repeat_ngram_size=2)
+        results.append((T, K, cons))
+    # the variable-batch C ABI has no sequence constraints; the device
+    # variable batch does (dbs_device_decode_batch_variable_ex)
+    import torch
+    import torch_dbs_extension as ext
+    dev = torch.device("cuda", 0)
+    xd = torch.tensor(x, device=dev)
+    eos = np.full(B, 4, np.int32)
+    minl = np.zeros(B, np.int32)
+    sel = int((steps.astype(np.int64) * beams).sum())
+    pool = int((steps.astype(np.int64) * beams * 3).sum())
+    fin = int(beams.sum())
+    sel_names = ("parents", "tokens", "lengths", "from_logprob", "raw_scores", "scores", "weights")
+    out = {}
+    for name, _ in dc.DBSDeviceDecodeOutputs._fields_:
+        n = sel if name in sel_names else (fin if name.startswith("final") else pool)
+        dt = torch.uint8 if "from_logprob" in name else (
+            torch.int32 if name.split("_")[-1] in ("parents", "tokens", "lengths") else torch.float32)
+        out[name] = torch.empty(max(n, 1), dtype=dt, device=dev)
+    s = dc.DBSDeviceDecodeOutputs()
+    for name, _ in dc.DBSDeviceDecodeOutputs._fields_:
+        setattr(s, name, out[name].data_ptr())
+    bd = torch.tensor(banned, device=dev)
+    fd = torch.tensor(forced, device=dev)
+    h = ext._handle(ext.DBSOptions(**base))
+    lib = ext._library()
+    rc = lib.dbs_device_decode_batch_variable_ex(
+        h, ext._vp(xd), B, maxT, maxK, V, steps.ctypes.data_as(ctypes.c_void_p), beams.ctypes.data_as(ctypes.c_void_p),
+        eos.ctypes.data_as(ctypes.c_void_p), minl.ctypes.data_as(ctypes.c_void_p), ext._vp(bd), ext._vp(fd),
+        ctypes.c_float(1.3), 2, ctypes.byref(s), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, lib.dbs_last_error(h)
+    torch.cuda.synchronize()
+    sel_off = np.concatenate([[0], np.cumsum(steps.astype(np.int64) * beams)])
+    pool_off = np.concatenate([[0], np.cumsum(steps.astype(np.int64) * beams * 3)])
+    fin_off = np.concatenate([[0], np.cumsum(beams)])
+    host = {f: out[f].cpu().numpy() for f in ("parents", "tokens", "lengths", "raw_scores", "pool_tokens",
+                                               "pool_parents", "final_scores")}
+    for b, (T, K, cons) in enumerate(results):
+        opts = dict(base, beam_size=K)
+        want = oracle_lib.decode(oracle_lib.options(**opts), np.ascontiguousarray(x[b, :T, :K]), T, V, **cons)
+        a, c = sel_off[b], sel_off[b + 1]
+        for f in ("parents", "tokens", "lengths", "raw_scores"):
+            assert np.array_equal(host[f][a:c], want[f]), (b, f)
+        for f in ("pool_tokens", "pool_parents"):
+            assert np.array_equal(host[f][pool_off[b]:pool_off[b + 1]], want[f]), (b, f)
+        assert np.array_equal(host["final_scores"][fin_off[b]:fin_off[b + 1]], want["final_scores"]), b
