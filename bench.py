@@ -70,6 +70,11 @@ def parse_args():
                          "--steps times on the workload and print no bench line")
     ap.add_argument("--shape", default=None, metavar="T,K,V",
                     help="profiling only (--pool-decode): steps, beams and vocabulary instead of the workload's")
+    ap.add_argument("--constrained", type=int, default=None, metavar="EXAMPLES",
+                    help="profiling only: run the constrained variable-batch device decode (V=128256, K_b in "
+                         "{1,2,4,8,16}, T_b in [8,128], 256 banned ids, forced first token, minimum length 8 before "
+                         "EOS 2, repetition penalty 1.2, no repeated 3-gram) on its first EXAMPLES examples, "
+                         "--steps times, and print no bench line")
     ap.add_argument("--rows", choices=("zipf", "normal"), default="zipf",
                     help="profiling only (--pool-decode): the workload's Zipf-biased rows, or "
                          "log_softmax(N(0,1)) rows as in the 256-example V=50257 configuration")
@@ -100,6 +105,65 @@ def pool_decode_loop(args):
         ext.device_decode(x, opts, with_pool=True, with_weights=True)
     torch.cuda.synchronize()
     print(f"pool decode x{args.steps} done")
+
+
+def constrained_loop(args):
+    """Device decode of the 512-example constrained variable batch's first
+    slice (padded [n, 128, 16, 128256] layout, live rows only written), for
+    profiling the constrained row scan and merge."""
+    import numpy as np
+    import torch
+    import dbs_ctypes as dc
+    import torch_dbs_extension as ext
+    rng = np.random.default_rng(4)
+    B, maxT, maxK, V = 512, 128, 16, 128256
+    steps_all = rng.integers(8, maxT + 1, B).astype(np.int32)
+    beams_all = rng.choice(np.array([1, 2, 4, 8, 16], np.int32), B).astype(np.int32)
+    banned_row = np.zeros(V, np.uint8)
+    banned_row[rng.choice(V, 256, replace=False)] = 1
+    nb = min(B, args.constrained)
+    steps = np.ascontiguousarray(steps_all[:nb])
+    beams = np.ascontiguousarray(beams_all[:nb])
+    dev = torch.device("cuda", 0)
+    x = torch.zeros((nb, maxT, maxK, V), dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev)
+    for b in range(nb):
+        g.manual_seed(4 * 1_000_003 + b)
+        T, K = int(steps[b]), int(beams[b])
+        z = torch.empty((T, K, V), device=dev)
+        z.normal_(generator=g)
+        x[b, :T, :K] = torch.log_softmax(1.5 * z, dim=-1)
+    eos = np.full(nb, 2, np.int32)
+    minl = np.full(nb, 8, np.int32)
+    banned = torch.tensor(np.tile(banned_row, (nb, 1)), device=dev)
+    forced_np = np.full((nb, maxT), -1, np.int32)
+    forced_np[:, 0] = 1
+    forced = torch.tensor(forced_np, device=dev)
+    sel = int((steps.astype(np.int64) * beams).sum())
+    fin = int(beams.sum())
+    sel_names = ("parents", "tokens", "lengths", "from_logprob", "raw_scores", "scores", "weights")
+    out = {}
+    s = dc.DBSDeviceDecodeOutputs()
+    for name, _ in dc.DBSDeviceDecodeOutputs._fields_:
+        n = sel if name in sel_names else (fin if name.startswith("final") else 8 * sel)
+        dt = torch.uint8 if "from_logprob" in name else (
+            torch.int32 if name.split("_")[-1] in ("parents", "tokens", "lengths") else torch.float32)
+        out[name] = torch.empty(n, dtype=dt, device=dev)
+        setattr(s, name, out[name].data_ptr())
+    opts = ext.DBSOptions(beam_size=maxK, eos_token=2, min_length=8)
+    h = ext._handle(opts)
+    lib = ext._library()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(args.steps):
+        rc = lib.dbs_device_decode_batch_variable_ex(
+            h, ext._vp(x), nb, maxT, maxK, V, steps.ctypes.data_as(ctypes.c_void_p),
+            beams.ctypes.data_as(ctypes.c_void_p), eos.ctypes.data_as(ctypes.c_void_p),
+            minl.ctypes.data_as(ctypes.c_void_p), ext._vp(banned), ext._vp(forced), ctypes.c_float(1.2), 3,
+            ctypes.byref(s), stream)
+        if rc != 0:
+            raise RuntimeError(lib.dbs_last_error(h).decode())
+    torch.cuda.synchronize()
+    print(f"constrained decode of {nb} examples ({sel} live rows) x{args.steps} done")
 
 
 def measured_peaks():
@@ -294,6 +358,9 @@ def main():
         return
     if args.pool_decode:
         pool_decode_loop(args)
+        return
+    if args.constrained:
+        constrained_loop(args)
         return
 
     import numpy as np
