@@ -93,7 +93,7 @@ struct DecodeParams {
     const uint8_t* row_allow;
     int32_t force_seq;
     // Short row lists (many-example relaxed-pool decodes): the one live row
-    // of step 0, (t=0, k=0), gets a list of up to min(N, K*C) entries in the
+    // of step 0, (t=0, k=0), gets a list of up to min(N, K*C, 1024) entries in the
     // list space of step 0's K rows (the other K-1 rows of step 0 are never
     // extended). The main row scan skips that row; a second launch with
     // first_rows_only = 1 scans exactly those rows (claim i -> row_prefix[i]);
@@ -192,6 +192,10 @@ cudaError_t noalloc_prepare();
 
 // Limits of this implementation.
 constexpr int kMaxMergeCandidates = 8192;   // K * C per step handled by one CTA
+// Longest list of the step-0 row of a short-list decode (a shorter list than
+// the pool only costs a rescan; longer ones would not fit the scan's shared
+// memory for every pool size).
+constexpr int kStep0ListMax = 1024;
 constexpr int kMergeThreads = 512;
 
 }  // namespace dbs_dev

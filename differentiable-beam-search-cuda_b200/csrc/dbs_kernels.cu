@@ -724,7 +724,7 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     j.list_at = d.list_offset + lr * d.C;
     // the live step-0 row of a short-list decode keeps a long list in the
     // list space of step 0's K rows
-    j.C = p.first_rows_only ? min(d.N, d.K * d.C) : d.C;
+    j.C = p.first_rows_only ? min(min(d.N, d.K * d.C), kStep0ListMax) : d.C;
     j.forced = d.forced ? d.forced[t] : -1;
     // A decode starts from beam 0 alone (the other beams score -inf), so the
     // rows of the other beams at step 0 can never yield a candidate; like

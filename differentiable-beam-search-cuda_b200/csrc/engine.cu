@@ -426,7 +426,7 @@ int list_capacity(const Options& opt, int K, bool pool, bool dynamic) {
 // 3.5 TB/s with 256-entry lists); the merge proves every other row per step
 // and rescans the few that could hold more from HBM, so the selection stays
 // exact. Step 0 has one live row, which holds the whole pool: it gets a list
-// of up to K*64 entries in the list space of step 0's rows (the other beams'
+// of up to min(P, 64*K, 1024) entries in the list space of step 0's rows (the other beams'
 // rows at step 0 are never extended). The saving grows with the rows a
 // call scans (the speculative scan needs many rows per warp) while the
 // rescans cost each example's merge a fixed time, and the merges of many
@@ -503,7 +503,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         max_T = std::max(max_T, e.T);
         max_K = std::max(max_K, e.K);
         max_C = std::max(max_C, C);
-        max_C0 = std::max(max_C0, std::min(N, e.K * C));   // step-0 list of a short-list decode
+        max_C0 = std::max(max_C0, std::min({N, e.K * C, dbs_dev::kStep0ListMax}));   // step-0 list of a short-list decode
         max_N = std::max(max_N, N);
         max_P = std::max(max_P, P);
     }

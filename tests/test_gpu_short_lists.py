@@ -1,6 +1,6 @@
 """Relaxed-pool decodes of 32 or more examples and 64K or more rows, with
 pools above 64 entries, keep row lists of 64 entries (step 0's one live row
-keeps a list of up to 64*K entries): the step merge proves, per step, that
+keeps a list of up to min(P, 64*K, 1024) entries): the step merge proves, per step, that
 no row holds more of the pool than its list, and rescans the rows it cannot
 prove from HBM. Every path of that (run merge and selection merge, 16-bit
 rows, static constraints, exact ties at the list cut, a dominant beam whose
@@ -149,3 +149,31 @@ def test_short_lists_variable_batch_with_static_constraints(libdbs, oracle_lib):
         assert_decode_equal(dc.read_result(libdbs, libdbs.dbs_batch_result_at(br, b)), want, f"example {b}")
     libdbs.dbs_free_batch_result(br)
     dec.close()
+
+
+def test_short_lists_pool_longer_than_the_step0_list(libdbs, oracle_lib):
+    # a pool of 1280 entries without weights (device API): step 0's one live
+    # row lists 1024 entries, fewer than the pool, so the merge completes
+    # step 0 from a rescan of that row
+    import torch
+    import torch_dbs_extension as ext
+    rng = np.random.default_rng(41)
+    B, T, K, V = 32, 64, 32, 300
+    x = log_softmax_np(rng.standard_normal((B, T, K, V)).astype(np.float32))
+    opts = ext.DBSOptions(beam_size=K, relaxed_pool_multiplier=40)
+    xd = torch.tensor(x, device="cuda")
+    tr = ext.DeviceTrace(B, T, K, xd.device, with_pool=True, P=40 * K)
+    s = tr.struct()
+    s.relaxed_weights = None   # weights are limited to pools of 1024; the decode itself is not
+    lib = ext._library()
+    h = ext._handle(opts)
+    rc = lib.dbs_device_decode_batch_ex(h, ext._vp(xd), B, T, V, ctypes.byref(s), None, 0,
+                                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, lib.dbs_last_error(h)
+    torch.cuda.synchronize()
+    for b in (0, 17, B - 1):
+        want = oracle_lib.decode(oracle_lib.options(beam_size=K, relaxed_pool_multiplier=40),
+                                 np.ascontiguousarray(x[b]), T, V)
+        for f in ("parents", "tokens", "lengths", "raw_scores", "pool_parents", "pool_tokens", "pool_raw_scores",
+                  "final_scores"):
+            assert np.array_equal(getattr(tr, f)[b].cpu().numpy().ravel(), want[f]), (b, f)
