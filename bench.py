@@ -12,7 +12,8 @@ Metric: log-prob elements per second, B*T*K*V / (forward + backward time).
 
   * value  -- device-resident inputs, timed with CUDA events, max over ranks.
   * e2e    -- the same call with the inputs copied from pinned host memory
-              every step and the loss read back.
+              every step and the loss read back (two input buffers: the next
+              step's copy overlaps this step's decode and backward).
   * roofline -- the row scan kernel (the pass that streams every log-prob
               once) timed live with CUDA events around its launches; its
               algorithmic bytes are 4*B*(T*K - (K-1))*V per launch (every
@@ -479,29 +480,46 @@ def main():
     whole = {"achieved_gbs": step_bytes / (ms_per_step / 1e3) / 1e9,
              "frac": step_bytes / (ms_per_step / 1e3) / 1e9 / peak}
 
-    # end to end from pinned host memory
+    # end to end from pinned host memory: every step copies its inputs from
+    # pinned host memory and reads its loss back; two device input buffers
+    # let the next step's copy (a side stream) run beside this step's decode
+    # and backward. A buffer is refilled only after the loss read-back of
+    # the step that used it, and every copy lies inside the timed region.
     x_host = x.detach().cpu().pin_memory()
-    xd = torch.empty_like(x.detach()).requires_grad_(True)
+    bufs = [torch.empty_like(x.detach()).requires_grad_(True) for _ in range(2)]
+    copy_stream = torch.cuda.Stream(device=device)
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    main_stream = torch.cuda.current_stream(device)
 
-    def e2e_step():
-        with torch.no_grad():
-            xd.copy_(x_host, non_blocking=True)
-        xd.grad = None
-        y = ext.final_scores(xd, opts)
-        loss = y.sum()
-        loss.backward()
-        return loss.item()
+    def issue_copy(i, after=None):
+        with torch.cuda.stream(copy_stream):
+            if after is not None:
+                copy_stream.wait_event(after)
+            with torch.no_grad():
+                bufs[i % 2].copy_(x_host, non_blocking=True)
+            ready[i % 2].record(copy_stream)
 
-    for _ in range(2):
-        e2e_step()
+    def e2e_run(n, start=None):
+        issue_copy(0, start)
+        for i in range(n):
+            if i + 1 < n:
+                issue_copy(i + 1)
+            main_stream.wait_event(ready[i % 2])
+            xd = bufs[i % 2]
+            xd.grad = None
+            y = ext.final_scores(xd, opts)
+            loss = y.sum()
+            loss.backward()
+            loss.item()
+
+    e2e_run(2)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.e2e_steps):
-        e2e_step()
+    e2e_run(args.e2e_steps, start=e0)
     e1.record()
     torch.cuda.synchronize()
     te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
