@@ -20,7 +20,9 @@ Metric: log-prob elements per second, B*T*K*V / (forward + backward time).
               row but those of beams 1..K-1 at step 0, which no live beam
               extends).
   * cpu_baseline -- the reference's CPU library (compiled from its source into
-              oracle/_ref) on the same workload, all host threads.
+              oracle/_ref) on the same workload, all host threads; the
+              oracle's C restatement on one thread when that library is not
+              built.
 
 Warm-up: at least --warmup steps and at least --warmup-seconds (5 s) of
 steps, since a freshly started GPU runs the first seconds measurably slower;
@@ -276,7 +278,7 @@ def reference_cpu_run(x_host, steps_budget_s=20.0):
     B, T, K, V = x_host.shape
     x = np.ascontiguousarray(x_host)
     if path is None:
-        return None
+        return _oracle_port_run(x, steps_budget_s)
     lib = dc.load_library(path, device_api=False)
     dec = dc.Decoder(lib, dc.Options(**OPTIONS))
     gf = np.ones(K, dtype=np.float32)
@@ -305,6 +307,39 @@ def reference_cpu_run(x_host, steps_budget_s=20.0):
     return elems / dt, cores, "reference", sample
 
 
+def _oracle_port_run(x, steps_budget_s):
+    """The CPU restatement in oracle/ on one host thread, for when the reference
+    library could not be built: per example the decode, the sparse backward of
+    grad_final = ones and the scatter into a zero dense gradient. Returns
+    (elems/s, 1, "port", sample), or None when the oracle is not built either."""
+    import numpy as np
+    from oracle import ORACLE_SO, OracleLib
+    if not os.path.exists(ORACLE_SO):
+        return None
+    ol = OracleLib()
+    opts = ol.options(**OPTIONS)
+    B, T, K, V = x.shape
+    gf = np.ones(K, dtype=np.float32)
+    elems = 0
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        grad = np.zeros((B, T * K * V), dtype=np.float32)
+        for b in range(B):
+            fwd = ol.decode(opts, x[b], T, V)
+            out = ol.backward_sparse(fwd, grad_final=gf)
+            grad[b, out["indices"]] += out["values"]
+        del grad
+        elems += B * T * K * V
+        reps += 1
+        if time.perf_counter() - t0 >= steps_budget_s or reps >= 50:
+            break
+    dt = time.perf_counter() - t0
+    sample = (f"{reps} x full batch B={B},T={T},K={K},V={V} through the oracle's C restatement (1 thread) "
+              f"+ sparse backward + dense scatter")
+    return elems / dt, 1, "port", sample
+
+
 def bench_config(B, T, K, V, world):
     return {"workload": f"torch final_scores fwd + y.sum().backward(), B={B} T={T} K={K} V={V}, eos_token=2, "
                         "length_penalty_alpha=0.2, selected_temperature=0.7 (per GPU)",
@@ -330,7 +365,7 @@ def run_reference_arm(args, rank, world):
     for i in range(max(3, args.warmup) + args.steps):
         res = reference_cpu_run(x, steps_budget_s=0.0)
         if res is None:
-            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdbs_ref.so was not built"}))
+            print(json.dumps({"impl": "reference", "unavailable": "neither oracle/_ref/libdbs_ref.so nor the oracle port was built"}))
             return
         if i >= max(3, args.warmup):
             vals.append(res[0])

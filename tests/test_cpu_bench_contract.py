@@ -50,3 +50,15 @@ def test_reference_arm_other_ranks_exit_without_work():
     out = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert out.returncode == 0, out.stderr[-2000:]
     assert out.stdout.strip() == ""
+
+
+def test_port_baseline_when_the_reference_library_is_absent():
+    """Without oracle/_ref the arm times the oracle's C restatement instead."""
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import torch
+    import bench
+    x = bench.make_inputs(torch, 2, 4, 8, 32000, 0, "cpu").numpy()
+    value, cores, kind, sample = bench._oracle_port_run(x, 0.0)
+    assert value > 0 and cores == 1 and kind == "port"
+    assert "B=2,T=4,K=8,V=32000" in sample
