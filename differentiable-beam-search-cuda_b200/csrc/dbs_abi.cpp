@@ -1767,10 +1767,16 @@ DBS_EXPORT int dbs_device_profile_read(int kernel, double* total_ms, int64_t* la
 
 DBS_EXPORT int dbs_device_last_rescan_counts(DBSDecoderHandle* handle, int64_t* row_rescans, int64_t* merge_rescans) {
     if (!handle) return -1;
-    unsigned long long merge = 0;
-    dbs_host::last_decode_diagnostics(&merge, nullptr);
-    if (row_rescans) *row_rescans = 0;  // the row scan is exact in one pass
+    unsigned long long merge = 0, rows = 0;
+    dbs_host::last_decode_diagnostics(&merge, nullptr, &rows);
+    if (row_rescans) *row_rescans = static_cast<int64_t>(rows);
     if (merge_rescans) *merge_rescans = static_cast<int64_t>(merge);
+    return 0;
+}
+
+DBS_EXPORT int dbs_device_kernel_launches(int64_t* count) {
+    if (!count) return -1;
+    *count = static_cast<int64_t>(dbs_host::kernel_launches());
     return 0;
 }
 

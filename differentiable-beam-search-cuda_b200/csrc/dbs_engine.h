@@ -100,12 +100,31 @@ struct DecodeParams {
     // the step merge reads step 0 as that one list.
     int32_t first_row_apart;
     int32_t first_rows_only;
+    // Row-scan launch controls. `claim` is the counter this launch claims
+    // rows from (nullptr: counters[2]); concurrent launches of one call each
+    // get their own. With step_major_bk = B*K (a uniform batch of B
+    // examples, K beams, row stride step_major_tk = T*K per example) claim c
+    // scans step c / (B*K) of example (c / K) % B, beam c % K, so a launch
+    // over claims [t0*B*K, t1*B*K) lists exactly the rows of steps
+    // [t0, t1) of every example. spec_seed (kSpecSlots entries of
+    // C << 32 | float bits, 0 = empty) carries speculative thresholds from
+    // one launch to the next. Warps on an SM whose id is below reserve_sms
+    // stop claiming rows (and return) once a warp of the same launch on
+    // another SM has started, which it marks in *worker_flag (zeroed per
+    // launch): those SMs are then left to merge launches that run beside
+    // the scan, and every claimed row is still scanned by its warp.
+    unsigned long long* claim;
+    int64_t step_major_bk;
+    int64_t step_major_tk;
+    unsigned long long* spec_seed;
+    int32_t reserve_sms;
+    unsigned int* worker_flag;
     // workspace
     uint64_t* lists;              // row lists, key = ord(lp)<<32 | ~token
     int32_t* list_count;          // [total_rows]
     float* list_bound;            // [total_rows] max dropped lp (-inf: none)
     int32_t* status;              // [B] 0 ok, 1 NaN/+Inf sampled
-    unsigned long long* counters; // [4] diagnostics: rescans, merge fallbacks
+    unsigned long long* counters; // [4]: row-scan second passes, merge rescans, next row claim, wait timeouts
     int32_t* seq_scratch;         // [B, 2, K, T] beam prefixes (constraints only)
     // outputs (element pointers; any may be null except the trace needed by
     // later stages)
@@ -164,9 +183,17 @@ struct BackwardParams {
 cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream);
 // Scans the rows claimed from counters[2] (the first row to scan) up to
 // p.total_rows; `rows` is how many that is (-1: p.total_rows), for sizing.
-cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream, int64_t rows = -1);
+// speculate: -1 decides by the rows per warp, 1 forces speculative thresholds
+// for long lists (a launch seeded from an earlier one's spec_seed).
+cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream, int64_t rows = -1,
+                            int speculate = -1);
+// max_threads caps the CTA size of the selection merge (256 lets two merge
+// CTAs share an SM).
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T,
-                              int max_N, bool need_sequences, cudaStream_t stream);
+                              int max_N, bool need_sequences, cudaStream_t stream, int max_threads = 0);
+// Kernel launches made by this library in this process (every launcher
+// counts the launches it queues).
+long long kernel_launch_count();
 cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_P,
                            cudaStream_t stream);
 cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool sparse,
@@ -197,5 +224,9 @@ constexpr int kMaxMergeCandidates = 8192;   // K * C per step handled by one CTA
 // memory for every pool size).
 constexpr int kStep0ListMax = 1024;
 constexpr int kMergeThreads = 512;
+// Speculative row-scan thresholds a warp remembers, one per list length
+// (rows of one call can have different list lengths, e.g. per-example beam
+// sizes); also the entries of DecodeParams::spec_seed.
+constexpr int kSpecSlots = 4;
 
 }  // namespace dbs_dev

@@ -11,6 +11,7 @@
 #include <cfloat>
 #include <cmath>
 #include <cstdint>
+#include <atomic>
 #include <mutex>
 #include <tuple>
 #include <vector>
@@ -459,9 +460,6 @@ constexpr int kScanWarpsPerCta = 4;
 __host__ __device__ constexpr int row_scan_hist_ints(int capw, bool k16) {
     return capw - (k16 ? 128 : 0) > 2 * 32 + 136 ? 256 : 0;
 }
-// Speculative thresholds a warp remembers, one per list length (rows of
-// one call can have different list lengths, e.g. per-example beam sizes).
-constexpr int kSpecSlots = 4;
 // Per-warp shared memory: chunk ring | mbarriers | survivor buffer | radix
 // histogram | speculation slots (threshold, list length), 128-byte aligned.
 __host__ __device__ constexpr size_t row_scan_warp_bytes(int capw, bool k16) {
@@ -711,7 +709,8 @@ __device__ __forceinline__ float row_lp(const RowJob& j, int i, bool bf16) {
 
 template <bool k16>
 __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int& e) {
-    while (r >= p.row_prefix[e + 1]) ++e;
+    if (p.step_major_bk) e = static_cast<int>(r / p.step_major_tk);   // uniform batch: rows jump between examples
+    else while (r >= p.row_prefix[e + 1]) ++e;
     const ExampleDesc& d = p.desc[e];
     RowJob j;
     const int64_t lr = r - d.row_begin;
@@ -761,31 +760,73 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     int* hist = reinterpret_cast<int*>(buf + capw);
     float* spec_lp = reinterpret_cast<float*>(hist + hist_ints);   // [kSpecSlots]
     int* spec_len = reinterpret_cast<int*>(spec_lp + kSpecSlots);   // [kSpecSlots], 0 = empty
+    // SMs kept for the merge launches that run beside this scan: a warp there
+    // works only until a warp of this launch runs elsewhere (a launch that
+    // starts while another scan holds the other SMs would otherwise leave
+    // all of its rows unscanned)
+    bool reserved = false;
+    if (p.reserve_sms > 0 && p.worker_flag) {
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        reserved = static_cast<int>(smid) < p.reserve_sms;
+        if (!reserved && lane == 0) atomicExch(p.worker_flag, 1u);
+    }
     unsigned long long* err = p.counters ? p.counters + 3 : nullptr;
-    unsigned long long* next_row = p.counters + 2;
+    unsigned long long* next_row = p.claim ? p.claim : p.counters + 2;
     const bool bf16 = p.x16_bf16 != 0;
     const unsigned lt_mask = (1u << lane) - 1u;
 
     if (lane == 0) {
         for (int s = 0; s < kScanStages; ++s) mbar_init(full + s, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int s = 0; s < kSpecSlots; ++s) spec_len[s] = 0;
+        for (int s = 0; s < kSpecSlots; ++s) {
+            // thresholds an earlier launch of this call learned, if any
+            const unsigned long long seed = p.spec_seed ? p.spec_seed[s] : 0ull;
+            spec_len[s] = static_cast<int>(seed >> 32);
+            spec_lp[s] = __uint_as_float(static_cast<uint32_t>(seed));
+        }
     }
     __syncwarp();
+    // a warp that runs out of rows leaves its thresholds for later launches
+    auto leave_seeds = [&]() {
+        if (p.spec_seed && lane == 0) {
+            for (int s = 0; s < kSpecSlots; ++s)
+                if (spec_len[s] > 0)
+                    p.spec_seed[s] = (static_cast<unsigned long long>(spec_len[s]) << 32) | __float_as_uint(spec_lp[s]);
+        }
+    };
 
+    // Claim index -> row (kNoRow once this launch's claims are used up, or
+    // when a warp on a reserved SM should leave them to the others).
+    constexpr int64_t kNoRow = INT64_MAX;
     auto claim = [&]() -> int64_t {
+        if (reserved) {
+            unsigned int others = 0;
+            if (lane == 0) others = *reinterpret_cast<volatile unsigned int*>(p.worker_flag);
+            if (__shfl_sync(FULL, others, 0)) return kNoRow;
+        }
         unsigned long long r = 0;
         if (lane == 0) r = atomicAdd(next_row, 1ull);
         r = __shfl_sync(FULL, r, 0);
         if (p.first_rows_only)   // claim i: the first row of example i
-            return r < static_cast<unsigned long long>(p.B) ? p.row_prefix[r] : INT64_MAX;
+            return r < static_cast<unsigned long long>(p.B) ? p.row_prefix[r] : kNoRow;
+        if (r >= static_cast<unsigned long long>(p.total_rows)) return kNoRow;
+        if (p.step_major_bk) {
+            // claim order: step, then example, then beam
+            const int64_t c = static_cast<int64_t>(r);
+            const int64_t t = c / p.step_major_bk;
+            const int64_t rem = c - t * p.step_major_bk;
+            const int64_t kk = p.step_major_bk / p.B;   // beams per step
+            const int64_t b = rem / kk;
+            return b * p.step_major_tk + t * kk + (rem - b * kk);
+        }
         return static_cast<int64_t>(r);
     };
 
     // two-row window: `cur` is consumed, `nxt` is being prefetched
     int e_cur = 0, e_nxt = 0;
     int64_t r_cur = claim();
-    if (r_cur >= p.total_rows) return;
+    if (r_cur == kNoRow) { leave_seeds(); return; }
     e_cur = find_example(p.row_prefix, p.B, r_cur);
     RowJob cur = make_job<k16>(p, r_cur, e_cur);
     e_nxt = e_cur;
@@ -815,7 +856,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
                 // move the issue cursor to the next claimed row
                 if (!have_nxt) {
                     const int64_t rn = claim();
-                    if (rn >= p.total_rows) break;
+                    if (rn == kNoRow) break;
                     nxt = make_job<k16>(p, rn, e_nxt);
                     have_nxt = true;
                 }
@@ -1068,6 +1109,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             const int k_spec = C + static_cast<int>(4.0f * sqrtf(static_cast<float>(C)));
             const bool missed = spec_used && cnt < C;
             if (missed) {
+                if (lane == 0 && p.counters) atomicAdd(p.counters, 1ull);   // diagnostics: second passes
                 // The speculative threshold dropped part of the best C: scan
                 // the row again (global memory, token order). No compaction
                 // ran, so the buffer holds every candidate at or above the
@@ -1142,7 +1184,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
         if (!inxt) {
             // nothing of the next row was issued yet (nor claimed)
             const int64_t rn = claim();
-            if (rn >= p.total_rows) return;
+            if (rn == kNoRow) { leave_seeds(); return; }
             nxt = make_job<k16>(p, rn, e_nxt);
             cursor_to(nxt);
         }
@@ -2843,6 +2885,14 @@ static std::vector<std::tuple<const void*, int, size_t>> g_smem_set;
 static std::vector<std::tuple<int, size_t, int>> g_row_scan_occ;
 static std::vector<std::pair<const void*, int>> g_carveout_set;
 
+// Launches queued by the launchers below (process-wide, for benchmarks).
+static std::atomic<long long> g_kernel_launches{0};
+static cudaError_t counted(cudaError_t err) {
+    if (err == cudaSuccess) g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+    return err;
+}
+long long kernel_launch_count() { return g_kernel_launches.load(std::memory_order_relaxed); }
+
 static cudaError_t prefer_shared(const void* fn);
 
 static cudaError_t ensure_dynamic_smem(const void* fn, size_t smem) {
@@ -2887,7 +2937,7 @@ cudaError_t launch_validate(const DecodeParams& p, cudaStream_t stream) {
     cudaError_t err = prefer_shared(reinterpret_cast<const void*>(validate_kernel));
     if (err != cudaSuccess) return err;
     validate_kernel<<<p.B, 1024, 0, stream>>>(p);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 // Per-warp survivor buffer: C kept + max(C, 16) appended between compactions +
@@ -2900,7 +2950,8 @@ static size_t row_scan_smem(int capw, bool k16) {
     return static_cast<size_t>(kScanWarpsPerCta) * row_scan_warp_bytes(capw, k16);
 }
 
-cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream, int64_t rows) {
+cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaStream_t stream, int64_t rows,
+                            int speculate_mode) {
     if (rows < 0) rows = p.total_rows;
     if (rows <= 0) return cudaSuccess;
     const bool k16 = p.x16 != nullptr;
@@ -2950,11 +3001,12 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     if (ctas > need) ctas = need;
     // The speculative threshold pays off over several rows per warp; with
     // few rows a failed guess (a second read of the row) only adds to the tail.
-    const int speculate = (max_C > 32 && rows >= 4 * ctas * kScanWarpsPerCta) ? 1 : 0;
+    int speculate = (max_C > 32 && rows >= 4 * ctas * kScanWarpsPerCta) ? 1 : 0;
+    if (speculate_mode > 0 && max_C > 32) speculate = 1;
     const dim3 grid(static_cast<unsigned>(ctas));
     if (k16) row_scan_kernel<true><<<grid, threads, smem, stream>>>(p, capw, speculate);
     else row_scan_kernel<false><<<grid, threads, smem, stream>>>(p, capw, speculate);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 static size_t merge_rank_smem(int ring, int max_K, int max_C, int max_N, int tab_n) {
@@ -2972,7 +3024,7 @@ static size_t merge_rank_smem(int ring, int max_K, int max_C, int max_N, int tab
 constexpr size_t kMergeRankSmemBudget = 200 * 1024;
 
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T, int max_N,
-                              bool need_sequences, cudaStream_t stream) {
+                              bool need_sequences, cudaStream_t stream, int max_threads) {
     // (the ranking merge reads every row as one list of at most C entries)
     if (!need_sequences && !p.first_row_apart && static_cast<int64_t>(max_K) * max_C <= 256) {
         const int tab_n = (p.Lmax + 1 <= 4096) ? p.Lmax + 1 : 0;
@@ -2993,7 +3045,7 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
             cudaError_t err = ensure_dynamic_smem(reinterpret_cast<const void*>(step_merge_rank_kernel), smem);
             if (err != cudaSuccess) return err;
             step_merge_rank_kernel<<<p.B, threads, smem, stream>>>(p, ring, max_K, max_C, max_N, tab_n);
-            return cudaGetLastError();
+            return counted(cudaGetLastError());
         }
     }
     const int M = max_K * max_C;
@@ -3024,6 +3076,7 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     if (aerr == cudaSuccess) aerr = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (aerr != cudaSuccess) return aerr;
     if (p.B > sms && threads > 256) threads = 256;
+    if (max_threads > 0 && threads > max_threads) threads = max_threads;
     const bool runs = !need_sequences && M <= 1024;
     const void* fn = runs ? reinterpret_cast<const void*>(step_merge_kernel<true>)
                           : reinterpret_cast<const void*>(step_merge_kernel<false>);
@@ -3031,7 +3084,7 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     if (err != cudaSuccess) return err;
     if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2, seq_smem);
     else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2, seq_smem);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_P, cudaStream_t stream) {
@@ -3050,7 +3103,7 @@ cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_
     else if (max_P <= 512) weights_kernel<512><<<blocks, threads, 0, stream>>>(p, max_T);
     else if (max_P <= 1024) weights_kernel<1024><<<blocks, threads, 0, stream>>>(p, max_T);
     else return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 static size_t backward_sweep_smem(int max_T, int max_K, int max_P, bool with_pool) {
@@ -3077,7 +3130,7 @@ cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool 
             if (err != cudaSuccess) return err;
             backward_sweep_kernel<<<p.B, 256, smem, stream>>>(p, p.max_T, max_K, max_P, with_pool ? 1 : 0,
                                                               sparse ? 1 : 0);
-            return cudaGetLastError();
+            return counted(cudaGetLastError());
         }
     }
     const size_t smem = backward_smem_bytes(max_K, max_P);
@@ -3086,7 +3139,7 @@ cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool 
     int threads = 128;
     if (max_P > 512) threads = 256;
     backward_kernel<<<p.B, threads, smem, stream>>>(p, sparse ? 1 : 0, max_K, max_P);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_fill_zero_bulk(float* dst, int64_t count, int num_sms, cudaStream_t stream) {
@@ -3098,7 +3151,7 @@ cudaError_t launch_fill_zero_bulk(float* dst, int64_t count, int num_sms, cudaSt
     if (blocks > tiles) blocks = tiles;
     if (blocks < 1) blocks = 1;
     fill_zero_bulk_kernel<<<static_cast<unsigned>(blocks), 32, kFillTileBytes, stream>>>(dst, count);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_t stream, int blocks_per_sm) {
@@ -3111,7 +3164,7 @@ cudaError_t launch_fill_zero(float* dst, int64_t count, int num_sms, cudaStream_
     cudaError_t err = prefer_shared(reinterpret_cast<const void*>(fill_zero_kernel));
     if (err != cudaSuccess) return err;
     fill_zero_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(dst, count);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 
@@ -3206,7 +3259,7 @@ cudaError_t launch_backward_noalloc(const BackwardParams& p, int T, int K, int P
     const size_t smem = backward_smem_bytes(K, P);
     const int threads = P > 512 ? 256 : 128;
     backward_noalloc_kernel<<<p.B, threads, smem, stream>>>(q, T, K, P, tab, scratch);
-    return cudaGetLastError();
+    return counted(cudaGetLastError());
 }
 
 }  // namespace dbs_dev

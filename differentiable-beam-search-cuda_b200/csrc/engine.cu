@@ -242,6 +242,7 @@ struct Slot {
 };
 
 std::atomic<unsigned long long> g_last_merge_rescans{0};
+std::atomic<unsigned long long> g_last_row_rescans{0};
 std::atomic<unsigned long long> g_timeouts{0};
 
 // Reads the counters an asynchronous decode left in the slot (its event has
@@ -250,6 +251,7 @@ void settle(Slot* s) {
     if (!s->pending) return;
     const unsigned long long merge = s->pending[1];
     const unsigned long long timeout = s->pending[3];
+    g_last_row_rescans.store(s->pending[0]);
     s->pending = nullptr;
     g_last_merge_rescans.store(merge);
     if (timeout) {
@@ -266,14 +268,31 @@ class Arena {
         Slot* s = nullptr;
         {
             std::lock_guard<std::mutex> lock(mu_);
-            // prefer an idle slot whose last use has finished
+            // Prefer an idle slot whose last use has finished and that is
+            // already large enough (the smallest such), then the largest idle
+            // finished one: calls of different sizes (a decode and its
+            // backward) alternating over the slots must not free and
+            // reallocate a workspace on every call.
+            Slot* fit = nullptr;
+            Slot* big = nullptr;
+            Slot* busy = nullptr;
             for (Slot* c : slots_) {
                 if (c->device != device || c->in_use) continue;
-                if (cudaEventQuery(c->done) == cudaSuccess) { s = c; break; }
-                cudaGetLastError();
-                if (!s) s = c;
+                if (cudaEventQuery(c->done) != cudaSuccess) {
+                    cudaGetLastError();
+                    if (!busy) busy = c;
+                    continue;
+                }
+                if (c->dev_bytes >= dev_bytes && c->pinned_bytes >= pinned_bytes) {
+                    if (!fit || c->dev_bytes < fit->dev_bytes) fit = c;
+                } else if (!big || c->dev_bytes > big->dev_bytes) {
+                    big = c;
+                }
             }
-            if (!s || (cudaEventQuery(s->done) != cudaSuccess && count_on(device) < kMaxSlots)) {
+            s = fit ? fit : (big ? big : busy);
+            // a new slot rather than waiting for a busy one or growing a small one
+            if (!s || ((s == busy || s->dev_bytes < dev_bytes || s->pinned_bytes < pinned_bytes) &&
+                       count_on(device) < kMaxSlots)) {
                 cudaGetLastError();
                 s = new Slot;
                 s->device = device;
@@ -347,6 +366,9 @@ struct Lease {
 // merge (the dense gradient zero fill).
 struct Helper {
     cudaStream_t side = nullptr;
+    cudaStream_t side2 = nullptr;   // second row-scan stream of a pipelined batch decode
+    cudaStream_t mside = nullptr;   // merges of a pipelined batch decode, at the highest priority
+    cudaEvent_t merged = nullptr;
     cudaEvent_t before = nullptr;
     cudaEvent_t after = nullptr;
     std::vector<cudaEvent_t> seg;   // end of each row-scan segment of a pipelined decode
@@ -361,6 +383,12 @@ Helper& helper_locked() {
     Helper& h = g_helpers[dev];
     if (!h.side) {
         check_cuda(cudaStreamCreateWithFlags(&h.side, cudaStreamNonBlocking), "cudaStreamCreate(helper)");
+        check_cuda(cudaStreamCreateWithFlags(&h.side2, cudaStreamNonBlocking), "cudaStreamCreate(helper)");
+        // a merge CTA that waits for room is placed before the scans' CTAs
+        int lo = 0, hi = 0;
+        check_cuda(cudaDeviceGetStreamPriorityRange(&lo, &hi), "cudaDeviceGetStreamPriorityRange");
+        check_cuda(cudaStreamCreateWithPriority(&h.mside, cudaStreamNonBlocking, hi), "cudaStreamCreate(helper)");
+        check_cuda(cudaEventCreateWithFlags(&h.merged, cudaEventDisableTiming), "cudaEventCreate");
         check_cuda(cudaEventCreateWithFlags(&h.before, cudaEventDisableTiming), "cudaEventCreate");
         check_cuda(cudaEventCreateWithFlags(&h.after, cudaEventDisableTiming), "cudaEventCreate");
     }
@@ -369,10 +397,14 @@ Helper& helper_locked() {
 
 }  // namespace
 
-void last_decode_diagnostics(unsigned long long* merge_rescans, unsigned long long* timeouts) {
+void last_decode_diagnostics(unsigned long long* merge_rescans, unsigned long long* timeouts,
+                             unsigned long long* row_rescans) {
     if (merge_rescans) *merge_rescans = g_last_merge_rescans.load();
+    if (row_rescans) *row_rescans = g_last_row_rescans.load();
     if (timeouts) *timeouts = g_timeouts.load();
 }
+
+long long kernel_launches() { return dbs_dev::kernel_launch_count(); }
 
 void profile_enable(unsigned mask) {
     std::lock_guard<std::mutex> lock(g_prof_mu);
@@ -414,7 +446,7 @@ static int list_capacity_for(int N, int K, bool dynamic) {
 }
 
 int list_capacity(const Options& opt, int K, bool pool, bool dynamic) {
-    const int P = std::max(K, K * opt.relaxed_pool_multiplier);
+    const int P = pool_size(K, opt.relaxed_pool_multiplier);
     return list_capacity_for(pool ? P : K, K, dynamic);
 }
 
@@ -434,6 +466,28 @@ int list_capacity(const Options& opt, int K, bool pool, bool dynamic) {
 // 64K rows (measured with T = 64: K = 32, 256 examples 33.5 -> 22.2 ms and
 // 32 examples 5.8 -> 4.9 ms; K = 64, 128 examples 25.8 -> 22.5 ms; but
 // K = 16 with 32 examples, 32K rows, 2.73 -> 2.88 ms).
+// Pipelined batch decode (see decode()): segments per call, SMs kept free
+// for the merges while the scans run (-1: by batch size), and a switch
+// (off by default); DBS_BATCH_PIPELINE=1, DBS_PIPE_SEGMENTS=<n> and
+// DBS_PIPE_RESERVE=<SMs> override them (read once, for measurements).
+struct PipeTuning {
+    bool enabled = false;
+    int segments = 8;
+    int reserve = -1;
+};
+const PipeTuning& pipe_tuning() {
+    static const PipeTuning t = [] {
+        PipeTuning v;
+        if (const char* e = std::getenv("DBS_BATCH_PIPELINE")) v.enabled = std::atoi(e) != 0;
+        if (const char* e = std::getenv("DBS_PIPE_SEGMENTS")) v.segments = std::max(2, std::atoi(e));
+        if (const char* e = std::getenv("DBS_PIPE_RESERVE")) v.reserve = std::max(0, std::atoi(e));
+        return v;
+    }();
+    return t;
+}
+// CTA size of the pipelined merges: two fit an SM beside nothing else.
+constexpr int kPipeMergeThreads = 256;
+
 constexpr int kShortListEntries = 64;
 constexpr int kShortListMinExamples = 32;
 constexpr int64_t kShortListMinRows = 65536;
@@ -456,7 +510,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         for (const ExampleSpec& e : ex) {
             kmax = std::max(kmax, e.K);
             nrows += static_cast<int64_t>(e.T) * e.K;
-            const int N = std::max(e.K, e.K * opt.relaxed_pool_multiplier);
+            const int N = pool_size(e.K, opt.relaxed_pool_multiplier);
             cut = cut || list_capacity_for(N, e.K, false) > kShortListEntries;
         }
         // (calls whose merge would be the ranking merge keep full lists)
@@ -537,6 +591,31 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         if (n_seg < 2) n_seg = 0;
     }
     const bool pipeline = n_seg > 0;
+    // Many examples of one shape whose merge is the selection merge: the row
+    // scan runs step-major (claims ordered by step, then example, then beam)
+    // in segments of steps, alternating between two helper streams so that
+    // consecutive segments overlap instead of each draining the GPU; the
+    // merge of segment i (every example, one CTA each) runs on `stream` as
+    // soon as scan i is done, beside the scans of later segments, on SMs the
+    // scans leave free. Only the last segment's merge is not hidden.
+    bool uniform = true;
+    for (const ExampleSpec& e : ex) uniform = uniform && e.T == ex[0].T && e.K == ex[0].K;
+    std::vector<int> bp_bound;   // segment boundaries in steps
+    int bp_reserve = 0;
+    if (B >= 2 && uniform && ctl.scan && ctl.merge && !ext_lists && scan_begin == 0 && scan_end == rows &&
+        ctl.t_begin <= 0 && ctl.t_end >= max_T && !ctl.merge_state && !ctl.row_allow && max_T >= 16 &&
+        (dynamic || static_cast<int64_t>(max_K) * max_C > 256) && pipe_tuning().enabled) {
+        const int want = pipe_tuning().segments;
+        const int sz = std::max(2, (max_T + want - 1) / want);
+        for (int t = 0; t < max_T; t += sz) bp_bound.push_back(t);
+        bp_bound.push_back(max_T);
+        if (bp_bound.size() < 3) bp_bound.clear();   // fewer than two segments
+        // two 256-thread merge CTAs per reserved SM
+        bp_reserve = pipe_tuning().reserve >= 0 ? pipe_tuning().reserve : std::min(24, std::max(8, (B + 1) / 2));
+        bp_reserve = std::min(bp_reserve, device_sm_count() / 4);
+    }
+    const bool batch_pipe = !bp_bound.empty();
+    const int bp_n = batch_pipe ? static_cast<int>(bp_bound.size()) - 1 : 0;
     size_t hdr = 0;
     hdr += bytes_of<dbs_dev::ExampleDesc>(B);
     hdr += bytes_of<int64_t>(B + 1);
@@ -544,6 +623,11 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     hdr += bytes_of<int32_t>(B);
     hdr += bytes_of<unsigned long long>(4);
     if (pipeline) hdr += bytes_of<unsigned long long>(n_seg);   // first row of each scan segment
+    // claim counter of each scan launch (the segments and the step-0 lists), speculation seeds
+    if (batch_pipe) {
+        hdr += bytes_of<unsigned long long>(bp_n + 1) + bytes_of<unsigned long long>(dbs_dev::kSpecSlots) +
+               bytes_of<unsigned int>(bp_n);   // + a worker flag per segment
+    }
     if (ext_lists && (!ctl.list_count || !ctl.list_bound)) throw InvalidArgument("row lists need counts and bounds");
     if (!ext_lists && !(ctl.scan && ctl.merge)) throw InvalidArgument("a split decode needs caller row lists");
     size_t ws = hdr;
@@ -553,7 +637,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         ws += bytes_of<float>(static_cast<size_t>(rows));
     }
     if (dynamic && !ctl.seq_scratch) ws += bytes_of<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
-    if (pipeline) ws += bytes_of<float>(static_cast<size_t>(4) * max_K);   // merge state between segments
+    if (pipeline || batch_pipe) ws += bytes_of<float>(static_cast<size_t>(4) * max_K * B);   // merge state between segments
     trace.mark("prepared");
     Lease lease(ws, hdr, stream);
     trace.mark("slot");
@@ -583,6 +667,19 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         for (int i = 0; i < n_seg; ++i)
             h_seeds[i] = static_cast<unsigned long long>(i) * seg_steps * desc[0].K;
     }
+    unsigned long long* d_claims = nullptr;
+    unsigned long long* d_spec = nullptr;
+    unsigned int* d_flags = nullptr;
+    if (batch_pipe) {
+        d_claims = cv.take<unsigned long long>(bp_n + 1);
+        unsigned long long* hc = hv.take<unsigned long long>(bp_n + 1);
+        for (int i = 0; i < bp_n; ++i) hc[i] = static_cast<unsigned long long>(bp_bound[i]) * B * max_K;
+        hc[bp_n] = 0;   // the step-0 lists: claim i is example i
+        d_spec = cv.take<unsigned long long>(dbs_dev::kSpecSlots);
+        std::memset(hv.take<unsigned long long>(dbs_dev::kSpecSlots), 0, sizeof(unsigned long long) * dbs_dev::kSpecSlots);
+        d_flags = cv.take<unsigned int>(bp_n);
+        std::memset(hv.take<unsigned int>(bp_n), 0, sizeof(unsigned int) * bp_n);
+    }
     check_cuda(cudaMemcpyAsync(lease.s->dev, lease.s->pinned, cv.off, cudaMemcpyHostToDevice, stream),
                "upload decode metadata");
     if (ext_lists) {
@@ -597,7 +694,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     p.seq_scratch = !dynamic ? nullptr
                   : ctl.seq_scratch ? ctl.seq_scratch
                                     : cv.take<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
-    float* d_state = pipeline ? cv.take<float>(static_cast<size_t>(4) * max_K) : nullptr;
+    float* d_state = (pipeline || batch_pipe) ? cv.take<float>(static_cast<size_t>(4) * max_K * B) : nullptr;
     p.t_begin = ctl.t_begin;
     p.t_end = ctl.t_end;
     p.merge_state = ctl.merge_state;
@@ -649,19 +746,18 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     const size_t st_bytes = reinterpret_cast<char*>(p.counters + 4) - reinterpret_cast<char*>(p.status);
     const bool validate = opt.validate_inputs && ctl.scan;   // a merge-only call trusts its scan call
     if (validate) {
-        // the small validation kernel runs on the helper stream beside the row
-        // scan (both only read log_probs), so it costs the scan no time
-        std::lock_guard<std::mutex> lock(g_helper_mu);
-        Helper& hp = helper_locked();
-        check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
-        check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
+        // The small validation kernel runs first, on the caller's stream: it
+        // takes microseconds alone, whereas beside a persistent row-scan grid
+        // it waited for SM room until the scan ended, and the host waits for
+        // its verdict before it queues the merge. Its verdict is then back
+        // while the scan runs.
         {
-            ProfileScope ps(kValidate, hp.side);
-            check_cuda(dbs_dev::launch_validate(p, hp.side), "validate kernel");
+            ProfileScope ps(kValidate, stream);
+            check_cuda(dbs_dev::launch_validate(p, stream), "validate kernel");
         }
-        check_cuda(cudaMemcpyAsync(lease.s->pinned + st_off, p.status, st_bytes, cudaMemcpyDeviceToHost, hp.side),
+        check_cuda(cudaMemcpyAsync(lease.s->pinned + st_off, p.status, st_bytes, cudaMemcpyDeviceToHost, stream),
                    "read status");
-        check_cuda(cudaEventRecord(lease.s->validated, hp.side), "cudaEventRecord");
+        check_cuda(cudaEventRecord(lease.s->validated, stream), "cudaEventRecord");
     }
     if (pipeline) {
         // Segments of steps: the helper stream seeds the row-claim counter
@@ -683,10 +779,9 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         {
             std::lock_guard<std::mutex> lock(g_helper_mu);
             Helper& hp = helper_locked();
-            if (!validate) {   // the metadata upload and the caller's earlier work come first
-                check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
-                check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
-            }
+            // the metadata upload, the validation and the caller's earlier work come first
+            check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
+            check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
             for (int i = 0; i < n_seg; ++i) {
                 const int64_t r0 = static_cast<int64_t>(i) * seg_steps * K0;
                 const int64_t r1 = std::min<int64_t>(rows, r0 + static_cast<int64_t>(seg_steps) * K0);
@@ -735,6 +830,95 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         }
         trace.mark("merge queued");
         check_cuda(cudaStreamWaitEvent(stream, seg_done[n_seg], 0), "cudaStreamWaitEvent");
+    } else if (batch_pipe) {
+        // ev[i]: scan segment i listed; ev[bp_n]: the step-0 lists; ev[bp_n + 1]:
+        // the helper streams' part of the call is over
+        std::vector<cudaEvent_t> ev(bp_n + 2, nullptr);
+        struct EventsGuard {
+            std::vector<cudaEvent_t>& v;
+            ~EventsGuard() {
+                for (cudaEvent_t e : v)
+                    if (e) cudaEventDestroy(e);   // released once the queued waits are done
+            }
+        } events_guard{ev};
+        for (cudaEvent_t& e : ev) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+        const int sms = device_sm_count();
+        {
+            std::lock_guard<std::mutex> lock(g_helper_mu);
+            Helper& hp = helper_locked();
+            check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
+            check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
+            check_cuda(cudaStreamWaitEvent(hp.side2, hp.before, 0), "cudaStreamWaitEvent");
+            {
+                ProfileScope ps(kRowScan, hp.side);   // one pair around all of the call's scans
+                if (short_lists) {
+                    // the live step-0 row of every example, with its long list
+                    dbs_dev::DecodeParams s0 = p;
+                    s0.first_rows_only = 1;
+                    s0.claim = d_claims + bp_n;
+                    check_cuda(dbs_dev::launch_row_scan(s0, max_C0, sms, hp.side2, B), "row scan kernel (step 0)");
+                }
+                check_cuda(cudaEventRecord(ev[bp_n], hp.side2), "cudaEventRecord");
+                dbs_dev::DecodeParams sp = p;
+                sp.step_major_bk = static_cast<int64_t>(B) * max_K;
+                sp.step_major_tk = static_cast<int64_t>(max_T) * max_K;
+                sp.spec_seed = d_spec;
+                sp.reserve_sms = bp_reserve;
+                for (int i = 0; i < bp_n; ++i) {
+                    cudaStream_t ss = (i & 1) ? hp.side2 : hp.side;
+                    sp.claim = d_claims + i;
+                    sp.worker_flag = d_flags + i;
+                    sp.total_rows = static_cast<int64_t>(bp_bound[i + 1]) * B * max_K;   // claim limit
+                    const int64_t seg_rows = static_cast<int64_t>(bp_bound[i + 1] - bp_bound[i]) * B * max_K;
+                    check_cuda(dbs_dev::launch_row_scan(sp, max_C, sms, ss, seg_rows, 1), "row scan kernel");
+                    check_cuda(cudaEventRecord(ev[i], ss), "cudaEventRecord");
+                }
+                check_cuda(cudaEventRecord(hp.after, hp.side2), "cudaEventRecord");
+                check_cuda(cudaStreamWaitEvent(hp.side, hp.after, 0), "cudaStreamWaitEvent");
+            }
+            if (ctl.zero_fill && ctl.zero_fill_count > 0) {
+                ProfileScope ps(kFillZero, hp.side);
+                check_cuda(dbs_dev::launch_fill_zero_bulk(ctl.zero_fill, ctl.zero_fill_count, sms, hp.side),
+                           "zero fill kernel");
+            }
+            check_cuda(cudaEventRecord(ev[bp_n + 1], hp.side), "cudaEventRecord");
+        }
+        trace.mark("row scan queued");
+        if (validate) {
+            check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
+            trace.mark("validate synced");
+            for (int b = 0; b < B; ++b) {
+                if (h_status[b]) {
+                    // the workspace is released on `stream`: it must cover the scans
+                    check_cuda(cudaStreamWaitEvent(stream, ev[bp_n + 1], 0), "cudaStreamWaitEvent");
+                    throw InvalidArgument("log_probs contains NaN or +Inf");
+                }
+            }
+        }
+        {
+            // the merges run on the highest-priority helper stream: when an SM
+            // frees up, a waiting merge CTA is placed before a scan CTA
+            std::lock_guard<std::mutex> lock(g_helper_mu);
+            Helper& hp = helper_locked();
+            check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
+            check_cuda(cudaStreamWaitEvent(hp.mside, hp.before, 0), "cudaStreamWaitEvent");
+            for (int i = 0; i < bp_n; ++i) {
+                check_cuda(cudaStreamWaitEvent(hp.mside, ev[i], 0), "cudaStreamWaitEvent");
+                if (i == 0) check_cuda(cudaStreamWaitEvent(hp.mside, ev[bp_n], 0), "cudaStreamWaitEvent");
+                dbs_dev::DecodeParams mp = p;
+                mp.t_begin = bp_bound[i];
+                mp.t_end = bp_bound[i + 1];
+                mp.merge_state = d_state;
+                ProfileScope ps(kStepMerge, hp.mside);
+                check_cuda(dbs_dev::launch_step_merge(mp, max_K, max_C, max_T, max_N, dynamic, hp.mside,
+                                                      kPipeMergeThreads),
+                           "step merge kernel");
+            }
+            check_cuda(cudaEventRecord(hp.merged, hp.mside), "cudaEventRecord");
+            check_cuda(cudaStreamWaitEvent(stream, hp.merged, 0), "cudaStreamWaitEvent");
+        }
+        trace.mark("merge queued");
+        check_cuda(cudaStreamWaitEvent(stream, ev[bp_n + 1], 0), "cudaStreamWaitEvent");
     } else {
         if (ctl.scan && scan_end > scan_begin) {
             ProfileScope ps(kRowScan, stream);
@@ -809,6 +993,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
             stats->merge_fallbacks = h_counters[1];
         }
         g_last_merge_rescans.store(h_counters[1]);
+        g_last_row_rescans.store(h_counters[0]);
         if (h_counters[3]) {
             g_timeouts.fetch_add(1);
             throw CudaFailure("row scan: a shared-memory copy did not complete within the wait bound");
@@ -903,7 +1088,7 @@ void backward(const Options& opt, int V, const std::vector<ExampleSpec>& ex, con
 void backward_sparse_noalloc(const Options& opt, int V, int B, int T, const BackwardInputs& in,
                              const BackwardOutputs& out, cudaStream_t stream) {
     const int K = opt.beam_size;
-    const int P = std::max(K, K * opt.relaxed_pool_multiplier);
+    const int P = pool_size(K, opt.relaxed_pool_multiplier);
     if (T > dbs_dev::kNoAllocMaxSteps)
         throw LengthError("the allocation-free backward takes at most " + std::to_string(dbs_dev::kNoAllocMaxSteps) +
                           " steps");

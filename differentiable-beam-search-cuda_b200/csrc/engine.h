@@ -187,8 +187,14 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
             bool weights, cudaStream_t stream, DecodeStats* stats, const DecodeControl& ctl);
 
 // Diagnostics of the most recent decode whose counters have been read back
-// (process-wide): rows rescanned by the step merge, device wait timeouts.
-void last_decode_diagnostics(unsigned long long* merge_rescans, unsigned long long* timeouts);
+// (process-wide): rows rescanned by the step merge, device wait timeouts,
+// and rows the row scan read a second time (a speculative threshold that
+// kept fewer than the row's list length).
+void last_decode_diagnostics(unsigned long long* merge_rescans, unsigned long long* timeouts,
+                             unsigned long long* row_rescans = nullptr);
+
+// Kernel launches this library has queued in this process.
+long long kernel_launches();
 
 struct BackwardInputs {
     // trace (device), tight layout from `decode`

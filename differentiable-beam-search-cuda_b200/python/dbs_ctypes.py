@@ -202,6 +202,7 @@ DEVICE_FUNCTIONS = {
     "dbs_device_profile": (_I, [_I]),
     "dbs_device_profile_read": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_I64)]),
     "dbs_device_profile_kernels": (_I, [ctypes.c_uint]),
+    "dbs_device_kernel_launches": (_I, [ctypes.POINTER(_I64)]),
     "dbs_device_row_list_capacity": (_I, [_VP, _I, ctypes.POINTER(_I)]),
     "dbs_device_scan_rows": (_I, [_VP, _VP, _I, _I, _I, _I, _I64, _I64, _VP, _VP, _VP, _VP]),
     "dbs_device_merge_rows": (_I, [_VP, _VP, _I, _I, _I, _VP, _VP, _VP, ctypes.POINTER(DBSDeviceDecodeOutputs), _VP]),

@@ -64,8 +64,12 @@ typedef int (*DBSModelStepFn)(void* user_data, int batch_index, int step,
                               const int32_t* prev_tokens, const float* prev_scores,
                               int beam_size, int vocab_size, float* out_log_probs);
 
-/* include/dbs.h:64-72. Host callbacks cannot run inside the device scan; a
- * non-null token_filter makes dbs_decode_constrained_ex fail with -2. */
+/* include/dbs.h:64-72. The callback is host code: with a non-null
+ * token_filter, dbs_decode_constrained_ex decodes one step at a time, asks
+ * the filter about each step's candidates on the host (in the reference's
+ * order: parent ascending, token ascending, only tokens that pass the
+ * forced / banned / minimum-length / n-gram checks) and scans and merges the
+ * step on the device with its verdicts. */
 typedef int (*DBSTokenFilterFn)(void* user_data, int batch_index, int step, int parent_beam,
                                 const int32_t* prefix_tokens, int prefix_len, int token);
 
@@ -76,7 +80,7 @@ typedef struct DBSAdvancedConstraintsC {
     int min_length;                    /* negative = decoder default */
     float repetition_penalty;          /* <=1 disables */
     int no_repeat_ngram_size;          /* <=0 disables */
-    DBSTokenFilterFn token_filter;     /* must be NULL on the device decoder */
+    DBSTokenFilterFn token_filter;     /* optional host callback, see DBSTokenFilterFn */
     void* token_filter_user_data;
     int batch_index;
 } DBSAdvancedConstraintsC;

@@ -156,11 +156,17 @@ DBS_EXPORT int dbs_device_backward_sparse_noalloc(DBSDecoderHandle* handle, int 
                                                   float* grad_initial_scores, void* cuda_stream);
 
 /* Diagnostics of the most recent device decode whose counters have been read
- * back (process-wide): rows rescanned by the row scan (always 0: the scan is
- * exact in one pass) and rows the step merge could not prove complete and
- * rescanned from HBM. */
+ * back (process-wide): rows the row scan read a second time from HBM (a
+ * speculative threshold, learned from earlier rows, kept fewer entries than
+ * the row's list length; the list stays exact) and rows the step merge could
+ * not prove complete and rescanned from HBM. No counterpart in the reference. */
 DBS_EXPORT int dbs_device_last_rescan_counts(DBSDecoderHandle* handle, int64_t* row_rescans,
                                              int64_t* merge_rescans);
+
+/* Kernel launches this library has queued in this process so far (for
+ * benchmarks counting the launches of a timed region). No counterpart in
+ * the reference. */
+DBS_EXPORT int dbs_device_kernel_launches(int64_t* count);
 
 /* Live kernel timing for benchmarks: enable = 1 starts bracketing every
  * device launch with CUDA events on its stream, 0 stops, -1 clears the
