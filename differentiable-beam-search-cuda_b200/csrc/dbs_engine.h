@@ -100,25 +100,12 @@ struct DecodeParams {
     // the step merge reads step 0 as that one list.
     int32_t first_row_apart;
     int32_t first_rows_only;
-    // Row-scan launch controls. `claim` is the counter this launch claims
-    // rows from (nullptr: counters[2]); concurrent launches of one call each
-    // get their own. With step_major_bk = B*K (a uniform batch of B
-    // examples, K beams, row stride step_major_tk = T*K per example) claim c
-    // scans step c / (B*K) of example (c / K) % B, beam c % K, so a launch
-    // over claims [t0*B*K, t1*B*K) lists exactly the rows of steps
-    // [t0, t1) of every example. spec_seed (kSpecSlots entries of
-    // C << 32 | float bits, 0 = empty) carries speculative thresholds from
-    // one launch to the next. Warps on an SM whose id is below reserve_sms
-    // stop claiming rows (and return) once a warp of the same launch on
-    // another SM has started, which it marks in *worker_flag (zeroed per
-    // launch): those SMs are then left to merge launches that run beside
-    // the scan, and every claimed row is still scanned by its warp.
-    unsigned long long* claim;
+    // Step-major row claims (the fused decode of a uniform batch of B
+    // examples, K beams, row stride step_major_tk = T*K per example): with
+    // step_major_bk = B*K, claim c scans step c / (B*K) of example
+    // (c / K) % B, beam c % K, so the rows of early steps are listed first.
     int64_t step_major_bk;
     int64_t step_major_tk;
-    unsigned long long* spec_seed;
-    int32_t reserve_sms;
-    unsigned int* worker_flag;
     // workspace
     uint64_t* lists;              // row lists, key = ord(lp)<<32 | ~token
     int32_t* list_count;          // [total_rows]
@@ -196,6 +183,13 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
 long long kernel_launch_count();
 cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_P,
                            cudaStream_t stream);
+// Fused decode of a uniform batch without sequence constraints (rows
+// claimed step-major; p.merge_state holds [B][4][max_K] beams when
+// merge_ctas < B; step_done [B*T] zeroed). cudaErrorNotSupported when the
+// shape or the device does not allow it (the caller then scans and merges
+// in separate launches).
+cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int max_N, int merge_ctas,
+                                unsigned int* step_done, int num_sms, cudaStream_t stream);
 cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool sparse,
                             cudaStream_t stream);
 // blocks_per_sm: 4 fills the GPU; 1 leaves three quarters of every SM's
@@ -224,6 +218,11 @@ constexpr int kMaxMergeCandidates = 8192;   // K * C per step handled by one CTA
 // memory for every pool size).
 constexpr int kStep0ListMax = 1024;
 constexpr int kMergeThreads = 512;
+// Compact merge (no sequence constraints): CTA size and candidates per step.
+constexpr int kListMergeThreads = 512;
+constexpr int kListMergeMaxCandidates = 8 * kListMergeThreads;
+// Fused decode (scan and merge in one cooperative launch): CTA size.
+constexpr int kFusedThreads = 512;
 // Speculative row-scan thresholds a warp remembers, one per list length
 // (rows of one call can have different list lengths, e.g. per-example beam
 // sizes); also the entries of DecodeParams::spec_seed.

@@ -11,6 +11,7 @@
 #include <cfloat>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <atomic>
 #include <mutex>
 #include <tuple>
@@ -699,6 +700,7 @@ struct RowJob {
     int h;       // unaligned head elements
     int nv;      // float4 in the aligned body
     int chunks;
+    int done_idx;  // e * T + t: the step-completion counter of the row (fused decode)
 };
 
 template <bool k16>
@@ -742,12 +744,22 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     j.h = h;
     j.nv = (p.V - h) >> (4 - kShift);
     j.chunks = (j.forced >= 0 || j.dead || j.apart) ? 0 : (j.nv + kScanChunkF4 - 1) / kScanChunkF4;
+    j.done_idx = e * d.T + t;
     return j;
 }
 
+// The row-scan loop of one warp (per-warp shared memory at smem_raw + warp
+// index * row_scan_warp_bytes). With step_done, each finished row (its list,
+// count and bound written and fenced) adds one to step_done[e * T + t].
+__device__ __forceinline__ void scan_row_done(unsigned int* step_done, int idx, int lane) {
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) atomicAdd(step_done + idx, 1u);
+}
+
 template <bool k16>
-__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(DecodeParams p, int capw, int speculate) {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
+__device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, int speculate, unsigned char* smem_raw,
+                                              unsigned int* step_done) {
     constexpr unsigned FULL = 0xFFFFFFFFu;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // per-warp region: ring | barriers | survivor buffer
@@ -760,51 +772,21 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     int* hist = reinterpret_cast<int*>(buf + capw);
     float* spec_lp = reinterpret_cast<float*>(hist + hist_ints);   // [kSpecSlots]
     int* spec_len = reinterpret_cast<int*>(spec_lp + kSpecSlots);   // [kSpecSlots], 0 = empty
-    // SMs kept for the merge launches that run beside this scan: a warp there
-    // works only until a warp of this launch runs elsewhere (a launch that
-    // starts while another scan holds the other SMs would otherwise leave
-    // all of its rows unscanned)
-    bool reserved = false;
-    if (p.reserve_sms > 0 && p.worker_flag) {
-        uint32_t smid;
-        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-        reserved = static_cast<int>(smid) < p.reserve_sms;
-        if (!reserved && lane == 0) atomicExch(p.worker_flag, 1u);
-    }
     unsigned long long* err = p.counters ? p.counters + 3 : nullptr;
-    unsigned long long* next_row = p.claim ? p.claim : p.counters + 2;
+    unsigned long long* next_row = p.counters + 2;
     const bool bf16 = p.x16_bf16 != 0;
     const unsigned lt_mask = (1u << lane) - 1u;
 
     if (lane == 0) {
         for (int s = 0; s < kScanStages; ++s) mbar_init(full + s, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int s = 0; s < kSpecSlots; ++s) {
-            // thresholds an earlier launch of this call learned, if any
-            const unsigned long long seed = p.spec_seed ? p.spec_seed[s] : 0ull;
-            spec_len[s] = static_cast<int>(seed >> 32);
-            spec_lp[s] = __uint_as_float(static_cast<uint32_t>(seed));
-        }
+        for (int s = 0; s < kSpecSlots; ++s) spec_len[s] = 0;
     }
     __syncwarp();
-    // a warp that runs out of rows leaves its thresholds for later launches
-    auto leave_seeds = [&]() {
-        if (p.spec_seed && lane == 0) {
-            for (int s = 0; s < kSpecSlots; ++s)
-                if (spec_len[s] > 0)
-                    p.spec_seed[s] = (static_cast<unsigned long long>(spec_len[s]) << 32) | __float_as_uint(spec_lp[s]);
-        }
-    };
 
-    // Claim index -> row (kNoRow once this launch's claims are used up, or
-    // when a warp on a reserved SM should leave them to the others).
+    // Claim index -> row (kNoRow once this launch's claims are used up).
     constexpr int64_t kNoRow = INT64_MAX;
     auto claim = [&]() -> int64_t {
-        if (reserved) {
-            unsigned int others = 0;
-            if (lane == 0) others = *reinterpret_cast<volatile unsigned int*>(p.worker_flag);
-            if (__shfl_sync(FULL, others, 0)) return kNoRow;
-        }
         unsigned long long r = 0;
         if (lane == 0) r = atomicAdd(next_row, 1ull);
         r = __shfl_sync(FULL, r, 0);
@@ -826,7 +808,7 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
     // two-row window: `cur` is consumed, `nxt` is being prefetched
     int e_cur = 0, e_nxt = 0;
     int64_t r_cur = claim();
-    if (r_cur == kNoRow) { leave_seeds(); return; }
+    if (r_cur == kNoRow) return;
     e_cur = find_example(p.row_prefix, p.B, r_cur);
     RowJob cur = make_job<k16>(p, r_cur, e_cur);
     e_nxt = e_cur;
@@ -1180,11 +1162,12 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
             }
             __syncwarp();
         }
+        if (step_done && !j.apart) scan_row_done(step_done, j.done_idx, lane);
         // advance to the next claimed row
         if (!inxt) {
             // nothing of the next row was issued yet (nor claimed)
             const int64_t rn = claim();
-            if (rn == kNoRow) { leave_seeds(); return; }
+            if (rn == kNoRow) return;
             nxt = make_job<k16>(p, rn, e_nxt);
             cursor_to(nxt);
         }
@@ -1193,6 +1176,12 @@ __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(Deco
         inxt = false;
         e_cur = e_nxt;
     }
+}
+
+template <bool k16>
+__global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(DecodeParams p, int capw, int speculate) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    row_scan_body<k16>(p, capw, speculate, smem_raw, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -1881,6 +1870,808 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
         const int64_t o = d.final_offset + k;
         if (p.final_raw_scores) p.final_raw_scores[o] = s.prev_raw[k];
         if (p.final_scores) p.final_scores[o] = __fdiv_rn(s.prev_raw[k], p.pen[len]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2c. Compact selection merge (no repetition penalty / n-gram blocking /
+//     prefix-keeping, at most 4096 candidates per step, pools up to 1024).
+//
+// One CTA of NT threads per example walks its steps. Every thread owns
+// kLmPer candidate slots of a step (slot idx = tid + u * NT: entry idx % C
+// of row idx / C) and holds their 64-bit (rank, raw) keys and tokens in
+// registers, so a step needs no shared-memory copy of its K row lists. A
+// radix select over the 128-bit candidate keys (rank, raw, then parent and
+// token; 8 bits per pass from the highest bit where the keys differ,
+// per-warp histograms) narrows the keys that can be among the top N to at
+// most sel_cap; those are gathered and sorted by a bitonic network, and the
+// first N are the step's pool (the same order as the reference's
+// candidate_better, src/differentiable_beam.cpp:291-298). The exactness
+// proof and the rescans of truncated rows follow the selection merge.
+// ---------------------------------------------------------------------------
+
+// Descending bitonic sort of n2 (a power of two) two-word keys, (0, 0) pads
+// last. Called by all threads of the block; ends with a barrier.
+// Shared memory of list_merge_body: selection keys, per-warp histograms and
+// ten per-beam arrays.
+__host__ __device__ constexpr size_t list_merge_smem(int nt, int sel_cap, int max_K) {
+    return static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t) + 256 * sizeof(int) +
+           static_cast<size_t>(max_K) * 10 * sizeof(int) + 0 * nt;
+}
+// Selection buffer: a power of two with room for the top N plus a staging
+// area of at least 256 and of at least one value per thread (rescans).
+__host__ __device__ constexpr int list_merge_sel_cap(int max_N, int nt) {
+    int c = 1;
+    while (c < max_N + (nt > 256 ? nt : 256) || c < 2 * max_N) c <<= 1;
+    return c;
+}
+
+template <int NT>
+__device__ __forceinline__ void lm_sort(uint64_t* hi, uint64_t* lo, int n2) {
+    const int half = n2 >> 1;
+    for (int size = 2; size <= n2; size <<= 1) {
+        for (int st = size >> 1; st > 0; st >>= 1) {
+            for (int pid = threadIdx.x; pid < half; pid += NT) {
+                const int i = ((pid & ~(st - 1)) << 1) | (pid & (st - 1));
+                const int j = i + st;
+                const bool desc = (i & size) == 0;
+                const uint64_t ih = hi[i], jh = hi[j];
+                const uint64_t il = lo[i], jl = lo[j];
+                const bool i_less = key2_less(ih, il, jh, jl);
+                if (i_less == desc) { hi[i] = jh; lo[i] = jl; hi[j] = ih; lo[j] = il; }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// Bounded wait of a merge CTA for the K rows of step t of example e
+// (step_done[e * T + t] == K, counted by the row-scan warps of the same
+// launch after their lists are written). Returns false, after setting the
+// timeout counter, if the rows do not arrive within about two seconds.
+// Called by all threads of the block.
+__device__ __forceinline__ bool wait_step_rows(const DecodeParams& p, const unsigned int* step_done, int idx,
+                                               unsigned int want) {
+    __shared__ int sh_ok;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const long long t0 = clock64();
+        for (;;) {
+            unsigned int v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(step_done + idx) : "memory");
+            if (v >= want) break;
+            if (clock64() - t0 > (4ll << 30)) {
+                ok = 0;
+                if (p.counters) atomicExch(p.counters + 3, 1ull);
+                break;
+            }
+            __nanosleep(200);
+        }
+        sh_ok = ok;
+    }
+    __syncthreads();
+    const bool ok = sh_ok != 0;
+    __threadfence();
+    __syncthreads();   // sh_ok is read by every thread before it can change
+    return ok;
+}
+
+// Steps [t_first, t_stop) of example e. state (global, [4][seq_K] for this
+// example) carries the beams between calls: loaded when t_first > 0,
+// stored when steps remain. With step_done the CTA waits for each step's
+// rows (the fused decode); lists, counts and bounds are read around L1.
+template <int NT, int PER>
+__device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, int t_first, int t_stop, float* state,
+                                                int seq_K, int sel_cap, unsigned char* smem,
+                                                const unsigned int* step_done) {
+    constexpr int NW = NT / 32;
+    constexpr unsigned FULL = 0xFFFFFFFFu;
+    constexpr int kLmPer = PER;
+    const ExampleDesc d = p.desc[e];
+    const int K = d.K, C = d.C, N = d.N, T = d.T, P = d.P;
+    const int V = p.V;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    uint64_t* sh = reinterpret_cast<uint64_t*>(smem);   // [sel_cap] selection / sort keys (high words)
+    uint64_t* sl = sh + sel_cap;                         // [sel_cap] low words
+    int* hist = reinterpret_cast<int*>(sl + sel_cap);    // [256]
+    float* prev_raw = reinterpret_cast<float*>(hist + 256);
+    float* next_raw = prev_raw + seq_K;
+    float* row_bound = next_raw + seq_K;
+    float* row_inv = row_bound + seq_K;
+    int* prev_len = reinterpret_cast<int*>(row_inv + seq_K);
+    int* next_len = prev_len + seq_K;
+    int* ended = next_len + seq_K;
+    int* ended_next = ended + seq_K;
+    int* row_cnt = ended_next + seq_K;
+    int* unsafe = row_cnt + seq_K;
+    __shared__ int sh_n;
+    __shared__ int sh_g;   // gather counter of the step
+    __shared__ int sh_any;
+    __shared__ int sh_over;
+    __shared__ int sh_sel[3];
+    __shared__ unsigned long long sh_mm[2 * NW];
+    const bool use_eos = d.eos >= 0;
+    if (t_stop > T) t_stop = T;
+    __syncthreads();   // the block's previous call is done with the shared arrays
+    for (int k = tid; k < K; k += NT) {
+        if (t_first > 0 && state) {
+            prev_raw[k] = state[k];
+            prev_len[k] = __float_as_int(state[seq_K + k]);
+            ended[k] = __float_as_int(state[2 * seq_K + k]);
+        } else {
+            prev_raw[k] = (k == 0) ? 0.0f : -INFINITY;
+            prev_len[k] = 0;
+            ended[k] = 0;
+        }
+    }
+    int sort_n2 = 1;
+    while (sort_n2 < sel_cap) sort_n2 <<= 1;   // sel_cap is a power of two
+    const int M = K * C;
+    // the selection buffer past the top N is the rescans' staging area and
+    // is kept zero from here on (the sorts read it)
+    for (int i = tid; i < sort_n2; i += NT) { sh[i] = 0; sl[i] = 0; }
+
+    for (int t = t_first; t < t_stop; ++t) {
+        const int64_t row0 = d.row_begin + static_cast<int64_t>(t) * K;
+        const uint64_t* step_lists = p.lists + d.list_offset + (row0 - d.row_begin) * C;
+        const int forced = d.forced ? d.forced[t] : -1;
+        const bool eos_blocked = use_eos && (t + 1) < d.min_length;
+        __syncthreads();   // the previous step's state update is visible
+        if (step_done && !wait_step_rows(p, step_done, e * T + t, static_cast<unsigned int>(K))) return false;
+        for (int k = tid; k < K; k += NT) {
+            row_cnt[k] = __ldcg(p.list_count + row0 + k);
+            row_bound[k] = __ldcg(p.list_bound + row0 + k);
+            row_inv[k] = p.inv_pen[prev_len[k] + 1];
+            unsafe[k] = 0;
+        }
+        if (tid == 0) { sh_n = 0; sh_g = 0; sh_any = 0; }
+        __syncthreads();
+        const bool long0 = p.first_row_apart && t == 0;
+
+        // candidate keys of this thread's slots
+        uint64_t ch[kLmPer];
+        int ctok[kLmPer];
+        {
+            uint64_t raw_e[kLmPer];
+#pragma unroll
+            for (int u = 0; u < kLmPer; ++u) {
+                const int idx = tid + u * NT;
+                raw_e[u] = 0;
+                if (idx < M) {
+                    const int k = long0 ? 0 : idx / C;
+                    const int i = idx - k * C;
+                    if (i < row_cnt[k] && isfinite(prev_raw[k]) && !(use_eos && ended[k]))
+                        raw_e[u] = __ldcg(reinterpret_cast<const unsigned long long*>(step_lists) + idx);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kLmPer; ++u) {
+                const int idx = tid + u * NT;
+                uint64_t h = 0;
+                int tok = -1;
+                if (idx < M) {
+                    const int k = long0 ? 0 : idx / C;
+                    const int i = idx - k * C;
+                    const float pr = prev_raw[k];
+                    if (isfinite(pr)) {
+                        if (use_eos && ended[k]) {
+                            if (i == 0) {   // the ended parent's carry candidate
+                                const int len = prev_len[k] < 1 ? 1 : prev_len[k];
+                                h = cand_hi(__fdiv_rn(pr, p.pen[len]), pr);
+                                tok = d.eos;
+                            }
+                        } else if (raw_e[u] != 0) {
+                            const float raw = __fadd_rn(pr, list_lp(raw_e[u]));
+                            if (raw != -INFINITY) {
+                                h = cand_hi(__fmul_rn(raw, row_inv[k]), raw);
+                                tok = list_token(raw_e[u]);
+                            }
+                        }
+                    }
+                }
+                ch[u] = h;
+                ctok[u] = tok;
+            }
+        }
+        auto cand_lo_of = [&](int u) -> uint64_t {
+            const int idx = tid + u * NT;
+            const int k = long0 ? 0 : idx / C;
+            return cand_lo(k, ctok[u]);
+        };
+
+        // Radix select: the masked prefix (ph, pl) that the top-N keys reach
+        uint64_t ph = 0, pl = 0, mh = 0, ml = 0;   // prefix and mask over (hi, lo)
+        // the gathered keys are ranked by counting (one per thread), so
+        // at most NT of them; fewer when the radix passes can get there
+        const int gather_cap = NT < sel_cap ? NT : sel_cap;
+        const int gather_goal = N + 128 < gather_cap ? N + 128 : gather_cap;
+        int need = N;
+        int total = 0;
+        {
+            // real candidates and the range of their high words
+            unsigned long long mn = ~0ull, mx = 0ull;
+            int c = 0;
+#pragma unroll
+            for (int u = 0; u < kLmPer; ++u) {
+                if (ch[u]) {
+                    ++c;
+                    mn = min(mn, static_cast<unsigned long long>(ch[u]));
+                    mx = max(mx, static_cast<unsigned long long>(ch[u]));
+                }
+            }
+            c = warp_isum(c);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                mn = min(mn, __shfl_xor_sync(FULL, mn, o));
+                mx = max(mx, __shfl_xor_sync(FULL, mx, o));
+            }
+            if (lane == 0) {
+                atomicAdd(&sh_n, c);
+                sh_mm[2 * wid] = mn;
+                sh_mm[2 * wid + 1] = mx;
+            }
+            __syncthreads();
+            total = sh_n;
+            mn = ~0ull;
+            mx = 0ull;
+            for (int w = 0; w < NW; ++w) {
+                mn = min(mn, sh_mm[2 * w]);
+                mx = max(mx, sh_mm[2 * w + 1]);
+            }
+            __syncthreads();
+            if (total > N) {
+                // start at the highest bit where the high words differ; the
+                // bits above it are shared by every real candidate
+                int bit = (mn == mx) ? 0 : 63 - __clzll(static_cast<long long>(mn ^ mx));
+                int shift = bit >= 7 ? bit - 7 : 0;   // digit = bits [shift, shift + 8) of the 128-bit key
+                bool in_lo = false;
+                if (mn == mx) {   // every high word equal: decide on the low words
+                    mh = ~0ull;
+                    ph = mx;
+                    in_lo = true;
+                    shift = 56;
+                } else {
+                    mh = (shift + 8 >= 64) ? 0ull : ~((1ull << (shift + 8)) - 1ull);
+                    ph = mx & mh;
+                }
+                for (;;) {
+                    for (int i = tid; i < 256; i += NT) hist[i] = 0;
+                    __syncthreads();
+                    int* wh = hist;
+#pragma unroll
+                    for (int u = 0; u < kLmPer; ++u) {
+                        int bin = -1;
+                        if (ch[u] && (ch[u] & mh) == ph) {
+                            if (!in_lo) {
+                                bin = static_cast<int>((ch[u] >> shift) & 0xFFu);
+                            } else {
+                                const uint64_t l = cand_lo_of(u);
+                                if ((l & ml) == pl) bin = static_cast<int>((l >> shift) & 0xFFu);
+                            }
+                        }
+                        const unsigned same = __match_any_sync(FULL, bin);
+                        if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(wh + bin, __popc(same));
+                    }
+                    __syncthreads();
+                    if (wid == 0) {
+                        // digit d* with sum_{d > d*} < need <= sum_{d >= d*}
+                        int loc[8];
+                        int tot = 0;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            loc[j] = hist[lane * 8 + j];
+                            tot += loc[j];
+                        }
+                        int incl = tot;
+#pragma unroll
+                        for (int o = 1; o < 32; o <<= 1) {
+                            const int v = __shfl_down_sync(FULL, incl, o);
+                            if (lane + o < 32) incl += v;
+                        }
+                        const int excl = incl - tot;
+                        if (excl < need && need <= incl) {
+                            int run = excl;
+                            for (int j = 7; j >= 0; --j) {
+                                if (run + loc[j] >= need) {
+                                    sh_sel[0] = lane * 8 + j;
+                                    sh_sel[1] = run;
+                                    sh_sel[2] = loc[j];
+                                    break;
+                                }
+                                run += loc[j];
+                            }
+                        }
+                    }
+                    __syncthreads();
+                    const int digit = sh_sel[0];
+                    const int above = sh_sel[1];
+                    const int group = sh_sel[2];
+                    __syncthreads();   // sh_sel is rewritten by the next pass
+                    if (!in_lo) {
+                        ph |= static_cast<uint64_t>(digit) << shift;
+                        mh |= 0xFFull << shift;
+                    } else {
+                        pl |= static_cast<uint64_t>(digit) << shift;
+                        ml |= 0xFFull << shift;
+                    }
+                    need -= above;
+                    // keys above the group plus the group are few enough to rank
+                    if ((N - need) + group <= gather_goal) break;
+                    if (shift == 0) {
+                        if (in_lo) break;   // (unreachable: low words are unique)
+                        in_lo = true;
+                        shift = 56;
+                    } else {
+                        shift = shift >= 8 ? shift - 8 : 0;
+                    }
+                }
+            }
+        }
+        // gather every candidate whose masked key reaches the prefix (one
+        // shared atomic per warp and slot round)
+#pragma unroll
+        for (int u = 0; u < kLmPer; ++u) {
+            const uint64_t h = ch[u];
+            bool take = false;
+            if (h) {
+                take = total <= N || (h & mh) > ph;
+                if (!take && (h & mh) == ph) {
+                    const uint64_t l = cand_lo_of(u);
+                    take = ml == 0 || (l & ml) >= pl;
+                }
+            }
+            const unsigned bal = __ballot_sync(FULL, take);
+            int base = 0;
+            if (lane == 0 && bal) base = atomicAdd(&sh_g, __popc(bal));
+            base = __shfl_sync(FULL, base, 0);
+            if (take) {
+                const int pos = base + __popc(bal & ((1u << lane) - 1u));
+                sh[pos] = h;
+                sl[pos] = cand_lo_of(u);
+            }
+        }
+        __syncthreads();
+        {
+            // Rank of each gathered key = the gathered keys above it (keys
+            // are unique); those below N move to their slot. Every thread
+            // reads the same key at a time (shared-memory broadcast).
+            const int g = sh_g;
+            uint64_t mh_ = 0, ml_ = 0;
+            int rank = 0;
+            if (tid < g) {
+                mh_ = sh[tid];
+                ml_ = sl[tid];
+                int j = 0;
+                for (; j + 4 <= g; j += 4) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) rank += key2_less(mh_, ml_, sh[j + q], sl[j + q]) ? 1 : 0;
+                }
+                for (; j < g; ++j) rank += key2_less(mh_, ml_, sh[j], sl[j]) ? 1 : 0;
+            }
+            __syncthreads();
+            if (tid < g && rank < N) {
+                sh[rank] = mh_;
+                sl[rank] = ml_;
+            }
+            // keys past the first N are not part of the step (the buffer
+            // beyond them is the rescans' staging area, kept zero)
+            const int lim = g > N ? g : N;
+            for (int i = tid; i < lim; i += NT) {
+                if (i >= g && i < N) { sh[i] = 0; sl[i] = 0; }   // fewer than N candidates
+                if (i >= N) { sh[i] = 0; sl[i] = 0; }
+            }
+            __syncthreads();
+        }
+
+        // Exactness proof per truncated row (as in the selection merge): a
+        // dropped entry can beat the N-th key G only if the row's bound U does.
+        for (int k = tid; k < K; k += NT) {
+            const float pr = prev_raw[k];
+            if (!isfinite(pr) || (use_eos && ended[k])) continue;
+            const float bnd = row_bound[k];
+            if (!(bnd > -INFINITY)) continue;
+            const float raw_u = __fadd_rn(pr, bnd);
+            if (raw_u == -INFINITY) continue;
+            const float rank_u = __fmul_rn(raw_u, row_inv[k]);
+            bool safe = false;
+            if (sh[N - 1] != 0) {
+                const uint64_t uh = cand_hi(rank_u, raw_u);
+                const uint64_t gh = sh[N - 1];
+                safe = gh > uh || (gh == uh && cand_parent(sl[N - 1]) < k);
+            }
+            if (!safe) {
+                unsafe[k] = 1;
+                atomicOr(&sh_any, 1);
+            }
+        }
+        __syncthreads();
+        if (sh_any) {
+            // Rescan each unproven row from HBM: every candidate the scan
+            // dropped that beats the current N-th key G is staged behind the
+            // top N and merged in by one sort; a row with more winners than
+            // the staging room is swept again against the improved G.
+            const int room = sel_cap - N;
+            for (int k = 0; k < K; ++k) {
+                if (!unsafe[k]) continue;
+                if (tid == 0 && p.counters) atomicAdd(p.counters + 1, 1ull);
+                const float pr = prev_raw[k];
+                const float inv = row_inv[k];
+                const int64_t row = d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
+                const int cnt = row_cnt[k];
+                float m_lp = INFINITY;
+                int m_tok = -1;
+                if (cnt > 0) {
+                    const uint64_t last =
+                        __ldcg(reinterpret_cast<const unsigned long long*>(step_lists) + static_cast<int64_t>(k) * C + (cnt - 1));
+                    m_lp = list_lp(last);
+                    m_tok = list_token(last);
+                }
+                // The candidate of token v if the scan dropped it and it beats
+                // G = (gh, gl); 0 otherwise.
+                auto winner = [&](int v, float lp, float floor_lp, uint64_t gh, uint64_t gl, uint64_t& l) -> uint64_t {
+                    if (!(lp > floor_lp)) return 0;
+                    if (forced >= 0 && v != forced) return 0;
+                    if (d.banned && d.banned[v]) return 0;
+                    if (eos_blocked && v == d.eos) return 0;
+                    if (p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v]) return 0;
+                    if (!isfinite(lp)) return 0;
+                    const float lpc = __fadd_rn(lp, 0.0f);
+                    if (lpc > m_lp || (lpc == m_lp && v <= m_tok)) return 0;   // listed
+                    const float raw = __fadd_rn(pr, lp);
+                    if (raw == -INFINITY) return 0;
+                    const uint64_t h = cand_hi(__fmul_rn(raw, inv), raw);
+                    l = cand_lo(k, v);
+                    return key2_less(gh, gl, h, l) ? h : 0;
+                };
+                // lp floor for G: no lp at or below it forms a candidate above G
+                auto floor_of = [&](uint64_t gh) {
+                    float floor_lp = -INFINITY;
+                    if (gh != 0) {
+                        const float rg = cand_rank(gh);
+                        float f = __fsub_rn(__fdiv_rn(rg, inv), pr);
+                        f = __fsub_rn(f, (fabsf(f) + fabsf(pr) + 1.0f) * 1e-3f);
+                        const float rawf = __fadd_rn(pr, f);
+                        const float rankf = __fmul_rn(rawf, inv);
+                        if (isfinite(f) && isfinite(rawf) && isfinite(rankf) && cand_hi(rankf, rawf) < gh) floor_lp = f;
+                    }
+                    return floor_lp;
+                };
+                auto merge_stage = [&](int staged) {   // top N of (top N + staged); called by all threads
+                    if (staged <= 128 && N + staged <= 2 * NT) {
+                        // the new position of a top-N key is its index plus the
+                        // staged keys above it; that of a staged key is the
+                        // top-N keys above it (binary search) plus the staged
+                        // keys above it
+                        uint64_t kh[2], kl[2];
+                        int pos[2];
+#pragma unroll
+                        for (int r = 0; r < 2; ++r) {
+                            const int i = tid + r * NT;
+                            pos[r] = N;
+                            kh[r] = 0;
+                            kl[r] = 0;
+                            if (i < N + staged) {
+                                kh[r] = sh[i];
+                                kl[r] = sl[i];
+                                int ps = 0;
+                                if (i < N) {
+                                    ps = i;
+                                } else {
+                                    int lo = 0, hi = N;
+                                    while (lo < hi) {
+                                        const int mid = (lo + hi) >> 1;
+                                        if (key2_less(kh[r], kl[r], sh[mid], sl[mid])) lo = mid + 1; else hi = mid;
+                                    }
+                                    ps = lo;
+                                }
+                                for (int q = N; q < N + staged; ++q) ps += key2_less(kh[r], kl[r], sh[q], sl[q]) ? 1 : 0;
+                                pos[r] = ps;
+                            }
+                        }
+                        __syncthreads();
+#pragma unroll
+                        for (int r = 0; r < 2; ++r) {
+                            if (pos[r] < N && kh[r] != 0) {
+                                sh[pos[r]] = kh[r];
+                                sl[pos[r]] = kl[r];
+                            }
+                        }
+                        __syncthreads();
+                        for (int i = N + tid; i < N + staged; i += NT) { sh[i] = 0; sl[i] = 0; }
+                        __syncthreads();
+                        return;
+                    }
+                    int n2 = 2;
+                    while (n2 < N + staged) n2 <<= 1;
+                    lm_sort<NT>(sh, sl, n2);
+                    for (int i = N + tid; i < n2; i += NT) { sh[i] = 0; sl[i] = 0; }
+                    __syncthreads();
+                };
+                // While the step has fewer than N candidates (G empty: step 0 of
+                // a decode whose one live row has a short list), every entry of
+                // the row would win; only entries at or above the row's N-th
+                // largest allowed log-prob can be among the top N, so the floor
+                // is put just below that value, found by a radix select over the
+                // row (8 bits per pass).
+                float nth_floor = -INFINITY;
+                if (sh[N - 1] == 0) {
+                    uint32_t prefix = 0, mask = 0;
+                    int need_r = N;
+                    bool enough = true;
+                    for (int shift = 24; shift >= 0; shift -= 8) {
+                        for (int i = tid; i < 256; i += NT) hist[i] = 0;
+                        __syncthreads();
+                        for (int v = tid; v < V; v += NT) {
+                            const float lp = lp_at(p, row + v);
+                            int bin = -1;
+                            if (isfinite(lp) && !(forced >= 0 && v != forced) && !(d.banned && d.banned[v]) &&
+                                !(eos_blocked && v == d.eos) &&
+                                !(p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v])) {
+                                const uint32_t u = ord_f32(lp);
+                                if ((u & mask) == prefix) bin = static_cast<int>((u >> shift) & 0xFFu);
+                            }
+                            const unsigned act = __activemask();
+                            const unsigned same = __match_any_sync(act, bin);
+                            if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(hist + bin, __popc(same));
+                        }
+                        __syncthreads();
+                        if (wid == 0) {
+                            int loc[8];
+                            int tot = 0;
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                loc[j] = hist[lane * 8 + j];
+                                tot += loc[j];
+                            }
+                            int incl = tot;
+#pragma unroll
+                            for (int o = 1; o < 32; o <<= 1) {
+                                const int v = __shfl_down_sync(FULL, incl, o);
+                                if (lane + o < 32) incl += v;
+                            }
+                            const int excl = incl - tot;
+                            if (lane == 0 && incl < need_r) sh_sel[0] = -1;   // fewer than N allowed entries
+                            if (excl < need_r && need_r <= incl) {
+                                int run = excl;
+                                for (int j = 7; j >= 0; --j) {
+                                    if (run + loc[j] >= need_r) {
+                                        sh_sel[0] = lane * 8 + j;
+                                        sh_sel[1] = run;
+                                        break;
+                                    }
+                                    run += loc[j];
+                                }
+                            }
+                        }
+                        __syncthreads();
+                        const int digit = sh_sel[0];
+                        const int above = sh_sel[1];
+                        __syncthreads();
+                        if (digit < 0) { enough = false; break; }
+                        prefix |= static_cast<uint32_t>(digit) << shift;
+                        mask |= 0xFFu << shift;
+                        need_r -= above;
+                    }
+                    if (enough) nth_floor = nextafterf(unord_f32(prefix), -INFINITY);
+                }
+                // one sweep against the G of the row's start, no barrier inside
+                {
+                    const uint64_t gh = sh[N - 1], gl = sl[N - 1];
+                    const float floor_lp = gh == 0 ? nth_floor : floor_of(gh);
+                    if (tid == 0) { sh_n = 0; sh_over = 0; }
+                    __syncthreads();
+                    auto stage = [&](int v, float lp) {
+                        uint64_t l = 0;
+                        const uint64_t h = winner(v, lp, floor_lp, gh, gl, l);
+                        if (!h) return;
+                        const int pos = atomicAdd(&sh_n, 1);
+                        if (pos < room) {
+                            sh[N + pos] = h;
+                            sl[N + pos] = l;
+                        } else {
+                            sh_over = 1;
+                        }
+                    };
+                    if (!p.x16) {
+                        // fp32 rows: scalar head up to a 16-byte boundary, then
+                        // four float4 loads per thread in flight; a vector whose
+                        // largest value is at or below the floor is skipped
+                        const float* rp = p.x + row;
+                        const int head = min(V, static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(rp) & 15u)) & 15u) >> 2));
+                        if (tid < head) stage(tid, rp[tid]);
+                        const float4* body = reinterpret_cast<const float4*>(rp + head);
+                        const int nv = (V - head) >> 2;
+                        for (int base = 0; base < nv; base += 4 * NT) {
+                            float4 q[4];
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) {
+                                const int i = base + r * NT + tid;
+                                q[r] = i < nv ? __ldg(body + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                            }
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) {
+                                const float m4 = fmaxf(fmaxf(q[r].x, q[r].y), fmaxf(q[r].z, q[r].w));
+                                if (!(m4 > floor_lp)) continue;   // (NaN is not finite: never a candidate)
+                                const int v0 = head + 4 * (base + r * NT + tid);
+                                stage(v0, q[r].x);
+                                stage(v0 + 1, q[r].y);
+                                stage(v0 + 2, q[r].z);
+                                stage(v0 + 3, q[r].w);
+                            }
+                        }
+                        const int t0 = head + 4 * nv;
+                        if (t0 + tid < V) stage(t0 + tid, rp[t0 + tid]);
+                    } else {
+                        for (int base = 0; base < V; base += 16 * NT) {
+                            float lv[16];
+#pragma unroll
+                            for (int r = 0; r < 16; ++r) {
+                                const int v = base + r * NT + tid;
+                                lv[r] = v < V ? lp_at(p, row + v) : -INFINITY;
+                            }
+#pragma unroll
+                            for (int r = 0; r < 16; ++r) {
+                                const int v = base + r * NT + tid;
+                                if (v < V) stage(v, lv[r]);
+                            }
+                        }
+                    }
+                    __syncthreads();
+                }
+                const int staged = sh_n;
+                const int over = sh_over;
+                __syncthreads();
+                if (!over) {
+                    if (staged > 0) merge_stage(staged);
+                    continue;
+                }
+                // More winners than the staging room: drop the stage and sweep
+                // the row again in chunks of at most `room` values, merging the
+                // stage after each chunk (G only improves; each value is seen
+                // once, so nothing is staged twice).
+                for (int i = N + tid; i < sort_n2; i += NT) { sh[i] = 0; sl[i] = 0; }
+                __syncthreads();
+                const int chunk = (room / NT) * NT;
+                for (int base = 0; base < V; base += chunk) {
+                    const uint64_t gh = sh[N - 1], gl = sl[N - 1];
+                    const float floor_lp = floor_of(gh);
+                    if (tid == 0) sh_n = 0;
+                    __syncthreads();
+                    for (int v = base + tid; v < base + chunk && v < V; v += NT) {
+                        uint64_t l = 0;
+                        const uint64_t h = winner(v, lp_at(p, row + v), floor_lp, gh, gl, l);
+                        if (!h) continue;
+                        const int pos = atomicAdd(&sh_n, 1);
+                        sh[N + pos] = h;
+                        sl[N + pos] = l;
+                    }
+                    __syncthreads();
+                    const int st = sh_n;
+                    __syncthreads();
+                    if (st > 0) merge_stage(st);
+                }
+            }
+        }
+
+        // Outputs of step t and the beam state update.
+        const bool want_pool = p.pool_scores != nullptr;
+        for (int j = tid; j < N; j += NT) {
+            const uint64_t h = sh[j];
+            const uint64_t l = sl[j];
+            int parent = -1, token = -1, len = 0, flp = 0;
+            float rank = -INFINITY, raw = -INFINITY;
+            if (h != 0) {
+                parent = cand_parent(l);
+                token = cand_token(l);
+                rank = cand_rank(h);
+                raw = cand_raw(h);
+                const bool carry = use_eos && ended[parent];
+                len = carry ? (prev_len[parent] < 1 ? 1 : prev_len[parent]) : prev_len[parent] + 1;
+                flp = carry ? 0 : 1;
+            }
+            if (want_pool && j < P) {
+                const int64_t o = d.pool_offset + static_cast<int64_t>(t) * d.pool_t_stride + j;
+                p.pool_parents[o] = parent;
+                p.pool_tokens[o] = token;
+                p.pool_lengths[o] = len;
+                p.pool_raw_scores[o] = raw;
+                p.pool_scores[o] = rank;
+                if (p.pool_from_logprob) p.pool_from_logprob[o] = static_cast<uint8_t>(flp);
+            }
+            if (j < K) {
+                const int64_t o = d.sel_offset + static_cast<int64_t>(t) * d.sel_t_stride + j;
+                p.parents[o] = parent;
+                p.tokens[o] = token;
+                p.lengths[o] = len;
+                if (p.raw_scores) p.raw_scores[o] = raw;
+                if (p.scores) p.scores[o] = rank;
+                p.from_logprob[o] = static_cast<uint8_t>(flp);
+                next_raw[j] = raw;
+                next_len[j] = len;
+                ended_next[j] = (parent >= 0) ? ((ended[parent] != 0) || (use_eos && token == d.eos)) : 0;
+            }
+        }
+        __syncthreads();
+        for (int k = tid; k < K; k += NT) {
+            prev_raw[k] = next_raw[k];
+            prev_len[k] = next_len[k];
+            ended[k] = ended_next[k];
+        }
+    }
+    __syncthreads();
+    if (t_stop < T) {   // more steps follow in a later launch: keep the state
+        if (state) {
+            for (int k = tid; k < K; k += NT) {
+                state[k] = prev_raw[k];
+                state[seq_K + k] = __int_as_float(prev_len[k]);
+                state[2 * seq_K + k] = __int_as_float(ended[k]);
+                state[3 * seq_K + k] = __int_as_float(0);
+            }
+        }
+        return true;
+    }
+    // Finalisation (src/differentiable_beam.cpp:1661-1667): a division.
+    for (int k = tid; k < K; k += NT) {
+        const int len = prev_len[k] < 1 ? 1 : prev_len[k];
+        const int64_t o = d.final_offset + k;
+        if (p.final_raw_scores) p.final_raw_scores[o] = prev_raw[k];
+        if (p.final_scores) p.final_scores[o] = __fdiv_rn(prev_raw[k], p.pen[len]);
+    }
+    return true;
+}
+
+template <int NT, int PER>
+__global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int seq_K, int sel_cap) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int e = blockIdx.x;
+    float* state = p.merge_state ? p.merge_state + static_cast<int64_t>(e) * 4 * seq_K : nullptr;
+    list_merge_body<NT, PER>(p, e, p.t_begin > 0 ? p.t_begin : 0, p.t_end, state, seq_K, sel_cap, smem, nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// 3. Fused decode of a uniform batch without sequence constraints: ONE
+//    cooperative launch (every CTA resident at once) in which CTAs
+//    [0, merge_ctas) run the step merge and all others run the row scan.
+//    The scan claims rows step by step across the examples (step-major) and
+//    counts each finished row in step_done[e * T + t]; a merge CTA starts
+//    step t of its example once that counter reaches K (a bounded wait,
+//    which reports a timeout instead of hanging), so the T dependent merge
+//    steps run while later steps are still being scanned and only the last
+//    step's merge follows the scan. With fewer merge CTAs than examples a
+//    CTA merges its examples one step at a time in turn, their beams kept in
+//    merge_state. Merge CTAs write no output when the validation kernel
+//    (queued before this launch) flagged any example; the host then
+//    reports the error.
+// ---------------------------------------------------------------------------
+template <int PER>
+__global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodeParams p, int capw, int seq_K,
+                                                                      int sel_cap, int merge_ctas,
+                                                                      unsigned int* step_done) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    if (static_cast<int>(blockIdx.x) >= merge_ctas) {
+        row_scan_body<false>(p, capw, 1, smem_raw, step_done);
+        return;
+    }
+    __shared__ int sh_bad;
+    if (threadIdx.x == 0) {
+        int bad = 0;
+        if (p.validate_inputs)
+            for (int b = 0; b < p.B; ++b) bad |= p.status[b];
+        sh_bad = bad;
+    }
+    __syncthreads();
+    if (sh_bad) return;
+    const int T = p.desc[0].T;
+    if (merge_ctas >= p.B) {
+        list_merge_body<kFusedThreads, PER>(p, blockIdx.x, 0, T, nullptr, seq_K, sel_cap, smem_raw, step_done);
+        return;
+    }
+    for (int t = 0; t < T; ++t) {
+        for (int e = blockIdx.x; e < p.B; e += merge_ctas) {
+            float* state = p.merge_state + static_cast<int64_t>(e) * 4 * seq_K;
+            if (!list_merge_body<kFusedThreads, PER>(p, e, t, t + 1, state, seq_K, sel_cap, smem_raw, step_done))
+                return;
+        }
     }
 }
 
@@ -3009,6 +3800,15 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
     return counted(cudaGetLastError());
 }
 
+// DBS_LIST_MERGE=0 turns the compact merge off (read once, for measurements).
+static bool list_merge_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("DBS_LIST_MERGE");
+        return !(v && std::atoi(v) == 0);
+    }();
+    return on;
+}
+
 static size_t merge_rank_smem(int ring, int max_K, int max_C, int max_N, int tab_n) {
     size_t b = static_cast<size_t>(2) * tab_n * sizeof(float);              // length-penalty tables
     b += static_cast<size_t>(ring) * max_K * max_C * sizeof(uint64_t);      // ring lists
@@ -3049,6 +3849,20 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
         }
     }
     const int M = max_K * max_C;
+    if (!need_sequences && M <= kListMergeMaxCandidates && max_N <= 1024 && list_merge_enabled()) {
+        // compact merge: candidate keys in registers, radix select, one sort
+        constexpr int nt = kListMergeThreads;
+        const int sel_cap = list_merge_sel_cap(max_N, nt);
+        const size_t smem = list_merge_smem(nt, sel_cap, max_K);
+        const bool small = M <= nt * 4;
+        const void* fn = small ? reinterpret_cast<const void*>(list_merge_kernel<nt, 4>)
+                               : reinterpret_cast<const void*>(list_merge_kernel<nt, 8>);
+        cudaError_t err = ensure_dynamic_smem(fn, smem);
+        if (err != cudaSuccess) return err;
+        if (small) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
+        else list_merge_kernel<nt, 8><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
+        return counted(cudaGetLastError());
+    }
     int cand_cap = M;
     if (cand_cap < max_N + 2048) cand_cap = max_N + 2048;
     const int sel_cap = max_N + 2048;
@@ -3085,6 +3899,33 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     if (runs) step_merge_kernel<true><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2, seq_smem);
     else step_merge_kernel<false><<<p.B, threads, smem, stream>>>(p, cand_cap, max_T, max_K, sel_cap, bloom_log2, seq_smem);
     return counted(cudaGetLastError());
+}
+
+cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int max_N, int merge_ctas,
+                                unsigned int* step_done, int num_sms, cudaStream_t stream) {
+    const int M = max_K * max_C;
+    if (M > 8 * kFusedThreads || max_N > 1024 || merge_ctas < 1 || max_C > 64) return cudaErrorNotSupported;
+    const int capw = row_scan_capw(max_C);
+    const int sel_cap = list_merge_sel_cap(max_N, kFusedThreads);
+    size_t smem = static_cast<size_t>(kFusedThreads / 32) * row_scan_warp_bytes(capw, false);
+    const size_t msmem = list_merge_smem(kFusedThreads, sel_cap, max_K);
+    if (msmem > smem) smem = msmem;
+    const bool small = M <= kFusedThreads * 4;
+    const void* fn = small ? reinterpret_cast<const void*>(fused_decode_kernel<4>)
+                           : reinterpret_cast<const void*>(fused_decode_kernel<8>);
+    cudaError_t err = ensure_dynamic_smem(fn, smem);
+    if (err != cudaSuccess) return err;
+    int per_sm = 0;
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kFusedThreads, smem);
+    if (err != cudaSuccess) return err;
+    const int grid = per_sm * num_sms;
+    if (per_sm < 1 || grid <= merge_ctas) return cudaErrorNotSupported;
+    DecodeParams pp = p;
+    int a_capw = capw, a_seq = max_K, a_sel = sel_cap, a_m = merge_ctas;
+    unsigned int* a_done = step_done;
+    void* args[] = {&pp, &a_capw, &a_seq, &a_sel, &a_m, &a_done};
+    err = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kFusedThreads), args, smem, stream);
+    return counted(err);
 }
 
 cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_P, cudaStream_t stream) {

@@ -366,9 +366,6 @@ struct Lease {
 // merge (the dense gradient zero fill).
 struct Helper {
     cudaStream_t side = nullptr;
-    cudaStream_t side2 = nullptr;   // second row-scan stream of a pipelined batch decode
-    cudaStream_t mside = nullptr;   // merges of a pipelined batch decode, at the highest priority
-    cudaEvent_t merged = nullptr;
     cudaEvent_t before = nullptr;
     cudaEvent_t after = nullptr;
     std::vector<cudaEvent_t> seg;   // end of each row-scan segment of a pipelined decode
@@ -383,12 +380,6 @@ Helper& helper_locked() {
     Helper& h = g_helpers[dev];
     if (!h.side) {
         check_cuda(cudaStreamCreateWithFlags(&h.side, cudaStreamNonBlocking), "cudaStreamCreate(helper)");
-        check_cuda(cudaStreamCreateWithFlags(&h.side2, cudaStreamNonBlocking), "cudaStreamCreate(helper)");
-        // a merge CTA that waits for room is placed before the scans' CTAs
-        int lo = 0, hi = 0;
-        check_cuda(cudaDeviceGetStreamPriorityRange(&lo, &hi), "cudaDeviceGetStreamPriorityRange");
-        check_cuda(cudaStreamCreateWithPriority(&h.mside, cudaStreamNonBlocking, hi), "cudaStreamCreate(helper)");
-        check_cuda(cudaEventCreateWithFlags(&h.merged, cudaEventDisableTiming), "cudaEventCreate");
         check_cuda(cudaEventCreateWithFlags(&h.before, cudaEventDisableTiming), "cudaEventCreate");
         check_cuda(cudaEventCreateWithFlags(&h.after, cudaEventDisableTiming), "cudaEventCreate");
     }
@@ -466,28 +457,23 @@ int list_capacity(const Options& opt, int K, bool pool, bool dynamic) {
 // 64K rows (measured with T = 64: K = 32, 256 examples 33.5 -> 22.2 ms and
 // 32 examples 5.8 -> 4.9 ms; K = 64, 128 examples 25.8 -> 22.5 ms; but
 // K = 16 with 32 examples, 32K rows, 2.73 -> 2.88 ms).
-// Pipelined batch decode (see decode()): segments per call, SMs kept free
-// for the merges while the scans run (-1: by batch size), and a switch
-// (off by default); DBS_BATCH_PIPELINE=1, DBS_PIPE_SEGMENTS=<n> and
-// DBS_PIPE_RESERVE=<SMs> override them (read once, for measurements).
-struct PipeTuning {
-    bool enabled = false;
-    int segments = 8;
-    int reserve = -1;
-};
-const PipeTuning& pipe_tuning() {
-    static const PipeTuning t = [] {
-        PipeTuning v;
-        if (const char* e = std::getenv("DBS_BATCH_PIPELINE")) v.enabled = std::atoi(e) != 0;
-        if (const char* e = std::getenv("DBS_PIPE_SEGMENTS")) v.segments = std::max(2, std::atoi(e));
-        if (const char* e = std::getenv("DBS_PIPE_RESERVE")) v.reserve = std::max(0, std::atoi(e));
-        return v;
+constexpr int kFusedMaxExamples = 64;
+// Fused decode: DBS_FUSED=0 turns it off; DBS_FUSED_MERGE_CTAS=<n> sets how
+// many CTAs merge (default 32; fewer examples get one CTA each).
+bool fused_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("DBS_FUSED");
+        return !(v && std::atoi(v) == 0);
     }();
-    return t;
+    return on;
 }
-// CTA size of the pipelined merges: two fit an SM beside nothing else.
-constexpr int kPipeMergeThreads = 256;
-
+int fused_merge_ctas() {
+    static const int n = [] {
+        const char* v = std::getenv("DBS_FUSED_MERGE_CTAS");
+        return v ? std::max(1, std::atoi(v)) : 32;
+    }();
+    return n;
+}
 constexpr int kShortListEntries = 64;
 constexpr int kShortListMinExamples = 32;
 constexpr int64_t kShortListMinRows = 65536;
@@ -517,6 +503,30 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         short_lists = cut && nrows >= kShortListMinRows && static_cast<int64_t>(kmax) * kShortListEntries > 256;
     }
 
+    // Fused decode: a uniform batch of 2 to kFusedMaxExamples examples without
+    // sequence constraints whose merge is the selection merge runs its row
+    // scan and its step merge in one cooperative launch (dbs_kernels.cu,
+    // fused_decode_kernel), with row lists of at most 64 entries; the merge
+    // lists step 0's one live row by a rescan, so no step-0 launch runs.
+    // The merge CTAs hold whole SMs, and the row scan's rate is set by the
+    // SMs it runs on (it is issue-bound there), so larger batches, whose
+    // merges cost less than a tenth of their scan, keep separate launches
+    // (measured with T = 64, K = 32, V = 50257: 32 examples 5.07 -> 3.81 ms,
+    // 64 examples 7.28 -> 6.87 ms, but 128 examples 11.8 -> 13.0 ms).
+    bool fused = false;
+    if (B >= 2 && B <= kFusedMaxExamples && !dynamic && !ext_lists && ctl.scan && ctl.merge && ctl.t_begin <= 0 && ctl.t_end >= (1 << 30) &&
+        !ctl.merge_state && !ctl.row_allow && !ctl.x16 && ctl.scan_begin <= 0 && ctl.scan_end < 0 &&
+        !(ctl.zero_fill && ctl.zero_fill_count > 0) && fused_enabled()) {
+        bool uni = true;
+        for (const ExampleSpec& e : ex) uni = uni && e.T == ex[0].T && e.K == ex[0].K;
+        const int K0 = ex[0].K;
+        const int N0 = pool ? pool_size(K0, opt.relaxed_pool_multiplier) : K0;
+        const int C0 = std::min(list_capacity_for(N0, K0, false), kShortListEntries);
+        const int64_t M0 = static_cast<int64_t>(K0) * C0;
+        fused = uni && ex[0].T >= 2 && M0 > 256 && M0 <= dbs_dev::kListMergeMaxCandidates && N0 <= 1024;
+    }
+    if (fused) short_lists = false;
+
     std::vector<dbs_dev::ExampleDesc> desc(B);
     std::vector<int64_t> row_prefix(B + 1, 0);
     int max_T = 0, max_K = 0, max_C = 0, max_N = 0, max_P = 0, max_C0 = 0;
@@ -526,7 +536,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         const int P = layout.P[b];
         const int N = pool ? P : e.K;
         int C = list_capacity_for(N, e.K, dynamic);
-        if (short_lists && C > kShortListEntries) C = kShortListEntries;
+        if ((short_lists || fused) && C > kShortListEntries) C = kShortListEntries;
         if (e.K > 1024) throw LengthError("beam_size above 1024 is not supported by the device decoder");
         dbs_dev::ExampleDesc& d = desc[b];
         d.x_offset = e.x_offset;
@@ -591,31 +601,6 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         if (n_seg < 2) n_seg = 0;
     }
     const bool pipeline = n_seg > 0;
-    // Many examples of one shape whose merge is the selection merge: the row
-    // scan runs step-major (claims ordered by step, then example, then beam)
-    // in segments of steps, alternating between two helper streams so that
-    // consecutive segments overlap instead of each draining the GPU; the
-    // merge of segment i (every example, one CTA each) runs on `stream` as
-    // soon as scan i is done, beside the scans of later segments, on SMs the
-    // scans leave free. Only the last segment's merge is not hidden.
-    bool uniform = true;
-    for (const ExampleSpec& e : ex) uniform = uniform && e.T == ex[0].T && e.K == ex[0].K;
-    std::vector<int> bp_bound;   // segment boundaries in steps
-    int bp_reserve = 0;
-    if (B >= 2 && uniform && ctl.scan && ctl.merge && !ext_lists && scan_begin == 0 && scan_end == rows &&
-        ctl.t_begin <= 0 && ctl.t_end >= max_T && !ctl.merge_state && !ctl.row_allow && max_T >= 16 &&
-        (dynamic || static_cast<int64_t>(max_K) * max_C > 256) && pipe_tuning().enabled) {
-        const int want = pipe_tuning().segments;
-        const int sz = std::max(2, (max_T + want - 1) / want);
-        for (int t = 0; t < max_T; t += sz) bp_bound.push_back(t);
-        bp_bound.push_back(max_T);
-        if (bp_bound.size() < 3) bp_bound.clear();   // fewer than two segments
-        // two 256-thread merge CTAs per reserved SM
-        bp_reserve = pipe_tuning().reserve >= 0 ? pipe_tuning().reserve : std::min(24, std::max(8, (B + 1) / 2));
-        bp_reserve = std::min(bp_reserve, device_sm_count() / 4);
-    }
-    const bool batch_pipe = !bp_bound.empty();
-    const int bp_n = batch_pipe ? static_cast<int>(bp_bound.size()) - 1 : 0;
     size_t hdr = 0;
     hdr += bytes_of<dbs_dev::ExampleDesc>(B);
     hdr += bytes_of<int64_t>(B + 1);
@@ -623,11 +608,6 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     hdr += bytes_of<int32_t>(B);
     hdr += bytes_of<unsigned long long>(4);
     if (pipeline) hdr += bytes_of<unsigned long long>(n_seg);   // first row of each scan segment
-    // claim counter of each scan launch (the segments and the step-0 lists), speculation seeds
-    if (batch_pipe) {
-        hdr += bytes_of<unsigned long long>(bp_n + 1) + bytes_of<unsigned long long>(dbs_dev::kSpecSlots) +
-               bytes_of<unsigned int>(bp_n);   // + a worker flag per segment
-    }
     if (ext_lists && (!ctl.list_count || !ctl.list_bound)) throw InvalidArgument("row lists need counts and bounds");
     if (!ext_lists && !(ctl.scan && ctl.merge)) throw InvalidArgument("a split decode needs caller row lists");
     size_t ws = hdr;
@@ -637,7 +617,8 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         ws += bytes_of<float>(static_cast<size_t>(rows));
     }
     if (dynamic && !ctl.seq_scratch) ws += bytes_of<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
-    if (pipeline || batch_pipe) ws += bytes_of<float>(static_cast<size_t>(4) * max_K * B);   // merge state between segments
+    if (pipeline || fused) ws += bytes_of<float>(static_cast<size_t>(4) * max_K * B);   // merge state between segments
+    if (fused) ws += bytes_of<unsigned int>(static_cast<size_t>(B) * max_T);   // rows listed per (example, step)
     trace.mark("prepared");
     Lease lease(ws, hdr, stream);
     trace.mark("slot");
@@ -667,19 +648,6 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         for (int i = 0; i < n_seg; ++i)
             h_seeds[i] = static_cast<unsigned long long>(i) * seg_steps * desc[0].K;
     }
-    unsigned long long* d_claims = nullptr;
-    unsigned long long* d_spec = nullptr;
-    unsigned int* d_flags = nullptr;
-    if (batch_pipe) {
-        d_claims = cv.take<unsigned long long>(bp_n + 1);
-        unsigned long long* hc = hv.take<unsigned long long>(bp_n + 1);
-        for (int i = 0; i < bp_n; ++i) hc[i] = static_cast<unsigned long long>(bp_bound[i]) * B * max_K;
-        hc[bp_n] = 0;   // the step-0 lists: claim i is example i
-        d_spec = cv.take<unsigned long long>(dbs_dev::kSpecSlots);
-        std::memset(hv.take<unsigned long long>(dbs_dev::kSpecSlots), 0, sizeof(unsigned long long) * dbs_dev::kSpecSlots);
-        d_flags = cv.take<unsigned int>(bp_n);
-        std::memset(hv.take<unsigned int>(bp_n), 0, sizeof(unsigned int) * bp_n);
-    }
     check_cuda(cudaMemcpyAsync(lease.s->dev, lease.s->pinned, cv.off, cudaMemcpyHostToDevice, stream),
                "upload decode metadata");
     if (ext_lists) {
@@ -694,7 +662,8 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     p.seq_scratch = !dynamic ? nullptr
                   : ctl.seq_scratch ? ctl.seq_scratch
                                     : cv.take<int32_t>(static_cast<size_t>(B) * 3 * max_K * max_T);
-    float* d_state = (pipeline || batch_pipe) ? cv.take<float>(static_cast<size_t>(4) * max_K * B) : nullptr;
+    float* d_state = (pipeline || fused) ? cv.take<float>(static_cast<size_t>(4) * max_K * B) : nullptr;
+    unsigned int* d_done = fused ? cv.take<unsigned int>(static_cast<size_t>(B) * max_T) : nullptr;
     p.t_begin = ctl.t_begin;
     p.t_end = ctl.t_end;
     p.merge_state = ctl.merge_state;
@@ -830,95 +799,46 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         }
         trace.mark("merge queued");
         check_cuda(cudaStreamWaitEvent(stream, seg_done[n_seg], 0), "cudaStreamWaitEvent");
-    } else if (batch_pipe) {
-        // ev[i]: scan segment i listed; ev[bp_n]: the step-0 lists; ev[bp_n + 1]:
-        // the helper streams' part of the call is over
-        std::vector<cudaEvent_t> ev(bp_n + 2, nullptr);
-        struct EventsGuard {
-            std::vector<cudaEvent_t>& v;
-            ~EventsGuard() {
-                for (cudaEvent_t e : v)
-                    if (e) cudaEventDestroy(e);   // released once the queued waits are done
-            }
-        } events_guard{ev};
-        for (cudaEvent_t& e : ev) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
-        const int sms = device_sm_count();
+    } else if (fused) {
+        // merge CTAs: one per example up to kFusedMergeCtas, else examples in turn
+        const int merge_ctas = std::min(B, fused_merge_ctas());
+        check_cuda(cudaMemsetAsync(d_done, 0, sizeof(unsigned int) * static_cast<size_t>(B) * max_T, stream),
+                   "zero step counters");
+        dbs_dev::DecodeParams fp = p;
+        fp.step_major_bk = static_cast<int64_t>(B) * max_K;
+        fp.step_major_tk = static_cast<int64_t>(max_T) * max_K;
+        fp.merge_state = d_state;
+        cudaError_t ferr;
         {
-            std::lock_guard<std::mutex> lock(g_helper_mu);
-            Helper& hp = helper_locked();
-            check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
-            check_cuda(cudaStreamWaitEvent(hp.side, hp.before, 0), "cudaStreamWaitEvent");
-            check_cuda(cudaStreamWaitEvent(hp.side2, hp.before, 0), "cudaStreamWaitEvent");
+            ProfileScope ps(kRowScan, stream);   // the whole fused launch
+            ferr = dbs_dev::launch_fused_decode(fp, max_K, max_C, max_N, merge_ctas, d_done, device_sm_count(), stream);
+        }
+        if (ferr == cudaErrorNotSupported) {
+            cudaGetLastError();
+            // separate launches on the same lists (the merge's rescans list step 0)
             {
-                ProfileScope ps(kRowScan, hp.side);   // one pair around all of the call's scans
-                if (short_lists) {
-                    // the live step-0 row of every example, with its long list
-                    dbs_dev::DecodeParams s0 = p;
-                    s0.first_rows_only = 1;
-                    s0.claim = d_claims + bp_n;
-                    check_cuda(dbs_dev::launch_row_scan(s0, max_C0, sms, hp.side2, B), "row scan kernel (step 0)");
-                }
-                check_cuda(cudaEventRecord(ev[bp_n], hp.side2), "cudaEventRecord");
-                dbs_dev::DecodeParams sp = p;
-                sp.step_major_bk = static_cast<int64_t>(B) * max_K;
-                sp.step_major_tk = static_cast<int64_t>(max_T) * max_K;
-                sp.spec_seed = d_spec;
-                sp.reserve_sms = bp_reserve;
-                for (int i = 0; i < bp_n; ++i) {
-                    cudaStream_t ss = (i & 1) ? hp.side2 : hp.side;
-                    sp.claim = d_claims + i;
-                    sp.worker_flag = d_flags + i;
-                    sp.total_rows = static_cast<int64_t>(bp_bound[i + 1]) * B * max_K;   // claim limit
-                    const int64_t seg_rows = static_cast<int64_t>(bp_bound[i + 1] - bp_bound[i]) * B * max_K;
-                    check_cuda(dbs_dev::launch_row_scan(sp, max_C, sms, ss, seg_rows, 1), "row scan kernel");
-                    check_cuda(cudaEventRecord(ev[i], ss), "cudaEventRecord");
-                }
-                check_cuda(cudaEventRecord(hp.after, hp.side2), "cudaEventRecord");
-                check_cuda(cudaStreamWaitEvent(hp.side, hp.after, 0), "cudaStreamWaitEvent");
+                ProfileScope ps(kRowScan, stream);
+                check_cuda(dbs_dev::launch_row_scan(p, max_C, device_sm_count(), stream, rows), "row scan kernel");
             }
-            if (ctl.zero_fill && ctl.zero_fill_count > 0) {
-                ProfileScope ps(kFillZero, hp.side);
-                check_cuda(dbs_dev::launch_fill_zero_bulk(ctl.zero_fill, ctl.zero_fill_count, sms, hp.side),
-                           "zero fill kernel");
+            if (validate) {
+                check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
+                for (int b = 0; b < B; ++b)
+                    if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
             }
-            check_cuda(cudaEventRecord(ev[bp_n + 1], hp.side), "cudaEventRecord");
-        }
-        trace.mark("row scan queued");
-        if (validate) {
-            check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
-            trace.mark("validate synced");
-            for (int b = 0; b < B; ++b) {
-                if (h_status[b]) {
-                    // the workspace is released on `stream`: it must cover the scans
-                    check_cuda(cudaStreamWaitEvent(stream, ev[bp_n + 1], 0), "cudaStreamWaitEvent");
-                    throw InvalidArgument("log_probs contains NaN or +Inf");
-                }
+            ProfileScope ps(kStepMerge, stream);
+            check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream), "step merge kernel");
+        } else {
+            check_cuda(ferr, "fused decode kernel");
+            trace.mark("fused queued");
+            if (validate) {
+                // the fused launch writes no output when validation flagged an
+                // example; the call reports the error
+                check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
+                trace.mark("validate synced");
+                for (int b = 0; b < B; ++b)
+                    if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
             }
         }
-        {
-            // the merges run on the highest-priority helper stream: when an SM
-            // frees up, a waiting merge CTA is placed before a scan CTA
-            std::lock_guard<std::mutex> lock(g_helper_mu);
-            Helper& hp = helper_locked();
-            check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
-            check_cuda(cudaStreamWaitEvent(hp.mside, hp.before, 0), "cudaStreamWaitEvent");
-            for (int i = 0; i < bp_n; ++i) {
-                check_cuda(cudaStreamWaitEvent(hp.mside, ev[i], 0), "cudaStreamWaitEvent");
-                if (i == 0) check_cuda(cudaStreamWaitEvent(hp.mside, ev[bp_n], 0), "cudaStreamWaitEvent");
-                dbs_dev::DecodeParams mp = p;
-                mp.t_begin = bp_bound[i];
-                mp.t_end = bp_bound[i + 1];
-                mp.merge_state = d_state;
-                ProfileScope ps(kStepMerge, hp.mside);
-                check_cuda(dbs_dev::launch_step_merge(mp, max_K, max_C, max_T, max_N, dynamic, hp.mside,
-                                                      kPipeMergeThreads),
-                           "step merge kernel");
-            }
-            check_cuda(cudaEventRecord(hp.merged, hp.mside), "cudaEventRecord");
-            check_cuda(cudaStreamWaitEvent(stream, hp.merged, 0), "cudaStreamWaitEvent");
-        }
-        trace.mark("merge queued");
-        check_cuda(cudaStreamWaitEvent(stream, ev[bp_n + 1], 0), "cudaStreamWaitEvent");
     } else {
         if (ctl.scan && scan_end > scan_begin) {
             ProfileScope ps(kRowScan, stream);

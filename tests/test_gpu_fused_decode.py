@@ -1,16 +1,19 @@
-"""Pipelined decodes of uniform batches.
+"""Fused decodes of uniform batches, and their neighbours.
 
-A uniform batch (every example with the same steps and beams) whose merge is
-the selection merge (more than 256 candidates per step, or sequence
-constraints) is decoded in segments of steps: the row scan claims rows step
-by step across the examples, alternates its segments between two helper
-streams, and the merge of segment i runs beside the scans of later segments
-on SMs the scans leave free, the beam state passing between merge launches.
-These cases check every example against the oracle (bit-exact), with step
-counts that do not divide into the segments, EOS and length penalty,
-static and sequence constraints through the variable-batch entry point,
-16-bit rows, a rejected input followed by good decodes, and a sparse
-backward from the pipelined trace.
+A uniform batch of 2 to 64 examples (every example with the same steps and
+beams) without sequence constraints whose merge is the selection merge (more
+than 256 candidates per step) is decoded by one cooperative launch: scan
+warps list the rows step by step across the examples and count each listed
+row per (example, step); merge CTAs run each example's steps as soon as the
+step's rows are listed, so the merge follows the scan instead of waiting for
+it. Row lists hold at most 64 entries and step 0's one live row is completed
+by the merge (a radix-selected floor over the row). These cases check every
+example against the oracle, bit-exact: step counts that do not divide, EOS
+and length penalty, pools of 512 from 8 beams, a rejected input (the launch
+writes no output) followed by good decodes, a workspace that holds an
+earlier call's lists, and the sparse backward from the fused trace; plus the
+paths beside it (sequence constraints and 16-bit rows, which keep separate
+launches).
 """
 import ctypes
 

@@ -19,6 +19,7 @@ import importlib.machinery
 import importlib.util
 import os
 import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -60,11 +61,12 @@ def test_reference_microbenchmark_runs_on_the_dropin():
 
 
 def test_reference_torch_binding_on_the_dropin(oracle_lib, monkeypatch):
-    pyc = _need("torch_dbs.pyc")
+    pyc = _need("torch_dbs.bytecode")
     monkeypatch.setenv("DBS_LIBRARY", LIBDBS)
     loader = importlib.machinery.SourcelessFileLoader("reference_torch_dbs", pyc)
     spec = importlib.util.spec_from_loader("reference_torch_dbs", loader)
     mod = importlib.util.module_from_spec(spec)
+    monkeypatch.setitem(sys.modules, spec.name, mod)   # its dataclasses look their module up
     loader.exec_module(mod)
     rng = np.random.default_rng(12)
     T, K, V = 6, 4, 700

@@ -94,3 +94,67 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
                                                 dummy, dummy, dummy, None, _stream())
     assert rc == -2
     assert b"262144" in lib.dbs_last_error(h)
+
+
+def _synthetic_trace(B, T, K, P, V, device, seed):
+    """A trace with the layout a decode writes (parents < K, tokens < V,
+    lengths t + 1, weights in (0, 1)); the backward reads nothing else."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    t1 = torch.arange(1, T + 1, dtype=torch.int32)
+    arrays = dict(
+        parents=torch.randint(0, K, (B, T, K), generator=g, dtype=torch.int32),
+        tokens=torch.randint(0, V, (B, T, K), generator=g, dtype=torch.int32),
+        lengths=t1.view(1, T, 1).expand(B, T, K).contiguous(),
+        from_logprob=torch.randint(0, 2, (B, T, K), generator=g, dtype=torch.uint8),
+        weights=torch.rand((B, T, K), generator=g),
+        pool_parents=torch.randint(0, K, (B, T, P), generator=g, dtype=torch.int32),
+        pool_tokens=torch.randint(0, V, (B, T, P), generator=g, dtype=torch.int32),
+        pool_lengths=t1.view(1, T, 1).expand(B, T, P).contiguous(),
+        pool_from_logprob=torch.randint(0, 2, (B, T, P), generator=g, dtype=torch.uint8),
+        relaxed_weights=torch.rand((B, T, P), generator=g),
+    )
+    arrays = {k: v.to(device) for k, v in arrays.items()}
+    s = dbs_ctypes.DBSDeviceDecodeOutputs()
+    for name, _ in dbs_ctypes.DBSDeviceDecodeOutputs._fields_:
+        setattr(s, name, arrays[name].data_ptr() if name in arrays else None)
+    return s, arrays
+
+
+@pytest.mark.parametrize("B,T,K,mult,V", [
+    (2, 510, 4, 3, 100),       # the longest trace the scratch allows
+    (1024, 256, 2, 2, 50),     # batch_size * steps = 262144, the scratch's whole step-count table
+    (2, 5, 64, 63, 5000),      # beam + pool = 4096 entries per step
+])
+def test_noalloc_at_its_limits(B, T, K, mult, V):
+    device = torch.device("cuda", 0)
+    opts = ext.DBSOptions(beam_size=K, relaxed_pool_multiplier=mult, length_penalty_alpha=0.4,
+                          selected_temperature=0.8)
+    P = K * mult
+    tr, arrays = _synthetic_trace(B, T, K, P, V, device, seed=B + T + K)
+    gen = torch.Generator(device=device).manual_seed(5)
+    gs = torch.randn((B, T, K), device=device, generator=gen)
+    gr = torch.randn((B, T, P), device=device, generator=gen)
+    gf = torch.randn((B, K), device=device, generator=gen)
+    lib = ext._library()
+    h = ext._handle(opts)
+    ref = _sparse_outputs(B, T, K, P, device)
+    rc = lib.dbs_device_backward_batch_ex(h, B, T, V, ctypes.byref(tr), _vp(gs), _vp(gr), _vp(gf), None,
+                                          _vp(ref[0]), _vp(ref[1]), _vp(ref[2]), _vp(ref[3]), 0, _stream())
+    assert rc == 0, lib.dbs_last_error(h)
+    torch.cuda.synchronize()
+    counts = ref[2].cpu().numpy()
+    for _ in range(2):
+        out = _sparse_outputs(B, T, K, P, device)
+        rc = lib.dbs_device_backward_sparse_noalloc(h, B, T, V, ctypes.byref(tr), _vp(gs), _vp(gr), _vp(gf),
+                                                    _vp(out[0]), _vp(out[1]), _vp(out[2]), _vp(out[3]), _stream())
+        assert rc == 0, lib.dbs_last_error(h)
+        torch.cuda.synchronize()
+        assert np.array_equal(out[2].cpu().numpy(), counts)
+        n_max = int(counts.max())
+        idx_ref, idx = ref[0][:, :n_max].cpu().numpy(), out[0][:, :n_max].cpu().numpy()
+        val_ref, val = ref[1][:, :n_max].cpu().numpy(), out[1][:, :n_max].cpu().numpy()
+        for b in range(B):
+            n = int(counts[b])
+            assert np.array_equal(idx[b, :n], idx_ref[b, :n]), f"example {b} indices"
+            np.testing.assert_allclose(val[b, :n], val_ref[b, :n], rtol=1e-5, atol=1e-30)
+        np.testing.assert_allclose(out[3].cpu().numpy(), ref[3].cpu().numpy(), rtol=1e-5, atol=1e-30)
