@@ -73,6 +73,9 @@ OPTIONS = dict(beam_size=8, eos_token=2, length_penalty_alpha=0.2, selected_temp
 WORKLOAD3 = dict(B=256, T=64, K=32, V=50257)
 OPTIONS3 = dict(beam_size=32)
 REF_SAMPLE3 = 16
+# config 5 (one long huge-vocabulary example; one GPU)
+WORKLOAD5 = dict(B=1, T=256, K=16, V=256000)
+OPTIONS5 = dict(beam_size=16)
 
 
 def parse_args(argv=None):
@@ -80,7 +83,9 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=3, choices=(2, 3))
+    ap.add_argument("--config", type=int, default=3, choices=(2, 3, 5),
+                    help="3: the large-beam batch (default, the bench line); 2: the torch final_scores batch; "
+                         "5: the single B=1 T=256 K=16 V=256000 example (one GPU)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None,
                     help="end-to-end steps (default 20 for config 2, 2 for config 3)")
@@ -131,6 +136,20 @@ def make_inputs3(torch, B, T, K, V, first_example, device):
         g.manual_seed(SEED * 1_000_003 + first_example + b)
         x[b].normal_(generator=g)
         x[b] = torch.log_softmax(x[b], dim=-1)
+    return x
+
+
+def make_inputs5(torch, T, K, V, device):
+    """Config 5: log_softmax over V of N(0,1) logits plus +8 on 64 seeded ids of
+    each step (the same ids in every row of the step), one example."""
+    x = torch.empty((1, T, K, V), dtype=torch.float32, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED * 1_000_003)
+    x[0].normal_(generator=g)
+    for t in range(T):
+        ids = torch.randint(0, V, (64,), generator=g, device=device)
+        x[0, t, :, ids] += 8.0
+    x[0] = torch.log_softmax(x[0], dim=-1)
     return x
 
 
@@ -398,7 +417,7 @@ def _oracle_port_run(x, steps_budget_s):
     return elems / dt, 1, "port", sample
 
 
-def reference_run3(x_host, reps_min=1, budget_s=10.0, keep_outputs=False):
+def reference_run3(x_host, reps_min=1, budget_s=10.0, keep_outputs=False, options=None):
     """Config 3: time the reference CPU library on a sample of examples.
 
     One repetition = dbs_decode_batch over the sample (all host threads) and
@@ -423,7 +442,7 @@ def reference_run3(x_host, reps_min=1, budget_s=10.0, keep_outputs=False):
     if path is not None:
         cores = os.cpu_count() or 1
         lib = dc.load_library(path, device_api=False)
-        dec = dc.Decoder(lib, dc.Options(**OPTIONS3))
+        dec = dc.Decoder(lib, dc.Options(**(options or OPTIONS3)))
         while True:
             br = dec.decode_batch(x, n, T, V, cores)
             cur = []
@@ -451,7 +470,7 @@ def reference_run3(x_host, reps_min=1, budget_s=10.0, keep_outputs=False):
             return None
         cores = 1
         ol = OracleLib()
-        opts = ol.options(**OPTIONS3)
+        opts = ol.options(**(options or OPTIONS3))
         while True:
             cur = []
             for b in range(n):
@@ -487,6 +506,14 @@ def bench_config3(B, T, K, V, world, per_rank):
                             f"tokens, parents and sparse gradients each step" if world > 1 else
                             "one GPU, whole batch"),
             "l2": f"inputs larger than L2 ({4 * per_rank * T * K * V / 1e9:.1f} GB per GPU); no flush needed"}
+
+
+def bench_config5(T, K, V):
+    return {"workload": f"C ABI device decode (pool P={8 * K} + weights) + sparse backward (grad_final=e_0), "
+                        f"B=1 T={T} K={K} V={V}, log_softmax(N(0,1) + 8 on 64 ids per step), default options",
+            "global_batch": 1, "seq_len": T, "beam_size": K, "vocab": V, "examples_per_gpu": 1,
+            "parallelism": "one GPU",
+            "l2": f"inputs larger than L2 ({4 * T * K * V / 1e9:.1f} GB); no flush needed"}
 
 
 def bench_bytes_bound(B, T, K, V):
@@ -591,6 +618,9 @@ def compare_with_reference(ours, ref, label):
 
 
 def run_config3(args, rank, world, local):
+    """Configs 3 and 5: device decode (pool + weights) + sparse backward of
+    grad_final = e_0 through the C ABI's device entry points; config 3's
+    batch is split over the ranks with an all-gather of the results."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -603,19 +633,21 @@ def run_config3(args, rank, world, local):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
-    Bg, T, K, V = (WORKLOAD3[k] for k in "BTKV")
+    five = args.config == 5
+    W, O = (WORKLOAD5, OPTIONS5) if five else (WORKLOAD3, OPTIONS3)
+    Bg, T, K, V = (W[k] for k in "BTKV")
     if Bg % world:
         raise SystemExit(f"the {Bg}-example batch does not split over {world} ranks")
     Bl = args.batch or Bg // world
     first = rank * Bl
     P = 8 * K
     elems = Bl * T * K * V
-    opts = ext.DBSOptions(**OPTIONS3)
+    opts = ext.DBSOptions(**O)
     lib = ext._library()
     h = ext._handle(opts)
 
     t_gen = time.perf_counter()
-    x = make_inputs3(torch, Bl, T, K, V, first, device)
+    x = make_inputs5(torch, T, K, V, device) if five else make_inputs3(torch, Bl, T, K, V, first, device)
     torch.cuda.synchronize()
     t_gen = time.perf_counter() - t_gen
 
@@ -755,7 +787,7 @@ def run_config3(args, rank, world, local):
     rs_ms = rs["total_ms"] / max(1, rs["launches"])
     alg_bytes = bench_bytes_bound(Bl, T, K, V)
     achieved = alg_bytes / (rs_ms / 1e3) / 1e9 if rs_ms > 0 else None
-    traffic = ncu_traffic_per_launch(3)
+    traffic = ncu_traffic_per_launch(3) if not five else None
     if traffic is not None and args.batch is None:
         traffic = traffic * Bl / 32.0   # the committed capture covers 32 examples
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -799,16 +831,17 @@ def run_config3(args, rank, world, local):
     # pinned host log-probs (the library stages them to the device inside the
     # call), dbs_backward per example, every result read on the host
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else 2
-    x_host = torch.empty((Bl, T, K, V), dtype=torch.float32, pin_memory=True)
-    for b0 in range(0, Bl, 16):
-        x_host[b0:b0 + 16].copy_(x[b0:b0 + 16])
+    x_host = torch.empty((Bl if e2e_steps > 0 else 1, T, K, V), dtype=torch.float32, pin_memory=True)
+    if e2e_steps > 0:
+        for b0 in range(0, Bl, 16):
+            x_host[b0:b0 + 16].copy_(x[b0:b0 + 16])
     del x
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     import dbs_ctypes as dc
     gf_host = np.zeros(K, dtype=np.float32)
     gf_host[0] = 1.0
-    dec = dc.Decoder(lib, dc.Options(**OPTIONS3))
+    dec = dc.Decoder(lib, dc.Options(**O))
     xh = x_host.numpy()
     nnz_total = [0]
 
@@ -825,19 +858,21 @@ def run_config3(args, rank, world, local):
         lib.dbs_free_batch_result(br)
         nnz_total[0] = nnz
 
-    e2e_step()   # warm-up: the library's staging pools
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        e2e_step()
-    torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - e0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item()) * 1e3 / e2e_steps
+    e2e_ms = float("nan")
+    if e2e_steps > 0:   # (0: profiling runs without the end-to-end part)
+        e2e_step()   # warm-up: the library's staging pools
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step()
+        torch.cuda.synchronize()
+        e2e_s = time.perf_counter() - e0
+        te = torch.tensor([e2e_s], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item()) * 1e3 / e2e_steps
     dec.close()
     # bytes the library moves per step: the log-probs, and for each
     # example's backward the trace it stages (parents, tokens, lengths,
@@ -854,7 +889,7 @@ def run_config3(args, rank, world, local):
     cpu = None
     parity = "not run: the CPU baseline leg runs on rank 0 at one GPU only" if not want_cpu else None
     if want_cpu:
-        r = reference_run3(x_sample, reps_min=1, budget_s=10.0, keep_outputs=True)
+        r = reference_run3(x_sample, reps_min=1, budget_s=10.0, keep_outputs=True, options=O)
         if r is None:
             parity = "not run: neither the reference library nor the oracle is built"
         else:
@@ -877,8 +912,9 @@ def run_config3(args, rank, world, local):
         "metric": METRIC, "value": value, "unit": "elem/s", "n_gpus": world, "steps": args.steps,
         "warmup": warm_steps, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: log_softmax(N(0,1)) over V, generated on the device per example (seeded)",
-        "config": bench_config3(Bg, T, K, V, world, Bl),
+        "data": ("synthetic: log_softmax(N(0,1) + 8 on 64 seeded ids per step) over V, generated on the device"
+                 if five else "synthetic: log_softmax(N(0,1)) over V, generated on the device per example (seeded)"),
+        "config": bench_config5(T, K, V) if five else bench_config3(Bg, T, K, V, world, Bl),
         "roofline": roofline,
         "step_hbm": whole,
         "cpu_baseline": cpu,
@@ -1096,6 +1132,8 @@ def main():
     if args.config == 2:
         run_config2(args, rank, world, local)
     else:
+        if args.config == 5 and world > 1:
+            raise SystemExit("--config 5 runs on one GPU (its one example does not split by examples)")
         run_config3(args, rank, world, local)
 
 

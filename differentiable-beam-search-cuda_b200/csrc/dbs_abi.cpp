@@ -290,14 +290,17 @@ void check_example(const Options& opt, const float* x, int T, int V, int K, int 
     (void)checked_mul(sel, static_cast<size_t>(V), "log-prob tensor size overflow");
 }
 
+// Bytes of host log-probs staged on the device per chunk. Two chunks are in
+// flight (one decoding while the next is copied), so chunks stay a few GB:
+// the copies then run back to back at the host link's rate.
 size_t device_budget_bytes() {
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) {
         cudaGetLastError();
-        return static_cast<size_t>(4) << 30;
+        return static_cast<size_t>(1) << 30;
     }
-    size_t b = free_b / 2;
-    const size_t cap = static_cast<size_t>(48) << 30;
+    size_t b = free_b / 8;
+    const size_t cap = static_cast<size_t>(4) << 30;
     return std::min(b, cap);
 }
 
@@ -369,18 +372,74 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
     // 16-bit inputs arrive on the device; model-step rows are produced there
     const bool x_dev = x16 != nullptr || rows != nullptr || is_device_pointer(x);
     const size_t budget = device_budget_bytes();
-    int b0 = 0;
-    while (b0 < B) {
-        // chunk [b0, b1)
-        int b1 = b0;
+    // Example chunks: host inputs are staged a chunk at a time into one of
+    // two device buffers; the next chunk's copy (on a copy stream) runs while
+    // the current chunk decodes and its results are read back.
+    struct Chunk {
+        int b0, b1;
+        int64_t elems;
+    };
+    std::vector<Chunk> chunks;
+    int64_t max_elems = 0;
+    for (int c0 = 0; c0 < B;) {
+        int c1 = c0;
         size_t bytes = 0;
-        while (b1 < B) {
-            size_t need = static_cast<size_t>(hx[b1].T) * hx[b1].K * V * sizeof(float);
-            if (x_dev) need = 0;
-            if (b1 > b0 && bytes + need > budget) break;
+        int64_t elems = 0;
+        while (c1 < B) {
+            const int64_t ne = x_dev ? 0 : static_cast<int64_t>(hx[c1].T) * hx[c1].K * V;
+            const size_t need = static_cast<size_t>(ne) * sizeof(float);
+            if (c1 > c0 && bytes + need > budget) break;
             bytes += need;
-            ++b1;
+            elems += ne;
+            ++c1;
         }
+        chunks.push_back(Chunk{c0, c1, elems});
+        max_elems = std::max(max_elems, elems);
+        c0 = c1;
+    }
+    const int n_staged = x_dev ? 0 : (chunks.size() > 1 ? 2 : 1);
+    std::unique_ptr<DeviceBuffer> stage_buf[2];
+    for (int i = 0; i < n_staged; ++i)
+        stage_buf[i].reset(new DeviceBuffer(static_cast<size_t>(max_elems) * sizeof(float), s));
+    std::unique_ptr<CallStream> copy_cs;
+    cudaEvent_t staged_ev[2] = {nullptr, nullptr};
+    struct EventPairGuard {
+        cudaEvent_t* e;
+        ~EventPairGuard() {
+            for (int i = 0; i < 2; ++i)
+                if (e[i]) cudaEventDestroy(e[i]);
+        }
+    } staged_guard{staged_ev};
+    if (n_staged) {
+        copy_cs.reset(new CallStream(nullptr));
+        // the staging buffers come from `s`'s allocations: the copy stream waits for them
+        for (int i = 0; i < 2; ++i)
+            dbs_host::check_cuda(cudaEventCreateWithFlags(&staged_ev[i], cudaEventDisableTiming), "cudaEventCreate");
+        dbs_host::check_cuda(cudaEventRecord(staged_ev[0], s), "cudaEventRecord");
+        dbs_host::check_cuda(cudaStreamWaitEvent(copy_cs->s, staged_ev[0], 0), "cudaStreamWaitEvent");
+    }
+    auto stage = [&](size_t ci) {   // host -> device copy of chunk ci's log-probs
+        const Chunk& c = chunks[ci];
+        float* dst = stage_buf[ci & 1]->as<float>();
+        int64_t off = 0;
+        for (int b = c.b0; b < c.b1; ++b) {
+            const HostExample& e = hx[b];
+            const size_t width = static_cast<size_t>(e.K) * V * sizeof(float);
+            const size_t pitch = static_cast<size_t>(e.k_stride) * V * sizeof(float);
+            dbs_host::check_cuda(cudaMemcpy2DAsync(dst + off, width, x + e.x_offset, pitch, width,
+                                                   static_cast<size_t>(e.T), cudaMemcpyHostToDevice, copy_cs->s),
+                                 "stage log_probs");
+            off += static_cast<int64_t>(e.T) * e.K * V;
+        }
+        dbs_host::check_cuda(cudaEventRecord(staged_ev[ci & 1], copy_cs->s), "cudaEventRecord");
+    };
+    if (n_staged) stage(0);
+    for (size_t ci = 0; ci < chunks.size(); ++ci) {
+        const int b0 = chunks[ci].b0, b1 = chunks[ci].b1;
+        // the next chunk's buffer was last read by chunk ci - 1, whose decode
+        // has finished (each chunk's decode synchronises below)
+        if (n_staged && ci + 1 < chunks.size()) stage(ci + 1);
+        if (n_staged) dbs_host::check_cuda(cudaStreamWaitEvent(s, staged_ev[ci & 1], 0), "cudaStreamWaitEvent");
         const int nb = b1 - b0;
         std::vector<ExampleSpec> spec(nb);
         int64_t staged_elems = 0;
@@ -397,17 +456,6 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
                 spec[i].x_offset = staged_elems;
                 spec[i].k_stride = e.K;
                 staged_elems += static_cast<int64_t>(e.T) * e.K * V;
-            }
-        }
-        DeviceBuffer xs(x_dev ? 0 : static_cast<size_t>(staged_elems) * sizeof(float), s);
-        if (!x_dev) {
-            for (int i = 0; i < nb; ++i) {
-                const HostExample& e = hx[b0 + i];
-                const size_t width = static_cast<size_t>(e.K) * V * sizeof(float);
-                const size_t pitch = static_cast<size_t>(e.k_stride) * V * sizeof(float);
-                dbs_host::check_cuda(cudaMemcpy2DAsync(xs.as<float>() + spec[i].x_offset, width, x + e.x_offset, pitch,
-                                                       width, static_cast<size_t>(e.T), cudaMemcpyHostToDevice, s),
-                                     "stage log_probs");
             }
         }
         // constraint arrays
@@ -462,7 +510,7 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
         o.pool_from_logprob = reinterpret_cast<uint8_t*>(take(npool));
         o.final_raw_scores = reinterpret_cast<float*>(take(nfin * 4));
         o.final_scores = reinterpret_cast<float*>(take(nfin * 4));
-        const float* dx = x_dev ? x : xs.as<float>();
+        const float* dx = x_dev ? x : stage_buf[ci & 1]->as<float>();
         dbs_host::DecodeStats st;
         if (rows) {
             // one example (dbs_decode_model_steps): rows arrive step by step
@@ -506,7 +554,6 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
         d2h(store->final_raw.data() + fo, o.final_raw_scores, nfin * 4);
         d2h(store->final_scores.data() + fo, o.final_scores, nfin * 4);
         dbs_host::check_cuda(cudaStreamSynchronize(s), "decode");
-        b0 = b1;
     }
     (void)h;
     (void)stats_handle;

@@ -100,10 +100,11 @@ struct DecodeParams {
     // the step merge reads step 0 as that one list.
     int32_t first_row_apart;
     int32_t first_rows_only;
-    // Step-major row claims (the fused decode of a uniform batch of B
+    // Step-major row claims of the fused decode (a uniform batch of B
     // examples, K beams, row stride step_major_tk = T*K per example): with
     // step_major_bk = B*K, claim c scans step c / (B*K) of example
     // (c / K) % B, beam c % K, so the rows of early steps are listed first.
+    // (The separate row-scan launches claim rows in order.)
     int64_t step_major_bk;
     int64_t step_major_tk;
     // workspace

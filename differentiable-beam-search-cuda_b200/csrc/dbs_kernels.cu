@@ -700,7 +700,6 @@ struct RowJob {
     int h;       // unaligned head elements
     int nv;      // float4 in the aligned body
     int chunks;
-    int done_idx;  // e * T + t: the step-completion counter of the row (fused decode)
 };
 
 template <bool k16>
@@ -709,9 +708,9 @@ __device__ __forceinline__ float row_lp(const RowJob& j, int i, bool bf16) {
     else return static_cast<const float*>(j.row)[i];
 }
 
-template <bool k16>
+template <bool k16, bool kFused>
 __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int& e) {
-    if (p.step_major_bk) e = static_cast<int>(r / p.step_major_tk);   // uniform batch: rows jump between examples
+    if constexpr (kFused) e = static_cast<int>(r / p.step_major_tk);   // uniform batch: rows jump between examples
     else while (r >= p.row_prefix[e + 1]) ++e;
     const ExampleDesc& d = p.desc[e];
     RowJob j;
@@ -744,7 +743,6 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     j.h = h;
     j.nv = (p.V - h) >> (4 - kShift);
     j.chunks = (j.forced >= 0 || j.dead || j.apart) ? 0 : (j.nv + kScanChunkF4 - 1) / kScanChunkF4;
-    j.done_idx = e * d.T + t;
     return j;
 }
 
@@ -757,7 +755,7 @@ __device__ __forceinline__ void scan_row_done(unsigned int* step_done, int idx, 
     if (lane == 0) atomicAdd(step_done + idx, 1u);
 }
 
-template <bool k16>
+template <bool k16, bool kFused>
 __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, int speculate, unsigned char* smem_raw,
                                               unsigned int* step_done) {
     constexpr unsigned FULL = 0xFFFFFFFFu;
@@ -793,7 +791,7 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
         if (p.first_rows_only)   // claim i: the first row of example i
             return r < static_cast<unsigned long long>(p.B) ? p.row_prefix[r] : kNoRow;
         if (r >= static_cast<unsigned long long>(p.total_rows)) return kNoRow;
-        if (p.step_major_bk) {
+        if constexpr (kFused) {
             // claim order: step, then example, then beam
             const int64_t c = static_cast<int64_t>(r);
             const int64_t t = c / p.step_major_bk;
@@ -810,7 +808,7 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
     int64_t r_cur = claim();
     if (r_cur == kNoRow) return;
     e_cur = find_example(p.row_prefix, p.B, r_cur);
-    RowJob cur = make_job<k16>(p, r_cur, e_cur);
+    RowJob cur = make_job<k16, kFused>(p, r_cur, e_cur);
     e_nxt = e_cur;
     RowJob nxt = cur;
     bool have_nxt = false;
@@ -839,7 +837,7 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
                 if (!have_nxt) {
                     const int64_t rn = claim();
                     if (rn == kNoRow) break;
-                    nxt = make_job<k16>(p, rn, e_nxt);
+                    nxt = make_job<k16, kFused>(p, rn, e_nxt);
                     have_nxt = true;
                 }
                 inxt = true;
@@ -1162,13 +1160,19 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
             }
             __syncwarp();
         }
-        if (step_done && !j.apart) scan_row_done(step_done, j.done_idx, lane);
+        if constexpr (kFused) {
+            // step_done[e * T + t] of a uniform batch (row r = e * T * K + t * K + k)
+            const int64_t e = j.r / p.step_major_tk;
+            const int64_t kk = p.step_major_bk / p.B;
+            const int t = static_cast<int>((j.r - e * p.step_major_tk) / kk);
+            scan_row_done(step_done, static_cast<int>(e * (p.step_major_tk / kk)) + t, lane);
+        }
         // advance to the next claimed row
         if (!inxt) {
             // nothing of the next row was issued yet (nor claimed)
             const int64_t rn = claim();
             if (rn == kNoRow) return;
-            nxt = make_job<k16>(p, rn, e_nxt);
+            nxt = make_job<k16, kFused>(p, rn, e_nxt);
             cursor_to(nxt);
         }
         cur = nxt;
@@ -1181,7 +1185,7 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
 template <bool k16>
 __global__ void __launch_bounds__(kScanWarpsPerCta * 32, 4) row_scan_kernel(DecodeParams p, int capw, int speculate) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    row_scan_body<k16>(p, capw, speculate, smem_raw, nullptr);
+    row_scan_body<k16, false>(p, capw, speculate, smem_raw, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -2649,7 +2653,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodePa
                                                                       unsigned int* step_done) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     if (static_cast<int>(blockIdx.x) >= merge_ctas) {
-        row_scan_body<false>(p, capw, 1, smem_raw, step_done);
+        row_scan_body<false, true>(p, capw, 1, smem_raw, step_done);
         return;
     }
     __shared__ int sh_bad;
@@ -3904,7 +3908,7 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
 cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int max_N, int merge_ctas,
                                 unsigned int* step_done, int num_sms, cudaStream_t stream) {
     const int M = max_K * max_C;
-    if (M > 8 * kFusedThreads || max_N > 1024 || merge_ctas < 1 || max_C > 64) return cudaErrorNotSupported;
+    if (M > 8 * kFusedThreads || max_N > 1024 || merge_ctas < 1 || max_C > 128) return cudaErrorNotSupported;
     const int capw = row_scan_capw(max_C);
     const int sel_cap = list_merge_sel_cap(max_N, kFusedThreads);
     size_t smem = static_cast<size_t>(kFusedThreads / 32) * row_scan_warp_bytes(capw, false);

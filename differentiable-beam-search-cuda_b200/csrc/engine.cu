@@ -514,15 +514,20 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     // (measured with T = 64, K = 32, V = 50257: 32 examples 5.07 -> 3.81 ms,
     // 64 examples 7.28 -> 6.87 ms, but 128 examples 11.8 -> 13.0 ms).
     bool fused = false;
-    if (B >= 2 && B <= kFusedMaxExamples && !dynamic && !ext_lists && ctl.scan && ctl.merge && ctl.t_begin <= 0 && ctl.t_end >= (1 << 30) &&
+    int fused_C = 0;
+    if (B <= kFusedMaxExamples && !dynamic && !ext_lists && ctl.scan && ctl.merge && ctl.t_begin <= 0 && ctl.t_end >= (1 << 30) &&
         !ctl.merge_state && !ctl.row_allow && !ctl.x16 && ctl.scan_begin <= 0 && ctl.scan_end < 0 &&
         !(ctl.zero_fill && ctl.zero_fill_count > 0) && fused_enabled()) {
         bool uni = true;
         for (const ExampleSpec& e : ex) uni = uni && e.T == ex[0].T && e.K == ex[0].K;
         const int K0 = ex[0].K;
         const int N0 = pool ? pool_size(K0, opt.relaxed_pool_multiplier) : K0;
-        const int C0 = std::min(list_capacity_for(N0, K0, false), kShortListEntries);
-        const int64_t M0 = static_cast<int64_t>(K0) * C0;
+        // lists of 64 when many rows share the work (the merge rescans the
+        // few rows that hold more of a step's pool), up to 128 for a few
+        // examples, whose rows are long per warp and whose rescans would sit
+        // on the one merge CTA's critical path
+        fused_C = std::min(list_capacity_for(N0, K0, false), B >= 8 ? kShortListEntries : 2 * kShortListEntries);
+        const int64_t M0 = static_cast<int64_t>(K0) * fused_C;
         fused = uni && ex[0].T >= 2 && M0 > 256 && M0 <= dbs_dev::kListMergeMaxCandidates && N0 <= 1024;
     }
     if (fused) short_lists = false;
@@ -536,7 +541,8 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         const int P = layout.P[b];
         const int N = pool ? P : e.K;
         int C = list_capacity_for(N, e.K, dynamic);
-        if ((short_lists || fused) && C > kShortListEntries) C = kShortListEntries;
+        if (short_lists && C > kShortListEntries) C = kShortListEntries;
+        if (fused && C > fused_C) C = fused_C;
         if (e.K > 1024) throw LengthError("beam_size above 1024 is not supported by the device decoder");
         dbs_dev::ExampleDesc& d = desc[b];
         d.x_offset = e.x_offset;
@@ -590,7 +596,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     // as its rows are listed, beside the scan of the next segment; the beam
     // state passes between the merge launches in the workspace.
     int seg_steps = 0, n_seg = 0;
-    if (B == 1 && ctl.scan && ctl.merge && !ext_lists && scan_begin == 0 && scan_end == rows &&
+    if (!fused && B == 1 && ctl.scan && ctl.merge && !ext_lists && scan_begin == 0 && scan_end == rows &&
         ctl.t_begin <= 0 && ctl.t_end >= max_T && !ctl.merge_state && !ctl.row_allow && max_T >= 32 &&
         (dynamic || static_cast<int64_t>(max_K) * max_C > 256)) {
         // about 512 rows per segment (at least 16 steps): the first merge
