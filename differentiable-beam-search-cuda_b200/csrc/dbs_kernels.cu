@@ -1879,28 +1879,36 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
 
 // ---------------------------------------------------------------------------
 // 2c. Compact selection merge (no repetition penalty / n-gram blocking /
-//     prefix-keeping, at most 4096 candidates per step, pools up to 1024).
+//     prefix-keeping, at most 8 * NT candidates per step, pools up to NT).
 //
 // One CTA of NT threads per example walks its steps. Every thread owns
 // kLmPer candidate slots of a step (slot idx = tid + u * NT: entry idx % C
 // of row idx / C) and holds their 64-bit (rank, raw) keys and tokens in
 // registers, so a step needs no shared-memory copy of its K row lists. A
 // radix select over the 128-bit candidate keys (rank, raw, then parent and
-// token; 8 bits per pass from the highest bit where the keys differ,
-// per-warp histograms) narrows the keys that can be among the top N to at
-// most sel_cap; those are gathered and sorted by a bitonic network, and the
-// first N are the step's pool (the same order as the reference's
-// candidate_better, src/differentiable_beam.cpp:291-298). The exactness
-// proof and the rescans of truncated rows follow the selection merge.
+// token; 8 bits per pass from the highest bit where the keys differ)
+// narrows the keys that can be among the top N to at most NT; those form
+// one sorted run per row, which are merged pairwise, and the first N are
+// the step's pool (the same order as the reference's candidate_better,
+// src/differentiable_beam.cpp:291-298). The exactness proof and the
+// rescans of truncated rows follow the selection merge.
 // ---------------------------------------------------------------------------
 
-// Descending bitonic sort of n2 (a power of two) two-word keys, (0, 0) pads
-// last. Called by all threads of the block; ends with a barrier.
-// Shared memory of list_merge_body: selection keys, per-warp histograms and
-// ten per-beam arrays.
+// Shared memory of list_merge_body: selection keys, the histogram and ten
+// per-beam arrays; then, 128-byte aligned, the rescans' ring of row stages
+// and their barriers.
 __host__ __device__ constexpr size_t list_merge_smem(int nt, int sel_cap, int max_K) {
     return static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t) + 256 * sizeof(int) +
            static_cast<size_t>(max_K) * 10 * sizeof(int) + 0 * nt;
+}
+constexpr int kRescanChunkF4 = 1024;   // one rescan stage: 16 KB of a row
+constexpr int kRescanMaxStages = 8;
+__host__ __device__ constexpr size_t list_merge_ring_at(int nt, int sel_cap, int max_K) {
+    return (list_merge_smem(nt, sel_cap, max_K) + 127) & ~static_cast<size_t>(127);
+}
+__host__ __device__ constexpr size_t list_merge_total_smem(int nt, int sel_cap, int max_K, int stages) {
+    return list_merge_ring_at(nt, sel_cap, max_K) +
+           static_cast<size_t>(stages) * (kRescanChunkF4 * 16 + sizeof(uint64_t));
 }
 // Selection buffer: a power of two with room for the top N plus a staging
 // area of at least 256 and of at least one value per thread (rescans).
@@ -1910,6 +1918,8 @@ __host__ __device__ constexpr int list_merge_sel_cap(int max_N, int nt) {
     return c;
 }
 
+// Descending bitonic sort of n2 (a power of two) two-word keys, (0, 0) pads
+// last. Called by all threads of the block; ends with a barrier.
 template <int NT>
 __device__ __forceinline__ void lm_sort(uint64_t* hi, uint64_t* lo, int n2) {
     const int half = n2 >> 1;
@@ -1927,6 +1937,87 @@ __device__ __forceinline__ void lm_sort(uint64_t* hi, uint64_t* lo, int n2) {
             __syncthreads();
         }
     }
+}
+
+// Sorts the g <= NT keys in hi/lo[0, g) descending, one per thread, by a
+// bitonic network (strides below 32 by warp shuffles, larger ones through the
+// halves [0, NT) and [NT, 2 NT) of the buffers in turn, one barrier each),
+// leaves the first n in hi/lo[0, n) and zeroes [n, 2 NT). Called by all
+// threads of the block; ends with a barrier.
+template <int NT>
+__device__ __forceinline__ void lm_sort_registers(uint64_t* sh, uint64_t* sl, int g, int N) {
+    constexpr unsigned FULL = 0xFFFFFFFFu;
+    const int tid = threadIdx.x;
+    uint64_t kh = 0, kl = 0;
+    if (tid < g) {
+        kh = sh[tid];
+        kl = sl[tid];
+    }
+    int half = 0;
+    __syncthreads();   // every key is in registers
+#pragma unroll 1
+    for (int size = 2; size <= NT; size <<= 1) {
+#pragma unroll 1
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            uint64_t oh, ol;
+            if (stride >= 32) {
+                uint64_t* bh = sh + half * NT;
+                uint64_t* bl = sl + half * NT;
+                bh[tid] = kh;
+                bl[tid] = kl;
+                __syncthreads();
+                oh = bh[tid ^ stride];
+                ol = bl[tid ^ stride];
+                half ^= 1;
+            } else {
+                oh = __shfl_xor_sync(FULL, kh, stride);
+                ol = __shfl_xor_sync(FULL, kl, stride);
+            }
+            // a descending segment keeps the larger key at the lower index
+            const bool keep_max = ((tid & size) == 0) == ((tid & stride) == 0);
+            const bool take = keep_max ? key2_less(kh, kl, oh, ol) : key2_less(oh, ol, kh, kl);
+            if (take) {
+                kh = oh;
+                kl = ol;
+            }
+        }
+    }
+    __syncthreads();   // the last exchange's reads are done
+    if (tid < N) {
+        sh[tid] = kh;
+        sl[tid] = kl;
+    }
+    for (int i = N + tid; i < 2 * NT; i += NT) {
+        sh[i] = 0;
+        sl[i] = 0;
+    }
+    __syncthreads();
+}
+
+// Ring of row stages for the rescans of list_merge_body (stages 0 to
+// kRescanMaxStages of kRescanChunkF4 float4 each, at list_merge_ring_at(),
+// one mbarrier per stage after them). seq counts the stages consumed so far,
+// which gives each stage's next phase. Owned by the kernel: set up once by
+// rescan_ring_init, published by the block barrier at the start of
+// list_merge_body.
+struct RescanRing {
+    float4* stage;
+    uint64_t* bar;
+    int stages;
+    uint32_t seq;
+};
+template <int NT>
+__device__ __forceinline__ RescanRing rescan_ring_init(unsigned char* smem, int sel_cap, int seq_K, int stages) {
+    RescanRing r;
+    r.stages = stages;
+    r.seq = 0;
+    r.stage = reinterpret_cast<float4*>(smem + list_merge_ring_at(NT, sel_cap, seq_K));
+    r.bar = reinterpret_cast<uint64_t*>(r.stage + static_cast<size_t>(stages) * kRescanChunkF4);
+    if (stages > 0 && threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) mbar_init(r.bar + s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    return r;
 }
 
 // Bounded wait of a merge CTA for the K rows of step t of example e
@@ -1964,10 +2055,13 @@ __device__ __forceinline__ bool wait_step_rows(const DecodeParams& p, const unsi
 // example) carries the beams between calls: loaded when t_first > 0,
 // stored when steps remain. With step_done the CTA waits for each step's
 // rows (the fused decode); lists, counts and bounds are read around L1.
+// The rows that fp32 rescans read arrive in rs's 16 KB shared-memory stages
+// by bulk copies, every stage in flight at once; without stages the rescans
+// read the row with vector loads.
 template <int NT, int PER>
 __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, int t_first, int t_stop, float* state,
                                                 int seq_K, int sel_cap, unsigned char* smem,
-                                                const unsigned int* step_done) {
+                                                const unsigned int* step_done, RescanRing& rs) {
     constexpr int NW = NT / 32;
     constexpr unsigned FULL = 0xFFFFFFFFu;
     constexpr int kLmPer = PER;
@@ -2022,30 +2116,38 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
         const bool eos_blocked = use_eos && (t + 1) < d.min_length;
         __syncthreads();   // the previous step's state update is visible
         if (step_done && !wait_step_rows(p, step_done, e * T + t, static_cast<unsigned int>(K))) return false;
+        const bool long0 = p.first_row_apart && t == 0;
+        // The step's list entries (its M slots of the lists) are loaded
+        // together with the counts and bounds, one round trip; entries past
+        // a row's count are dropped after the barrier.
+        uint64_t raw_e[kLmPer];
+#pragma unroll
+        for (int u = 0; u < kLmPer; ++u) {
+            const int idx = tid + u * NT;
+            raw_e[u] = idx < M ? __ldcg(reinterpret_cast<const unsigned long long*>(step_lists) + idx) : 0ull;
+        }
         for (int k = tid; k < K; k += NT) {
             row_cnt[k] = __ldcg(p.list_count + row0 + k);
             row_bound[k] = __ldcg(p.list_bound + row0 + k);
             row_inv[k] = p.inv_pen[prev_len[k] + 1];
             unsafe[k] = 0;
+            next_len[k] = 0;   // the run lengths of the sort
         }
         if (tid == 0) { sh_n = 0; sh_g = 0; sh_any = 0; }
+        for (int i = tid; i < 256; i += NT) hist[i] = 0;   // the first radix pass
         __syncthreads();
-        const bool long0 = p.first_row_apart && t == 0;
 
         // candidate keys of this thread's slots
         uint64_t ch[kLmPer];
         int ctok[kLmPer];
         {
-            uint64_t raw_e[kLmPer];
 #pragma unroll
             for (int u = 0; u < kLmPer; ++u) {
                 const int idx = tid + u * NT;
-                raw_e[u] = 0;
                 if (idx < M) {
                     const int k = long0 ? 0 : idx / C;
                     const int i = idx - k * C;
-                    if (i < row_cnt[k] && isfinite(prev_raw[k]) && !(use_eos && ended[k]))
-                        raw_e[u] = __ldcg(reinterpret_cast<const unsigned long long*>(step_lists) + idx);
+                    if (!(i < row_cnt[k] && isfinite(prev_raw[k]) && !(use_eos && ended[k]))) raw_e[u] = 0;
                 }
             }
 #pragma unroll
@@ -2085,10 +2187,9 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
 
         // Radix select: the masked prefix (ph, pl) that the top-N keys reach
         uint64_t ph = 0, pl = 0, mh = 0, ml = 0;   // prefix and mask over (hi, lo)
-        // the gathered keys are ranked by counting (one per thread), so
-        // at most NT of them; fewer when the radix passes can get there
+        // the gathered keys are sorted one per thread, so at most NT of them
         const int gather_cap = NT < sel_cap ? NT : sel_cap;
-        const int gather_goal = N + 128 < gather_cap ? N + 128 : gather_cap;
+        const int gather_goal = gather_cap;
         int need = N;
         int total = 0;
         {
@@ -2138,9 +2239,11 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                     mh = (shift + 8 >= 64) ? 0ull : ~((1ull << (shift + 8)) - 1ull);
                     ph = mx & mh;
                 }
-                for (;;) {
-                    for (int i = tid; i < 256; i += NT) hist[i] = 0;
-                    __syncthreads();
+                for (bool first = true;; first = false) {
+                    if (!first) {
+                        for (int i = tid; i < 256; i += NT) hist[i] = 0;
+                        __syncthreads();
+                    }
                     int* wh = hist;
 #pragma unroll
                     for (int u = 0; u < kLmPer; ++u) {
@@ -2211,8 +2314,8 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                 }
             }
         }
-        // gather every candidate whose masked key reaches the prefix (one
-        // shared atomic per warp and slot round)
+        // The taken candidates: every one whose masked key reaches the prefix.
+        bool tk[kLmPer];
 #pragma unroll
         for (int u = 0; u < kLmPer; ++u) {
             const uint64_t h = ch[u];
@@ -2224,47 +2327,136 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                     take = ml == 0 || (l & ml) >= pl;
                 }
             }
-            const unsigned bal = __ballot_sync(FULL, take);
-            int base = 0;
-            if (lane == 0 && bal) base = atomicAdd(&sh_g, __popc(bal));
-            base = __shfl_sync(FULL, base, 0);
-            if (take) {
-                const int pos = base + __popc(bal & ((1u << lane) - 1u));
-                sh[pos] = h;
-                sl[pos] = cand_lo_of(u);
-            }
+            tk[u] = take;
         }
-        __syncthreads();
+        // Sort them, descending. They form one run per parent row (the
+        // row's first entries: a row list is in decreasing key order), so
+        // each run is placed at its offset and the runs are merged pairwise
+        // in ceil(log2 runs) rounds, each key finding its place in the
+        // partner run by binary search (the two halves [0, NT) and
+        // [NT, 2 NT) of the selection buffer in turn, sel_cap >= 2 NT). Two
+        // log-probs of a row that round to one raw score with their tokens
+        // the other way round break a run's order; then the keys are
+        // gathered and sorted by a bitonic network instead. At most NT keys
+        // are taken (gather_cap), one per thread.
         {
-            // Rank of each gathered key = the gathered keys above it (keys
-            // are unique); those below N move to their slot. Every thread
-            // reads the same key at a time (shared-memory broadcast).
-            const int g = sh_g;
-            uint64_t mh_ = 0, ml_ = 0;
-            int rank = 0;
-            if (tid < g) {
-                mh_ = sh[tid];
-                ml_ = sl[tid];
-                int j = 0;
-                for (; j + 4 <= g; j += 4) {
+            int* run_cnt = next_len;      // [runs], zeroed with the step's loads; free until the outputs
+            int* run_off = ended_next;    // [runs]
+            const int runs = long0 ? 1 : K;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) rank += key2_less(mh_, ml_, sh[j + q], sl[j + q]) ? 1 : 0;
+            for (int u = 0; u < kLmPer; ++u) {
+                if (tk[u]) {
+                    const int idx = tid + u * NT;
+                    atomicAdd(run_cnt + (long0 ? 0 : idx / C), 1);
                 }
-                for (; j < g; ++j) rank += key2_less(mh_, ml_, sh[j], sl[j]) ? 1 : 0;
             }
             __syncthreads();
-            if (tid < g && rank < N) {
-                sh[rank] = mh_;
-                sl[rank] = ml_;
-            }
-            // keys past the first N are not part of the step (the buffer
-            // beyond them is the rescans' staging area, kept zero)
-            const int lim = g > N ? g : N;
-            for (int i = tid; i < lim; i += NT) {
-                if (i >= g && i < N) { sh[i] = 0; sl[i] = 0; }   // fewer than N candidates
-                if (i >= N) { sh[i] = 0; sl[i] = 0; }
+            if (wid == 0) {   // exclusive prefix of the run lengths
+                int acc = 0;
+                for (int b = 0; b < runs; b += 32) {
+                    const int k = b + lane;
+                    const int c = k < runs ? run_cnt[k] : 0;
+                    int incl = c;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int v = __shfl_up_sync(FULL, incl, o);
+                        if (lane >= o) incl += v;
+                    }
+                    if (k < runs) run_off[k] = acc + incl - c;
+                    acc += __shfl_sync(FULL, incl, 31);
+                }
+                if (lane == 0) sh_g = acc;
             }
             __syncthreads();
+            const int g = sh_g;
+            auto off_of = [&](int r) { return r < runs ? run_off[r] : g; };
+            bool bad = false;
+#pragma unroll
+            for (int u = 0; u < kLmPer; ++u) {
+                if (tk[u]) {
+                    const int idx = tid + u * NT;
+                    const int k = long0 ? 0 : idx / C;
+                    const int i = idx - k * C;
+                    if (i >= run_cnt[k]) {
+                        bad = true;   // the taken entries of the row are not its first ones
+                    } else {
+                        sh[run_off[k] + i] = ch[u];
+                        sl[run_off[k] + i] = cand_lo_of(u);
+                    }
+                }
+            }
+            bool merged = false;
+            if (!__syncthreads_or(bad)) {
+                uint64_t kh = 0, kl = 0;
+                int kr = 0, pos = tid;
+                if (tid < g) {
+                    kh = sh[tid];
+                    kl = sl[tid];
+                    kr = long0 ? 0 : cand_parent(kl);
+                    if (tid > run_off[kr] && !key2_less(kh, kl, sh[tid - 1], sl[tid - 1])) bad = true;
+                }
+                if (!__syncthreads_or(bad)) {
+                    int cur = 0;
+                    for (int span = 1; span < runs; span <<= 1) {
+                        if (tid < g) {
+                            const int grp = kr / span;
+                            const int part = grp ^ 1;
+                            const uint64_t* bh = sh + cur * NT;
+                            const uint64_t* bl = sl + cur * NT;
+                            const int p0 = off_of(part * span);
+                            int lo = p0, hi = off_of((part + 1) * span);
+                            while (lo < hi) {   // partner keys above this one
+                                const int mid = (lo + hi) >> 1;
+                                if (key2_less(kh, kl, bh[mid], bl[mid])) lo = mid + 1;
+                                else hi = mid;
+                            }
+                            pos = off_of((grp & ~1) * span) + (pos - off_of(grp * span)) + (lo - p0);
+                            sh[(cur ^ 1) * NT + pos] = kh;
+                            sl[(cur ^ 1) * NT + pos] = kl;
+                        }
+                        cur ^= 1;
+                        __syncthreads();
+                    }
+                    // the first N keys are the step's; the buffer beyond them
+                    // is the rescans' staging area, kept zero
+                    if (tid < g && pos < N) {
+                        sh[pos] = kh;
+                        sl[pos] = kl;
+                    }
+                    for (int i = (g < N ? g : N) + tid; i < 2 * NT; i += NT) {
+                        sh[i] = 0;
+                        sl[i] = 0;
+                    }
+                    __syncthreads();
+                    merged = true;
+                }
+            }
+            if (!merged) {
+                if (tid == 0) sh_g = 0;
+                __syncthreads();
+                // gather (one shared atomic per warp), then sort
+                unsigned bal[kLmPer];
+                int wtot = 0;
+#pragma unroll
+                for (int u = 0; u < kLmPer; ++u) {
+                    bal[u] = __ballot_sync(FULL, tk[u]);
+                    wtot += __popc(bal[u]);
+                }
+                int base = 0;
+                if (lane == 0 && wtot) base = atomicAdd(&sh_g, wtot);
+                base = __shfl_sync(FULL, base, 0);
+#pragma unroll
+                for (int u = 0; u < kLmPer; ++u) {
+                    if ((bal[u] >> lane) & 1u) {
+                        const int pos = base + __popc(bal[u] & ((1u << lane) - 1u));
+                        sh[pos] = ch[u];
+                        sl[pos] = cand_lo_of(u);
+                    }
+                    base += __popc(bal[u]);
+                }
+                __syncthreads();
+                lm_sort_registers<NT>(sh, sl, sh_g, N);
+            }
         }
 
         // Exactness proof per truncated row (as in the selection merge): a
@@ -2391,22 +2583,112 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                     for (int i = N + tid; i < n2; i += NT) { sh[i] = 0; sl[i] = 0; }
                     __syncthreads();
                 };
+                // The row's values in token order, by all threads: fp32 rows
+                // take the scalar head up to a 16-byte boundary and the tail by
+                // plain loads and the body as float4 vectors, through the ring
+                // (bulk copies, every stage in flight at once; a stage is
+                // refilled after the block has read it) or by vector loads
+                // without one; 16-bit rows take element loads. fn1(v, lp) gets
+                // one value, fn4(q, v0) the vector of tokens v0 .. v0 + 3.
+                // Returns false after a copy timeout (reported).
+                auto sweep_row = [&](auto&& fn1, auto&& fn4) -> bool {
+                    if (p.x16) {
+                        for (int base = 0; base < V; base += 16 * NT) {
+                            float lv[16];
+#pragma unroll
+                            for (int r = 0; r < 16; ++r) {
+                                const int v = base + r * NT + tid;
+                                lv[r] = v < V ? lp_at(p, row + v) : -INFINITY;
+                            }
+#pragma unroll
+                            for (int r = 0; r < 16; ++r) {
+                                const int v = base + r * NT + tid;
+                                if (v < V) fn1(v, lv[r]);
+                            }
+                        }
+                        return true;
+                    }
+                    const float* rp = p.x + row;
+                    const int head = min(V, static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(rp) & 15u)) & 15u) >> 2));
+                    if (tid < head) fn1(tid, rp[tid]);
+                    const float4* body = reinterpret_cast<const float4*>(rp + head);
+                    const int nv = (V - head) >> 2;
+                    if (rs.stages > 0) {
+                        const int S = rs.stages;
+                        const int nch = (nv + kRescanChunkF4 - 1) / kRescanChunkF4;
+                        auto issue = [&](int c) {   // thread 0
+                            const uint32_t g = rs.seq + static_cast<uint32_t>(c);
+                            const int st = static_cast<int>(g % static_cast<uint32_t>(S));
+                            const int n4 = min(kRescanChunkF4, nv - c * kRescanChunkF4);
+                            mbar_arrive_expect_tx(rs.bar + st, static_cast<uint32_t>(n4) * 16u);
+                            bulk_copy_g2s(rs.stage + static_cast<size_t>(st) * kRescanChunkF4,
+                                          body + static_cast<size_t>(c) * kRescanChunkF4,
+                                          static_cast<uint32_t>(n4) * 16u, rs.bar + st);
+                        };
+                        unsigned long long* err = p.counters ? p.counters + 3 : nullptr;
+                        if (tid == 0)
+                            for (int c = 0; c < nch && c < S; ++c) issue(c);
+                        for (int c = 0; c < nch; ++c) {
+                            const uint32_t g = rs.seq + static_cast<uint32_t>(c);
+                            const int st = static_cast<int>(g % static_cast<uint32_t>(S));
+                            const bool ok = mbar_wait(rs.bar + st, (g / static_cast<uint32_t>(S)) & 1u, err);
+                            if (ok) {
+                                const float4* sv = rs.stage + static_cast<size_t>(st) * kRescanChunkF4;
+                                const int n4 = min(kRescanChunkF4, nv - c * kRescanChunkF4);
+                                for (int i = tid; i < n4; i += NT) fn4(sv[i], head + 4 * (c * kRescanChunkF4 + i));
+                            }
+                            if (__syncthreads_or(!ok)) {
+                                // a copy did not land in time: wait, bounded, for
+                                // the copies still in flight, then give up
+                                if (tid == 0)
+                                    for (int c2 = c + 1; c2 < nch && c2 < c + S; ++c2) {
+                                        const uint32_t g2 = rs.seq + static_cast<uint32_t>(c2);
+                                        mbar_wait(rs.bar + g2 % static_cast<uint32_t>(S),
+                                                  (g2 / static_cast<uint32_t>(S)) & 1u, err);
+                                    }
+                                return false;
+                            }
+                            if (tid == 0 && c + S < nch) {
+                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                                issue(c + S);
+                            }
+                        }
+                        rs.seq += static_cast<uint32_t>(nch);
+                    } else {
+                        for (int base = 0; base < nv; base += 4 * NT) {
+                            float4 q[4];
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) {
+                                const int i = base + r * NT + tid;
+                                q[r] = i < nv ? __ldg(body + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                            }
+#pragma unroll
+                            for (int r = 0; r < 4; ++r) {
+                                const int i = base + r * NT + tid;
+                                if (i < nv) fn4(q[r], head + 4 * i);
+                            }
+                        }
+                    }
+                    const int t0 = head + 4 * nv;
+                    if (t0 + tid < V) fn1(t0 + tid, rp[t0 + tid]);
+                    return true;
+                };
                 // While the step has fewer than N candidates (G empty: step 0 of
                 // a decode whose one live row has a short list), every entry of
                 // the row would win; only entries at or above the row's N-th
-                // largest allowed log-prob can be among the top N, so the floor
-                // is put just below that value, found by a radix select over the
-                // row (8 bits per pass).
+                // largest allowed log-prob can be among the top N. A radix
+                // select over the row (8 bits per pass from the top) narrows a
+                // prefix of ord(lp) until the values at or above it fit the
+                // staging room, and the floor is put just below the prefix.
                 float nth_floor = -INFINITY;
                 if (sh[N - 1] == 0) {
                     uint32_t prefix = 0, mask = 0;
                     int need_r = N;
                     bool enough = true;
-                    for (int shift = 24; shift >= 0; shift -= 8) {
+                    for (int shift = 24;; shift -= 8) {
                         for (int i = tid; i < 256; i += NT) hist[i] = 0;
                         __syncthreads();
-                        for (int v = tid; v < V; v += NT) {
-                            const float lp = lp_at(p, row + v);
+                        auto count = [&](int v, float lp) {
                             int bin = -1;
                             if (isfinite(lp) && !(forced >= 0 && v != forced) && !(d.banned && d.banned[v]) &&
                                 !(eos_blocked && v == d.eos) &&
@@ -2417,7 +2699,14 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                             const unsigned act = __activemask();
                             const unsigned same = __match_any_sync(act, bin);
                             if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(hist + bin, __popc(same));
-                        }
+                        };
+                        const bool ok = sweep_row(count, [&](const float4 q, int v0) {
+                            count(v0, q.x);
+                            count(v0 + 1, q.y);
+                            count(v0 + 2, q.z);
+                            count(v0 + 3, q.w);
+                        });
+                        if (!ok) return false;
                         __syncthreads();
                         if (wid == 0) {
                             int loc[8];
@@ -2441,6 +2730,7 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                                     if (run + loc[j] >= need_r) {
                                         sh_sel[0] = lane * 8 + j;
                                         sh_sel[1] = run;
+                                        sh_sel[2] = loc[j];
                                         break;
                                     }
                                     run += loc[j];
@@ -2450,15 +2740,22 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                         __syncthreads();
                         const int digit = sh_sel[0];
                         const int above = sh_sel[1];
+                        const int group = sh_sel[2];
                         __syncthreads();
                         if (digit < 0) { enough = false; break; }
                         prefix |= static_cast<uint32_t>(digit) << shift;
                         mask |= 0xFFu << shift;
                         need_r -= above;
+                        // the values at or above the prefix: (N - need_r) + group
+                        if (shift == 0 || (N - need_r) + group <= room) break;
                     }
-                    if (enough) nth_floor = nextafterf(unord_f32(prefix), -INFINITY);
+                    if (enough) {
+                        const float edge = unord_f32(prefix);   // the least value with the prefix
+                        nth_floor = isfinite(edge) ? nextafterf(edge, -INFINITY) : -INFINITY;
+                    }
                 }
                 // one sweep against the G of the row's start, no barrier inside
+                // but the ring's
                 {
                     const uint64_t gh = sh[N - 1], gl = sl[N - 1];
                     const float floor_lp = gh == 0 ? nth_floor : floor_of(gh);
@@ -2476,50 +2773,16 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                             sh_over = 1;
                         }
                     };
-                    if (!p.x16) {
-                        // fp32 rows: scalar head up to a 16-byte boundary, then
-                        // four float4 loads per thread in flight; a vector whose
-                        // largest value is at or below the floor is skipped
-                        const float* rp = p.x + row;
-                        const int head = min(V, static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(rp) & 15u)) & 15u) >> 2));
-                        if (tid < head) stage(tid, rp[tid]);
-                        const float4* body = reinterpret_cast<const float4*>(rp + head);
-                        const int nv = (V - head) >> 2;
-                        for (int base = 0; base < nv; base += 4 * NT) {
-                            float4 q[4];
-#pragma unroll
-                            for (int r = 0; r < 4; ++r) {
-                                const int i = base + r * NT + tid;
-                                q[r] = i < nv ? __ldg(body + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-                            }
-#pragma unroll
-                            for (int r = 0; r < 4; ++r) {
-                                const float m4 = fmaxf(fmaxf(q[r].x, q[r].y), fmaxf(q[r].z, q[r].w));
-                                if (!(m4 > floor_lp)) continue;   // (NaN is not finite: never a candidate)
-                                const int v0 = head + 4 * (base + r * NT + tid);
-                                stage(v0, q[r].x);
-                                stage(v0 + 1, q[r].y);
-                                stage(v0 + 2, q[r].z);
-                                stage(v0 + 3, q[r].w);
-                            }
-                        }
-                        const int t0 = head + 4 * nv;
-                        if (t0 + tid < V) stage(t0 + tid, rp[t0 + tid]);
-                    } else {
-                        for (int base = 0; base < V; base += 16 * NT) {
-                            float lv[16];
-#pragma unroll
-                            for (int r = 0; r < 16; ++r) {
-                                const int v = base + r * NT + tid;
-                                lv[r] = v < V ? lp_at(p, row + v) : -INFINITY;
-                            }
-#pragma unroll
-                            for (int r = 0; r < 16; ++r) {
-                                const int v = base + r * NT + tid;
-                                if (v < V) stage(v, lv[r]);
-                            }
-                        }
-                    }
+                    const bool ok = sweep_row(stage, [&](const float4 q, int v0) {
+                        // a vector whose largest value is at or below the floor is skipped
+                        const float m4 = fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w));
+                        if (!(m4 > floor_lp)) return;   // (NaN is not finite: never a candidate)
+                        stage(v0, q.x);
+                        stage(v0 + 1, q.y);
+                        stage(v0 + 2, q.z);
+                        stage(v0 + 3, q.w);
+                    });
+                    if (!ok) return false;
                     __syncthreads();
                 }
                 const int staged = sh_n;
@@ -2625,11 +2888,12 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
 }
 
 template <int NT, int PER>
-__global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int seq_K, int sel_cap) {
+__global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int seq_K, int sel_cap, int rs_stages) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     float* state = p.merge_state ? p.merge_state + static_cast<int64_t>(e) * 4 * seq_K : nullptr;
-    list_merge_body<NT, PER>(p, e, p.t_begin > 0 ? p.t_begin : 0, p.t_end, state, seq_K, sel_cap, smem, nullptr);
+    RescanRing rs = rescan_ring_init<NT>(smem, sel_cap, seq_K, rs_stages);
+    list_merge_body<NT, PER>(p, e, p.t_begin > 0 ? p.t_begin : 0, p.t_end, state, seq_K, sel_cap, smem, nullptr, rs);
 }
 
 // ---------------------------------------------------------------------------
@@ -2650,7 +2914,7 @@ __global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int s
 template <int PER>
 __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodeParams p, int capw, int seq_K,
                                                                       int sel_cap, int merge_ctas,
-                                                                      unsigned int* step_done) {
+                                                                      unsigned int* step_done, int rs_stages) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     if (static_cast<int>(blockIdx.x) >= merge_ctas) {
         row_scan_body<false, true>(p, capw, 1, smem_raw, step_done);
@@ -2666,14 +2930,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodePa
     __syncthreads();
     if (sh_bad) return;
     const int T = p.desc[0].T;
+    RescanRing rs = rescan_ring_init<kFusedThreads>(smem_raw, sel_cap, seq_K, rs_stages);
     if (merge_ctas >= p.B) {
-        list_merge_body<kFusedThreads, PER>(p, blockIdx.x, 0, T, nullptr, seq_K, sel_cap, smem_raw, step_done);
+        list_merge_body<kFusedThreads, PER>(p, blockIdx.x, 0, T, nullptr, seq_K, sel_cap, smem_raw, step_done, rs);
         return;
     }
     for (int t = 0; t < T; ++t) {
         for (int e = blockIdx.x; e < p.B; e += merge_ctas) {
             float* state = p.merge_state + static_cast<int64_t>(e) * 4 * seq_K;
-            if (!list_merge_body<kFusedThreads, PER>(p, e, t, t + 1, state, seq_K, sel_cap, smem_raw, step_done))
+            if (!list_merge_body<kFusedThreads, PER>(p, e, t, t + 1, state, seq_K, sel_cap, smem_raw, step_done, rs))
                 return;
         }
     }
@@ -3853,18 +4118,19 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
         }
     }
     const int M = max_K * max_C;
-    if (!need_sequences && M <= kListMergeMaxCandidates && max_N <= 1024 && list_merge_enabled()) {
+    if (!need_sequences && M <= kListMergeMaxCandidates && max_N <= kListMergeThreads && list_merge_enabled()) {
         // compact merge: candidate keys in registers, radix select, one sort
         constexpr int nt = kListMergeThreads;
         const int sel_cap = list_merge_sel_cap(max_N, nt);
-        const size_t smem = list_merge_smem(nt, sel_cap, max_K);
+        const int stages = kRescanMaxStages;   // one CTA per SM either way (registers)
+        const size_t smem = list_merge_total_smem(nt, sel_cap, max_K, stages);
         const bool small = M <= nt * 4;
         const void* fn = small ? reinterpret_cast<const void*>(list_merge_kernel<nt, 4>)
                                : reinterpret_cast<const void*>(list_merge_kernel<nt, 8>);
         cudaError_t err = ensure_dynamic_smem(fn, smem);
         if (err != cudaSuccess) return err;
-        if (small) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
-        else list_merge_kernel<nt, 8><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
+        if (small) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap, stages);
+        else list_merge_kernel<nt, 8><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap, stages);
         return counted(cudaGetLastError());
     }
     int cand_cap = M;
@@ -3908,11 +4174,12 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
 cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int max_N, int merge_ctas,
                                 unsigned int* step_done, int num_sms, cudaStream_t stream) {
     const int M = max_K * max_C;
-    if (M > 8 * kFusedThreads || max_N > 1024 || merge_ctas < 1 || max_C > 128) return cudaErrorNotSupported;
+    if (M > 8 * kFusedThreads || max_N > kFusedThreads || merge_ctas < 1 || max_C > 128) return cudaErrorNotSupported;
     const int capw = row_scan_capw(max_C);
     const int sel_cap = list_merge_sel_cap(max_N, kFusedThreads);
     size_t smem = static_cast<size_t>(kFusedThreads / 32) * row_scan_warp_bytes(capw, false);
-    const size_t msmem = list_merge_smem(kFusedThreads, sel_cap, max_K);
+    const int stages = kRescanMaxStages;   // one CTA per SM either way (registers)
+    const size_t msmem = list_merge_total_smem(kFusedThreads, sel_cap, max_K, stages);
     if (msmem > smem) smem = msmem;
     const bool small = M <= kFusedThreads * 4;
     const void* fn = small ? reinterpret_cast<const void*>(fused_decode_kernel<4>)
@@ -3925,9 +4192,9 @@ cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int
     const int grid = per_sm * num_sms;
     if (per_sm < 1 || grid <= merge_ctas) return cudaErrorNotSupported;
     DecodeParams pp = p;
-    int a_capw = capw, a_seq = max_K, a_sel = sel_cap, a_m = merge_ctas;
+    int a_capw = capw, a_seq = max_K, a_sel = sel_cap, a_m = merge_ctas, a_st = stages;
     unsigned int* a_done = step_done;
-    void* args[] = {&pp, &a_capw, &a_seq, &a_sel, &a_m, &a_done};
+    void* args[] = {&pp, &a_capw, &a_seq, &a_sel, &a_m, &a_done, &a_st};
     err = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kFusedThreads), args, smem, stream);
     return counted(err);
 }

@@ -528,7 +528,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         // on the one merge CTA's critical path
         fused_C = std::min(list_capacity_for(N0, K0, false), B >= 8 ? kShortListEntries : 2 * kShortListEntries);
         const int64_t M0 = static_cast<int64_t>(K0) * fused_C;
-        fused = uni && ex[0].T >= 2 && M0 > 256 && M0 <= dbs_dev::kListMergeMaxCandidates && N0 <= 1024;
+        fused = uni && ex[0].T >= 2 && M0 > 256 && M0 <= dbs_dev::kListMergeMaxCandidates && N0 <= dbs_dev::kFusedThreads;
     }
     if (fused) short_lists = false;
 

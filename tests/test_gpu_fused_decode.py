@@ -9,7 +9,8 @@ step's rows are listed, so the merge follows the scan instead of waiting for
 it. Row lists hold at most 64 entries and step 0's one live row is completed
 by the merge (a radix-selected floor over the row). These cases check every
 example against the oracle, bit-exact: step counts that do not divide, EOS
-and length penalty, pools of 512 from 8 beams, a rejected input (the launch
+and length penalty, pools of 512 from 8 beams (and of 1024, which take the
+separate launches), a rejected input (the launch
 writes no output) followed by good decodes, a workspace that holds an
 earlier call's lists, and the sparse backward from the fused trace; plus the
 paths beside it (sequence constraints and 16-bit rows, which keep separate
@@ -51,6 +52,7 @@ def _check_host_batch(lib, orc, opts, x, backward_examples=()):
     (4, 17, 32, 300, 8, 0.0, -1),    # 3-step segments, the last one 2 steps
     (6, 40, 16, 257, 8, 0.4, 3),     # 5-step segments, EOS carries and length penalty
     (3, 16, 8, 500, 64, 0.0, 2),     # pool 512 from 8 beams: 4096 candidates per step
+    (2, 9, 16, 700, 64, 0.2, 3),     # pool 1024 from 16 beams: above the compact merge's 512
 ])
 def test_pipelined_uniform_batch(libdbs, oracle_lib, B, T, K, V, mult, alpha, eos):
     rng = np.random.default_rng(B * 1000 + T)
