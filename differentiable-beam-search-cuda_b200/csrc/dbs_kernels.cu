@@ -1887,18 +1887,18 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
 // registers, so a step needs no shared-memory copy of its K row lists. A
 // radix select over the 128-bit candidate keys (rank, raw, then parent and
 // token; 8 bits per pass from the highest bit where the keys differ)
-// narrows the keys that can be among the top N to at most NT; those form
-// one sorted run per row, which are merged pairwise, and the first N are
-// the step's pool (the same order as the reference's candidate_better,
+// narrows the keys that can be among the top N to at most NT; those are
+// gathered and ranked by counting, and the first N are the step's pool (the
+// same order as the reference's candidate_better,
 // src/differentiable_beam.cpp:291-298). The exactness proof and the
 // rescans of truncated rows follow the selection merge.
 // ---------------------------------------------------------------------------
 
-// Shared memory of list_merge_body: selection keys, the histogram and ten
-// per-beam arrays; then, 128-byte aligned, the rescans' ring of row stages
-// and their barriers.
+// Shared memory of list_merge_body: selection keys and their rank words, the
+// histogram and ten per-beam arrays; then, 128-byte aligned, the rescans'
+// ring of row stages and their barriers.
 __host__ __device__ constexpr size_t list_merge_smem(int nt, int sel_cap, int max_K) {
-    return static_cast<size_t>(sel_cap) * 2 * sizeof(uint64_t) + 256 * sizeof(int) +
+    return static_cast<size_t>(sel_cap) * (2 * sizeof(uint64_t) + sizeof(uint32_t)) + 256 * sizeof(int) +
            static_cast<size_t>(max_K) * 10 * sizeof(int) + 0 * nt;
 }
 constexpr int kRescanChunkF4 = 1024;   // one rescan stage: 16 KB of a row
@@ -1937,61 +1937,6 @@ __device__ __forceinline__ void lm_sort(uint64_t* hi, uint64_t* lo, int n2) {
             __syncthreads();
         }
     }
-}
-
-// Sorts the g <= NT keys in hi/lo[0, g) descending, one per thread, by a
-// bitonic network (strides below 32 by warp shuffles, larger ones through the
-// halves [0, NT) and [NT, 2 NT) of the buffers in turn, one barrier each),
-// leaves the first n in hi/lo[0, n) and zeroes [n, 2 NT). Called by all
-// threads of the block; ends with a barrier.
-template <int NT>
-__device__ __forceinline__ void lm_sort_registers(uint64_t* sh, uint64_t* sl, int g, int N) {
-    constexpr unsigned FULL = 0xFFFFFFFFu;
-    const int tid = threadIdx.x;
-    uint64_t kh = 0, kl = 0;
-    if (tid < g) {
-        kh = sh[tid];
-        kl = sl[tid];
-    }
-    int half = 0;
-    __syncthreads();   // every key is in registers
-#pragma unroll 1
-    for (int size = 2; size <= NT; size <<= 1) {
-#pragma unroll 1
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            uint64_t oh, ol;
-            if (stride >= 32) {
-                uint64_t* bh = sh + half * NT;
-                uint64_t* bl = sl + half * NT;
-                bh[tid] = kh;
-                bl[tid] = kl;
-                __syncthreads();
-                oh = bh[tid ^ stride];
-                ol = bl[tid ^ stride];
-                half ^= 1;
-            } else {
-                oh = __shfl_xor_sync(FULL, kh, stride);
-                ol = __shfl_xor_sync(FULL, kl, stride);
-            }
-            // a descending segment keeps the larger key at the lower index
-            const bool keep_max = ((tid & size) == 0) == ((tid & stride) == 0);
-            const bool take = keep_max ? key2_less(kh, kl, oh, ol) : key2_less(oh, ol, kh, kl);
-            if (take) {
-                kh = oh;
-                kl = ol;
-            }
-        }
-    }
-    __syncthreads();   // the last exchange's reads are done
-    if (tid < N) {
-        sh[tid] = kh;
-        sl[tid] = kl;
-    }
-    for (int i = N + tid; i < 2 * NT; i += NT) {
-        sh[i] = 0;
-        sl[i] = 0;
-    }
-    __syncthreads();
 }
 
 // Ring of row stages for the rescans of list_merge_body (stages 0 to
@@ -2061,7 +2006,8 @@ __device__ __forceinline__ bool wait_step_rows(const DecodeParams& p, const unsi
 template <int NT, int PER>
 __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, int t_first, int t_stop, float* state,
                                                 int seq_K, int sel_cap, unsigned char* smem,
-                                                const unsigned int* step_done, RescanRing& rs) {
+                                                const unsigned int* step_done, RescanRing& rs,
+                                                float* beams = nullptr, bool fresh = true) {
     constexpr int NW = NT / 32;
     constexpr unsigned FULL = 0xFFFFFFFFu;
     constexpr int kLmPer = PER;
@@ -2071,15 +2017,21 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     uint64_t* sh = reinterpret_cast<uint64_t*>(smem);   // [sel_cap] selection / sort keys (high words)
     uint64_t* sl = sh + sel_cap;                         // [sel_cap] low words
-    int* hist = reinterpret_cast<int*>(sl + sel_cap);    // [256]
+    uint32_t* sr = reinterpret_cast<uint32_t*>(sl + sel_cap);   // [sel_cap] rank words of the gathered keys
+    int* hist = reinterpret_cast<int*>(sr + sel_cap);    // [256]
     float* prev_raw = reinterpret_cast<float*>(hist + 256);
     float* next_raw = prev_raw + seq_K;
+    int* prev_len = reinterpret_cast<int*>(prev_raw + 4 * seq_K);
+    int* ended = prev_len + 2 * seq_K;
+    if (beams) {   // the example's beams kept in the caller's shared memory between calls
+        prev_raw = beams;
+        prev_len = reinterpret_cast<int*>(beams + seq_K);
+        ended = reinterpret_cast<int*>(beams + 2 * seq_K);
+    }
     float* row_bound = next_raw + seq_K;
     float* row_inv = row_bound + seq_K;
-    int* prev_len = reinterpret_cast<int*>(row_inv + seq_K);
-    int* next_len = prev_len + seq_K;
-    int* ended = next_len + seq_K;
-    int* ended_next = ended + seq_K;
+    int* next_len = reinterpret_cast<int*>(row_inv + 2 * seq_K);
+    int* ended_next = next_len + 2 * seq_K;
     int* row_cnt = ended_next + seq_K;
     int* unsafe = row_cnt + seq_K;
     __shared__ int sh_n;
@@ -2092,11 +2044,11 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
     if (t_stop > T) t_stop = T;
     __syncthreads();   // the block's previous call is done with the shared arrays
     for (int k = tid; k < K; k += NT) {
-        if (t_first > 0 && state) {
+        if (t_first > 0 && state && !beams) {
             prev_raw[k] = state[k];
             prev_len[k] = __float_as_int(state[seq_K + k]);
             ended[k] = __float_as_int(state[2 * seq_K + k]);
-        } else {
+        } else if (t_first == 0) {
             prev_raw[k] = (k == 0) ? 0.0f : -INFINITY;
             prev_len[k] = 0;
             ended[k] = 0;
@@ -2106,8 +2058,9 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
     while (sort_n2 < sel_cap) sort_n2 <<= 1;   // sel_cap is a power of two
     const int M = K * C;
     // the selection buffer past the top N is the rescans' staging area and
-    // is kept zero from here on (the sorts read it)
-    for (int i = tid; i < sort_n2; i += NT) { sh[i] = 0; sl[i] = 0; }
+    // is kept zero from here on (the sorts read it; every step leaves it so)
+    if (fresh)
+        for (int i = tid; i < sort_n2; i += NT) { sh[i] = 0; sl[i] = 0; }
 
     for (int t = t_first; t < t_stop; ++t) {
         const int64_t row0 = d.row_begin + static_cast<int64_t>(t) * K;
@@ -2131,7 +2084,8 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
             row_bound[k] = __ldcg(p.list_bound + row0 + k);
             row_inv[k] = p.inv_pen[prev_len[k] + 1];
             unsafe[k] = 0;
-            next_len[k] = 0;   // the run lengths of the sort
+            next_raw[k] = INFINITY;   // the lp and token of the row's last listed entry (rescans)
+            next_len[k] = -1;
         }
         if (tid == 0) { sh_n = 0; sh_g = 0; sh_any = 0; }
         for (int i = tid; i < 256; i += NT) hist[i] = 0;   // the first radix pass
@@ -2147,6 +2101,10 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                 if (idx < M) {
                     const int k = long0 ? 0 : idx / C;
                     const int i = idx - k * C;
+                    if (i == row_cnt[k] - 1) {
+                        next_raw[k] = list_lp(raw_e[u]);
+                        next_len[k] = list_token(raw_e[u]);
+                    }
                     if (!(i < row_cnt[k] && isfinite(prev_raw[k]) && !(use_eos && ended[k]))) raw_e[u] = 0;
                 }
             }
@@ -2187,9 +2145,11 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
 
         // Radix select: the masked prefix (ph, pl) that the top-N keys reach
         uint64_t ph = 0, pl = 0, mh = 0, ml = 0;   // prefix and mask over (hi, lo)
-        // the gathered keys are sorted one per thread, so at most NT of them
+        // the gathered keys are ranked by counting (g x g comparisons), one
+        // per thread at the end, so at most NT of them; fewer when the
+        // radix passes can get there
         const int gather_cap = NT < sel_cap ? NT : sel_cap;
-        const int gather_goal = gather_cap;
+        const int gather_goal = N + 128 < gather_cap ? N + 128 : gather_cap;
         int need = N;
         int total = 0;
         {
@@ -2329,134 +2289,115 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
             }
             tk[u] = take;
         }
-        // Sort them, descending. They form one run per parent row (the
-        // row's first entries: a row list is in decreasing key order), so
-        // each run is placed at its offset and the runs are merged pairwise
-        // in ceil(log2 runs) rounds, each key finding its place in the
-        // partner run by binary search (the two halves [0, NT) and
-        // [NT, 2 NT) of the selection buffer in turn, sel_cap >= 2 NT). Two
-        // log-probs of a row that round to one raw score with their tokens
-        // the other way round break a run's order; then the keys are
-        // gathered and sorted by a bitonic network instead. At most NT keys
-        // are taken (gather_cap), one per thread.
+        // Gather them (one shared atomic per warp) with their rank words,
+        // and clear the counts of the ranking.
+        int* rank_cnt = reinterpret_cast<int*>(sh + NT);   // [NT]: greater | equal << 16 (sel_cap >= 2 NT)
+        for (int i = tid; i < NT; i += NT) rank_cnt[i] = 0;
+        if (tid == 0) sh_n = 0;   // the count of tied keys below (the radix total is read)
         {
-            int* run_cnt = next_len;      // [runs], zeroed with the step's loads; free until the outputs
-            int* run_off = ended_next;    // [runs]
-            const int runs = long0 ? 1 : K;
+            unsigned bal[kLmPer];
+            int wtot = 0;
 #pragma unroll
             for (int u = 0; u < kLmPer; ++u) {
-                if (tk[u]) {
-                    const int idx = tid + u * NT;
-                    atomicAdd(run_cnt + (long0 ? 0 : idx / C), 1);
-                }
+                bal[u] = __ballot_sync(FULL, tk[u]);
+                wtot += __popc(bal[u]);
             }
-            __syncthreads();
-            if (wid == 0) {   // exclusive prefix of the run lengths
-                int acc = 0;
-                for (int b = 0; b < runs; b += 32) {
-                    const int k = b + lane;
-                    const int c = k < runs ? run_cnt[k] : 0;
-                    int incl = c;
+            int base = 0;
+            if (lane == 0 && wtot) base = atomicAdd(&sh_g, wtot);
+            base = __shfl_sync(FULL, base, 0);
 #pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const int v = __shfl_up_sync(FULL, incl, o);
-                        if (lane >= o) incl += v;
-                    }
-                    if (k < runs) run_off[k] = acc + incl - c;
-                    acc += __shfl_sync(FULL, incl, 31);
+            for (int u = 0; u < kLmPer; ++u) {
+                if ((bal[u] >> lane) & 1u) {
+                    const int pos = base + __popc(bal[u] & ((1u << lane) - 1u));
+                    sh[pos] = ch[u];
+                    sl[pos] = cand_lo_of(u);
+                    sr[pos] = static_cast<uint32_t>(ch[u] >> 32);
                 }
-                if (lane == 0) sh_g = acc;
+                base += __popc(bal[u]);
             }
-            __syncthreads();
+        }
+        __syncthreads();
+        {
+            // Rank of each gathered key = the gathered keys above it (keys
+            // are unique). The g x g comparisons of rank words are cut into
+            // work items of (key, 64 words) spread over all threads, four
+            // words per broadcast load, counting the greater and the equal
+            // words without branches; the items' counts add up in shared
+            // memory. A key whose rank word is shared by another (rare)
+            // compares the full keys of those. The first N keys move to
+            // their slots.
             const int g = sh_g;
-            auto off_of = [&](int r) { return r < runs ? run_off[r] : g; };
-            bool bad = false;
-#pragma unroll
-            for (int u = 0; u < kLmPer; ++u) {
-                if (tk[u]) {
-                    const int idx = tid + u * NT;
-                    const int k = long0 ? 0 : idx / C;
-                    const int i = idx - k * C;
-                    if (i >= run_cnt[k]) {
-                        bad = true;   // the taken entries of the row are not its first ones
-                    } else {
-                        sh[run_off[k] + i] = ch[u];
-                        sl[run_off[k] + i] = cand_lo_of(u);
-                    }
+            constexpr int kChunk = 64;
+            const int parts = (g + kChunk - 1) / kChunk;
+            const uint4* sr4 = reinterpret_cast<const uint4*>(sr);
+            for (int item = tid; item < parts * g; item += NT) {
+                const int part = item / g;
+                const int i = item - part * g;
+                const uint32_t r = sr[i];
+                const int j1 = min(g, (part + 1) * kChunk);
+                int gt = 0, eq = 0;
+                int j = part * kChunk;
+                for (; j + 4 <= j1; j += 4) {
+                    const uint4 w = sr4[j >> 2];
+                    gt += (w.x > r ? 1 : 0) + (w.y > r ? 1 : 0) + (w.z > r ? 1 : 0) + (w.w > r ? 1 : 0);
+                    eq += (w.x == r ? 1 : 0) + (w.y == r ? 1 : 0) + (w.z == r ? 1 : 0) + (w.w == r ? 1 : 0);
+                }
+                for (; j < j1; ++j) {
+                    gt += sr[j] > r ? 1 : 0;
+                    eq += sr[j] == r ? 1 : 0;
+                }
+                atomicAdd(rank_cnt + i, gt | (eq << 16));
+            }
+            __syncthreads();
+            // keys whose rank word another key shares: one warp each counts
+            // the keys with that word above it
+            constexpr int kTieCap = 64;
+            __shared__ int sh_tie[kTieCap];
+            if (tid < g && (rank_cnt[tid] >> 16) > 1) {
+                const int q = atomicAdd(&sh_n, 1);
+                if (q < kTieCap) {
+                    sh_tie[q] = tid;
+                } else {
+                    const uint32_t r = sr[tid];
+                    int add = 0;
+                    for (int j = 0; j < g; ++j)
+                        if (sr[j] == r) add += key2_less(sh[tid], sl[tid], sh[j], sl[j]) ? 1 : 0;
+                    atomicAdd(rank_cnt + tid, add);
                 }
             }
-            bool merged = false;
-            if (!__syncthreads_or(bad)) {
-                uint64_t kh = 0, kl = 0;
-                int kr = 0, pos = tid;
-                if (tid < g) {
-                    kh = sh[tid];
-                    kl = sl[tid];
-                    kr = long0 ? 0 : cand_parent(kl);
-                    if (tid > run_off[kr] && !key2_less(kh, kl, sh[tid - 1], sl[tid - 1])) bad = true;
-                }
-                if (!__syncthreads_or(bad)) {
-                    int cur = 0;
-                    for (int span = 1; span < runs; span <<= 1) {
-                        if (tid < g) {
-                            const int grp = kr / span;
-                            const int part = grp ^ 1;
-                            const uint64_t* bh = sh + cur * NT;
-                            const uint64_t* bl = sl + cur * NT;
-                            const int p0 = off_of(part * span);
-                            int lo = p0, hi = off_of((part + 1) * span);
-                            while (lo < hi) {   // partner keys above this one
-                                const int mid = (lo + hi) >> 1;
-                                if (key2_less(kh, kl, bh[mid], bl[mid])) lo = mid + 1;
-                                else hi = mid;
-                            }
-                            pos = off_of((grp & ~1) * span) + (pos - off_of(grp * span)) + (lo - p0);
-                            sh[(cur ^ 1) * NT + pos] = kh;
-                            sl[(cur ^ 1) * NT + pos] = kl;
-                        }
-                        cur ^= 1;
-                        __syncthreads();
-                    }
-                    // the first N keys are the step's; the buffer beyond them
-                    // is the rescans' staging area, kept zero
-                    if (tid < g && pos < N) {
-                        sh[pos] = kh;
-                        sl[pos] = kl;
-                    }
-                    for (int i = (g < N ? g : N) + tid; i < 2 * NT; i += NT) {
-                        sh[i] = 0;
-                        sl[i] = 0;
-                    }
-                    __syncthreads();
-                    merged = true;
-                }
+            __syncthreads();
+            const int ties = sh_n < kTieCap ? sh_n : kTieCap;
+            for (int q = wid; q < ties; q += NW) {
+                const int i = sh_tie[q];
+                const uint32_t r = sr[i];
+                const uint64_t ih = sh[i], il = sl[i];
+                int add = 0;
+                for (int j = lane; j < g; j += 32)
+                    if (sr[j] == r) add += key2_less(ih, il, sh[j], sl[j]) ? 1 : 0;
+                add = warp_isum(add);
+                if (lane == 0) atomicAdd(rank_cnt + i, add);
             }
-            if (!merged) {
-                if (tid == 0) sh_g = 0;
-                __syncthreads();
-                // gather (one shared atomic per warp), then sort
-                unsigned bal[kLmPer];
-                int wtot = 0;
-#pragma unroll
-                for (int u = 0; u < kLmPer; ++u) {
-                    bal[u] = __ballot_sync(FULL, tk[u]);
-                    wtot += __popc(bal[u]);
-                }
-                int base = 0;
-                if (lane == 0 && wtot) base = atomicAdd(&sh_g, wtot);
-                base = __shfl_sync(FULL, base, 0);
-#pragma unroll
-                for (int u = 0; u < kLmPer; ++u) {
-                    if ((bal[u] >> lane) & 1u) {
-                        const int pos = base + __popc(bal[u] & ((1u << lane) - 1u));
-                        sh[pos] = ch[u];
-                        sl[pos] = cand_lo_of(u);
-                    }
-                    base += __popc(bal[u]);
-                }
-                __syncthreads();
-                lm_sort_registers<NT>(sh, sl, sh_g, N);
+            __syncthreads();
+            uint64_t kh = 0, kl = 0;
+            int rank = 0;
+            if (tid < g) {
+                kh = sh[tid];
+                kl = sl[tid];
+                rank = rank_cnt[tid] & 0xFFFF;
             }
+            if (tid == 0) sh_n = 0;
+            __syncthreads();
+            // the buffer beyond the first N keys is the rescans' staging
+            // area, kept zero
+            if (tid < g && rank < N) {
+                sh[rank] = kh;
+                sl[rank] = kl;
+            }
+            for (int i = (g < N ? g : N) + tid; i < 2 * NT; i += NT) {
+                sh[i] = 0;
+                sl[i] = 0;
+            }
+            __syncthreads();
         }
 
         // Exactness proof per truncated row (as in the selection merge): a
@@ -2493,15 +2434,9 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                 const float pr = prev_raw[k];
                 const float inv = row_inv[k];
                 const int64_t row = d.x_offset + (static_cast<int64_t>(t) * d.k_stride + k) * V;
-                const int cnt = row_cnt[k];
-                float m_lp = INFINITY;
-                int m_tok = -1;
-                if (cnt > 0) {
-                    const uint64_t last =
-                        __ldcg(reinterpret_cast<const unsigned long long*>(step_lists) + static_cast<int64_t>(k) * C + (cnt - 1));
-                    m_lp = list_lp(last);
-                    m_tok = list_token(last);
-                }
+                // the row's last listed entry (INFINITY / -1 for an empty list)
+                const float m_lp = next_raw[k];
+                const int m_tok = next_len[k];
                 // The candidate of token v if the scan dropped it and it beats
                 // G = (gh, gl); 0 otherwise.
                 auto winner = [&](int v, float lp, float floor_lp, uint64_t gh, uint64_t gl, uint64_t& l) -> uint64_t {
@@ -2866,8 +2801,8 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
         }
     }
     __syncthreads();
-    if (t_stop < T) {   // more steps follow in a later launch: keep the state
-        if (state) {
+    if (t_stop < T) {   // more steps follow in a later call: keep the state
+        if (state && !beams) {
             for (int k = tid; k < K; k += NT) {
                 state[k] = prev_raw[k];
                 state[seq_K + k] = __int_as_float(prev_len[k]);
@@ -2935,10 +2870,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodePa
         list_merge_body<kFusedThreads, PER>(p, blockIdx.x, 0, T, nullptr, seq_K, sel_cap, smem_raw, step_done, rs);
         return;
     }
+    // examples in turn, one step at a time, each one's beams in shared memory
+    float* beams_area = reinterpret_cast<float*>(smem_raw + list_merge_total_smem(kFusedThreads, sel_cap, seq_K, rs_stages));
     for (int t = 0; t < T; ++t) {
-        for (int e = blockIdx.x; e < p.B; e += merge_ctas) {
-            float* state = p.merge_state + static_cast<int64_t>(e) * 4 * seq_K;
-            if (!list_merge_body<kFusedThreads, PER>(p, e, t, t + 1, state, seq_K, sel_cap, smem_raw, step_done, rs))
+        int j = 0;
+        for (int e = blockIdx.x; e < p.B; e += merge_ctas, ++j) {
+            float* beams = beams_area + static_cast<size_t>(j) * 3 * seq_K;
+            if (!list_merge_body<kFusedThreads, PER>(p, e, t, t + 1, nullptr, seq_K, sel_cap, smem_raw, step_done, rs,
+                                                     beams, t == 0 && j == 0))
                 return;
         }
     }
@@ -4179,8 +4118,12 @@ cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int
     const int sel_cap = list_merge_sel_cap(max_N, kFusedThreads);
     size_t smem = static_cast<size_t>(kFusedThreads / 32) * row_scan_warp_bytes(capw, false);
     const int stages = kRescanMaxStages;   // one CTA per SM either way (registers)
-    const size_t msmem = list_merge_total_smem(kFusedThreads, sel_cap, max_K, stages);
+    // a merge CTA with several examples keeps their beams after its ring
+    const int per_cta = (p.B + merge_ctas - 1) / merge_ctas;
+    const size_t msmem = list_merge_total_smem(kFusedThreads, sel_cap, max_K, stages) +
+                         (per_cta > 1 ? static_cast<size_t>(per_cta) * 3 * max_K * sizeof(float) : 0);
     if (msmem > smem) smem = msmem;
+    if (smem > static_cast<size_t>(227) * 1024) return cudaErrorNotSupported;
     const bool small = M <= kFusedThreads * 4;
     const void* fn = small ? reinterpret_cast<const void*>(fused_decode_kernel<4>)
                            : reinterpret_cast<const void*>(fused_decode_kernel<8>);
