@@ -749,6 +749,12 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
 // The row-scan loop of one warp (per-warp shared memory at smem_raw + warp
 // index * row_scan_warp_bytes). With step_done, each finished row (its list,
 // count and bound written and fenced) adds one to step_done[e * T + t].
+// Speculative thresholds of long lists left by the warps that last ran out
+// of rows in a row-scan launch on this device, (list length << 32) | lp bits
+// per slot: a launch's warps start from them instead of from nothing (a row
+// whose list a guess cuts short is scanned again, so any value is safe).
+__device__ unsigned long long g_spec_seed[kSpecSlots];
+
 __device__ __forceinline__ void scan_row_done(unsigned int* step_done, int idx, int lane) {
     __threadfence();
     __syncwarp();
@@ -778,9 +784,20 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
     if (lane == 0) {
         for (int s = 0; s < kScanStages; ++s) mbar_init(full + s, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int s = 0; s < kSpecSlots; ++s) spec_len[s] = 0;
+        for (int s = 0; s < kSpecSlots; ++s) {
+            const unsigned long long seed = g_spec_seed[s];
+            spec_len[s] = static_cast<int>(seed >> 32);
+            spec_lp[s] = __uint_as_float(static_cast<uint32_t>(seed));
+        }
     }
     __syncwarp();
+    // a warp that runs out of rows leaves its thresholds for later launches
+    auto leave_seeds = [&]() {
+        if (lane == 0)
+            for (int s = 0; s < kSpecSlots; ++s)
+                if (spec_len[s] > 0)
+                    g_spec_seed[s] = (static_cast<unsigned long long>(spec_len[s]) << 32) | __float_as_uint(spec_lp[s]);
+    };
 
     // Claim index -> row (kNoRow once this launch's claims are used up).
     constexpr int64_t kNoRow = INT64_MAX;
@@ -1171,7 +1188,10 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
         if (!inxt) {
             // nothing of the next row was issued yet (nor claimed)
             const int64_t rn = claim();
-            if (rn == kNoRow) return;
+            if (rn == kNoRow) {
+                leave_seeds();
+                return;
+            }
             nxt = make_job<k16, kFused>(p, rn, e_nxt);
             cursor_to(nxt);
         }
