@@ -1915,20 +1915,10 @@ __global__ void __launch_bounds__(kMergeThreads, 1) step_merge_kernel(DecodePara
 // ---------------------------------------------------------------------------
 
 // Shared memory of list_merge_body: selection keys and their rank words, the
-// histogram and ten per-beam arrays; then, 128-byte aligned, the rescans'
-// ring of row stages and their barriers.
+// histogram and ten per-beam arrays.
 __host__ __device__ constexpr size_t list_merge_smem(int nt, int sel_cap, int max_K) {
     return static_cast<size_t>(sel_cap) * (2 * sizeof(uint64_t) + sizeof(uint32_t)) + 256 * sizeof(int) +
            static_cast<size_t>(max_K) * 10 * sizeof(int) + 0 * nt;
-}
-constexpr int kRescanChunkF4 = 1024;   // one rescan stage: 16 KB of a row
-constexpr int kRescanMaxStages = 8;
-__host__ __device__ constexpr size_t list_merge_ring_at(int nt, int sel_cap, int max_K) {
-    return (list_merge_smem(nt, sel_cap, max_K) + 127) & ~static_cast<size_t>(127);
-}
-__host__ __device__ constexpr size_t list_merge_total_smem(int nt, int sel_cap, int max_K, int stages) {
-    return list_merge_ring_at(nt, sel_cap, max_K) +
-           static_cast<size_t>(stages) * (kRescanChunkF4 * 16 + sizeof(uint64_t));
 }
 // Selection buffer: a power of two with room for the top N plus a staging
 // area of at least 256 and of at least one value per thread (rescans).
@@ -1957,32 +1947,6 @@ __device__ __forceinline__ void lm_sort(uint64_t* hi, uint64_t* lo, int n2) {
             __syncthreads();
         }
     }
-}
-
-// Ring of row stages for the rescans of list_merge_body (stages 0 to
-// kRescanMaxStages of kRescanChunkF4 float4 each, at list_merge_ring_at(),
-// one mbarrier per stage after them). seq counts the stages consumed so far,
-// which gives each stage's next phase. Owned by the kernel: set up once by
-// rescan_ring_init, published by the block barrier at the start of
-// list_merge_body.
-struct RescanRing {
-    float4* stage;
-    uint64_t* bar;
-    int stages;
-    uint32_t seq;
-};
-template <int NT>
-__device__ __forceinline__ RescanRing rescan_ring_init(unsigned char* smem, int sel_cap, int seq_K, int stages) {
-    RescanRing r;
-    r.stages = stages;
-    r.seq = 0;
-    r.stage = reinterpret_cast<float4*>(smem + list_merge_ring_at(NT, sel_cap, seq_K));
-    r.bar = reinterpret_cast<uint64_t*>(r.stage + static_cast<size_t>(stages) * kRescanChunkF4);
-    if (stages > 0 && threadIdx.x == 0) {
-        for (int s = 0; s < stages; ++s) mbar_init(r.bar + s, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    return r;
 }
 
 // Bounded wait of a merge CTA for the K rows of step t of example e
@@ -2020,14 +1984,11 @@ __device__ __forceinline__ bool wait_step_rows(const DecodeParams& p, const unsi
 // example) carries the beams between calls: loaded when t_first > 0,
 // stored when steps remain. With step_done the CTA waits for each step's
 // rows (the fused decode); lists, counts and bounds are read around L1.
-// The rows that fp32 rescans read arrive in rs's 16 KB shared-memory stages
-// by bulk copies, every stage in flight at once; without stages the rescans
-// read the row with vector loads.
 template <int NT, int PER>
 __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, int t_first, int t_stop, float* state,
                                                 int seq_K, int sel_cap, unsigned char* smem,
-                                                const unsigned int* step_done, RescanRing& rs,
-                                                float* beams = nullptr, bool fresh = true) {
+                                                const unsigned int* step_done, float* beams = nullptr,
+                                                bool fresh = true) {
     constexpr int NW = NT / 32;
     constexpr unsigned FULL = 0xFFFFFFFFu;
     constexpr int kLmPer = PER;
@@ -2540,13 +2501,10 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                 };
                 // The row's values in token order, by all threads: fp32 rows
                 // take the scalar head up to a 16-byte boundary and the tail by
-                // plain loads and the body as float4 vectors, through the ring
-                // (bulk copies, every stage in flight at once; a stage is
-                // refilled after the block has read it) or by vector loads
-                // without one; 16-bit rows take element loads. fn1(v, lp) gets
-                // one value, fn4(q, v0) the vector of tokens v0 .. v0 + 3.
-                // Returns false after a copy timeout (reported).
-                auto sweep_row = [&](auto&& fn1, auto&& fn4) -> bool {
+                // plain loads and the body as float4 vectors; 16-bit rows take
+                // element loads. fn1(v, lp) gets one value, fn4(q, v0) the
+                // vector of tokens v0 .. v0 + 3.
+                auto sweep_row = [&](auto&& fn1, auto&& fn4) {
                     if (p.x16) {
                         for (int base = 0; base < V; base += 16 * NT) {
                             float lv[16];
@@ -2561,72 +2519,28 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                                 if (v < V) fn1(v, lv[r]);
                             }
                         }
-                        return true;
+                        return;
                     }
                     const float* rp = p.x + row;
                     const int head = min(V, static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(rp) & 15u)) & 15u) >> 2));
                     if (tid < head) fn1(tid, rp[tid]);
                     const float4* body = reinterpret_cast<const float4*>(rp + head);
                     const int nv = (V - head) >> 2;
-                    if (rs.stages > 0) {
-                        const int S = rs.stages;
-                        const int nch = (nv + kRescanChunkF4 - 1) / kRescanChunkF4;
-                        auto issue = [&](int c) {   // thread 0
-                            const uint32_t g = rs.seq + static_cast<uint32_t>(c);
-                            const int st = static_cast<int>(g % static_cast<uint32_t>(S));
-                            const int n4 = min(kRescanChunkF4, nv - c * kRescanChunkF4);
-                            mbar_arrive_expect_tx(rs.bar + st, static_cast<uint32_t>(n4) * 16u);
-                            bulk_copy_g2s(rs.stage + static_cast<size_t>(st) * kRescanChunkF4,
-                                          body + static_cast<size_t>(c) * kRescanChunkF4,
-                                          static_cast<uint32_t>(n4) * 16u, rs.bar + st);
-                        };
-                        unsigned long long* err = p.counters ? p.counters + 3 : nullptr;
-                        if (tid == 0)
-                            for (int c = 0; c < nch && c < S; ++c) issue(c);
-                        for (int c = 0; c < nch; ++c) {
-                            const uint32_t g = rs.seq + static_cast<uint32_t>(c);
-                            const int st = static_cast<int>(g % static_cast<uint32_t>(S));
-                            const bool ok = mbar_wait(rs.bar + st, (g / static_cast<uint32_t>(S)) & 1u, err);
-                            if (ok) {
-                                const float4* sv = rs.stage + static_cast<size_t>(st) * kRescanChunkF4;
-                                const int n4 = min(kRescanChunkF4, nv - c * kRescanChunkF4);
-                                for (int i = tid; i < n4; i += NT) fn4(sv[i], head + 4 * (c * kRescanChunkF4 + i));
-                            }
-                            if (__syncthreads_or(!ok)) {
-                                // a copy did not land in time: wait, bounded, for
-                                // the copies still in flight, then give up
-                                if (tid == 0)
-                                    for (int c2 = c + 1; c2 < nch && c2 < c + S; ++c2) {
-                                        const uint32_t g2 = rs.seq + static_cast<uint32_t>(c2);
-                                        mbar_wait(rs.bar + g2 % static_cast<uint32_t>(S),
-                                                  (g2 / static_cast<uint32_t>(S)) & 1u, err);
-                                    }
-                                return false;
-                            }
-                            if (tid == 0 && c + S < nch) {
-                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                                issue(c + S);
-                            }
+                    for (int base = 0; base < nv; base += 4 * NT) {   // four vectors per thread in flight
+                        float4 q[4];
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) {
+                            const int i = base + r * NT + tid;
+                            q[r] = i < nv ? __ldg(body + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
                         }
-                        rs.seq += static_cast<uint32_t>(nch);
-                    } else {
-                        for (int base = 0; base < nv; base += 4 * NT) {
-                            float4 q[4];
 #pragma unroll
-                            for (int r = 0; r < 4; ++r) {
-                                const int i = base + r * NT + tid;
-                                q[r] = i < nv ? __ldg(body + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-                            }
-#pragma unroll
-                            for (int r = 0; r < 4; ++r) {
-                                const int i = base + r * NT + tid;
-                                if (i < nv) fn4(q[r], head + 4 * i);
-                            }
+                        for (int r = 0; r < 4; ++r) {
+                            const int i = base + r * NT + tid;
+                            if (i < nv) fn4(q[r], head + 4 * i);
                         }
                     }
                     const int t0 = head + 4 * nv;
                     if (t0 + tid < V) fn1(t0 + tid, rp[t0 + tid]);
-                    return true;
                 };
                 // While the step has fewer than N candidates (G empty: step 0 of
                 // a decode whose one live row has a short list), every entry of
@@ -2655,13 +2569,12 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                             const unsigned same = __match_any_sync(act, bin);
                             if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(hist + bin, __popc(same));
                         };
-                        const bool ok = sweep_row(count, [&](const float4 q, int v0) {
+                        sweep_row(count, [&](const float4 q, int v0) {
                             count(v0, q.x);
                             count(v0 + 1, q.y);
                             count(v0 + 2, q.z);
                             count(v0 + 3, q.w);
                         });
-                        if (!ok) return false;
                         __syncthreads();
                         if (wid == 0) {
                             int loc[8];
@@ -2710,7 +2623,6 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                     }
                 }
                 // one sweep against the G of the row's start, no barrier inside
-                // but the ring's
                 {
                     const uint64_t gh = sh[N - 1], gl = sl[N - 1];
                     const float floor_lp = gh == 0 ? nth_floor : floor_of(gh);
@@ -2728,7 +2640,7 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                             sh_over = 1;
                         }
                     };
-                    const bool ok = sweep_row(stage, [&](const float4 q, int v0) {
+                    sweep_row(stage, [&](const float4 q, int v0) {
                         // a vector whose largest value is at or below the floor is skipped
                         const float m4 = fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w));
                         if (!(m4 > floor_lp)) return;   // (NaN is not finite: never a candidate)
@@ -2737,7 +2649,6 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                         stage(v0 + 2, q.z);
                         stage(v0 + 3, q.w);
                     });
-                    if (!ok) return false;
                     __syncthreads();
                 }
                 const int staged = sh_n;
@@ -2843,12 +2754,11 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
 }
 
 template <int NT, int PER>
-__global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int seq_K, int sel_cap, int rs_stages) {
+__global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int seq_K, int sel_cap) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     float* state = p.merge_state ? p.merge_state + static_cast<int64_t>(e) * 4 * seq_K : nullptr;
-    RescanRing rs = rescan_ring_init<NT>(smem, sel_cap, seq_K, rs_stages);
-    list_merge_body<NT, PER>(p, e, p.t_begin > 0 ? p.t_begin : 0, p.t_end, state, seq_K, sel_cap, smem, nullptr, rs);
+    list_merge_body<NT, PER>(p, e, p.t_begin > 0 ? p.t_begin : 0, p.t_end, state, seq_K, sel_cap, smem, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -2869,7 +2779,7 @@ __global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int s
 template <int PER>
 __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodeParams p, int capw, int seq_K,
                                                                       int sel_cap, int merge_ctas,
-                                                                      unsigned int* step_done, int rs_stages) {
+                                                                      unsigned int* step_done) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     if (static_cast<int>(blockIdx.x) >= merge_ctas) {
         row_scan_body<false, true>(p, capw, 1, smem_raw, step_done);
@@ -2885,19 +2795,18 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodePa
     __syncthreads();
     if (sh_bad) return;
     const int T = p.desc[0].T;
-    RescanRing rs = rescan_ring_init<kFusedThreads>(smem_raw, sel_cap, seq_K, rs_stages);
     if (merge_ctas >= p.B) {
-        list_merge_body<kFusedThreads, PER>(p, blockIdx.x, 0, T, nullptr, seq_K, sel_cap, smem_raw, step_done, rs);
+        list_merge_body<kFusedThreads, PER>(p, blockIdx.x, 0, T, nullptr, seq_K, sel_cap, smem_raw, step_done);
         return;
     }
     // examples in turn, one step at a time, each one's beams in shared memory
-    float* beams_area = reinterpret_cast<float*>(smem_raw + list_merge_total_smem(kFusedThreads, sel_cap, seq_K, rs_stages));
+    float* beams_area = reinterpret_cast<float*>(smem_raw + list_merge_smem(kFusedThreads, sel_cap, seq_K));
     for (int t = 0; t < T; ++t) {
         int j = 0;
         for (int e = blockIdx.x; e < p.B; e += merge_ctas, ++j) {
             float* beams = beams_area + static_cast<size_t>(j) * 3 * seq_K;
-            if (!list_merge_body<kFusedThreads, PER>(p, e, t, t + 1, nullptr, seq_K, sel_cap, smem_raw, step_done, rs,
-                                                     beams, t == 0 && j == 0))
+            if (!list_merge_body<kFusedThreads, PER>(p, e, t, t + 1, nullptr, seq_K, sel_cap, smem_raw, step_done, beams,
+                                                     t == 0 && j == 0))
                 return;
         }
     }
@@ -4081,15 +3990,14 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
         // compact merge: candidate keys in registers, radix select, one sort
         constexpr int nt = kListMergeThreads;
         const int sel_cap = list_merge_sel_cap(max_N, nt);
-        const int stages = kRescanMaxStages;   // one CTA per SM either way (registers)
-        const size_t smem = list_merge_total_smem(nt, sel_cap, max_K, stages);
+        const size_t smem = list_merge_smem(nt, sel_cap, max_K);
         const bool small = M <= nt * 4;
         const void* fn = small ? reinterpret_cast<const void*>(list_merge_kernel<nt, 4>)
                                : reinterpret_cast<const void*>(list_merge_kernel<nt, 8>);
         cudaError_t err = ensure_dynamic_smem(fn, smem);
         if (err != cudaSuccess) return err;
-        if (small) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap, stages);
-        else list_merge_kernel<nt, 8><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap, stages);
+        if (small) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
+        else list_merge_kernel<nt, 8><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
         return counted(cudaGetLastError());
     }
     int cand_cap = M;
@@ -4137,10 +4045,9 @@ cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int
     const int capw = row_scan_capw(max_C);
     const int sel_cap = list_merge_sel_cap(max_N, kFusedThreads);
     size_t smem = static_cast<size_t>(kFusedThreads / 32) * row_scan_warp_bytes(capw, false);
-    const int stages = kRescanMaxStages;   // one CTA per SM either way (registers)
-    // a merge CTA with several examples keeps their beams after its ring
+    // a merge CTA with several examples keeps their beams after its arrays
     const int per_cta = (p.B + merge_ctas - 1) / merge_ctas;
-    const size_t msmem = list_merge_total_smem(kFusedThreads, sel_cap, max_K, stages) +
+    const size_t msmem = list_merge_smem(kFusedThreads, sel_cap, max_K) +
                          (per_cta > 1 ? static_cast<size_t>(per_cta) * 3 * max_K * sizeof(float) : 0);
     if (msmem > smem) smem = msmem;
     if (smem > static_cast<size_t>(227) * 1024) return cudaErrorNotSupported;
@@ -4155,9 +4062,9 @@ cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int
     const int grid = per_sm * num_sms;
     if (per_sm < 1 || grid <= merge_ctas) return cudaErrorNotSupported;
     DecodeParams pp = p;
-    int a_capw = capw, a_seq = max_K, a_sel = sel_cap, a_m = merge_ctas, a_st = stages;
+    int a_capw = capw, a_seq = max_K, a_sel = sel_cap, a_m = merge_ctas;
     unsigned int* a_done = step_done;
-    void* args[] = {&pp, &a_capw, &a_seq, &a_sel, &a_m, &a_done, &a_st};
+    void* args[] = {&pp, &a_capw, &a_seq, &a_sel, &a_m, &a_done};
     err = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kFusedThreads), args, smem, stream);
     return counted(err);
 }
