@@ -2550,114 +2550,122 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                 // prefix of ord(lp) until the values at or above it fit the
                 // staging room, and the floor is put just below the prefix.
                 float nth_floor = -INFINITY;
-                if (sh[N - 1] == 0) {
-                    uint32_t prefix = 0, mask = 0;
-                    int need_r = N;
-                    bool enough = true;
-                    for (int shift = 24;; shift -= 8) {
-                        for (int i = tid; i < 256; i += NT) hist[i] = 0;
-                        __syncthreads();
-                        auto count = [&](int v, float lp) {
-                            int bin = -1;
-                            if (isfinite(lp) && !(forced >= 0 && v != forced) && !(d.banned && d.banned[v]) &&
-                                !(eos_blocked && v == d.eos) &&
-                                !(p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v])) {
-                                const uint32_t u = ord_f32(lp);
-                                if ((u & mask) == prefix) bin = static_cast<int>((u >> shift) & 0xFFu);
-                            }
-                            const unsigned act = __activemask();
-                            const unsigned same = __match_any_sync(act, bin);
-                            if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(hist + bin, __popc(same));
-                        };
-                        sweep_row(count, [&](const float4 q, int v0) {
-                            count(v0, q.x);
-                            count(v0 + 1, q.y);
-                            count(v0 + 2, q.z);
-                            count(v0 + 3, q.w);
-                        });
-                        __syncthreads();
-                        if (wid == 0) {
-                            int loc[8];
-                            int tot = 0;
+                bool over = false;
+                // the sweep, and once more above the row's N-th largest allowed
+                // value if it stages more winners than the room
+                for (int attempt = 0; attempt < 2; ++attempt) {
+                    if (sh[N - 1] == 0 || attempt == 1) {
+                        uint32_t prefix = 0, mask = 0;
+                        int need_r = N;
+                        bool enough = true;
+                        for (int shift = 24;; shift -= 8) {
+                            for (int i = tid; i < 256; i += NT) hist[i] = 0;
+                            __syncthreads();
+                            auto count = [&](int v, float lp) {
+                                int bin = -1;
+                                if (isfinite(lp) && !(forced >= 0 && v != forced) && !(d.banned && d.banned[v]) &&
+                                    !(eos_blocked && v == d.eos) &&
+                                    !(p.row_allow && !p.row_allow[static_cast<int64_t>(k) * V + v])) {
+                                    const uint32_t u = ord_f32(lp);
+                                    if ((u & mask) == prefix) bin = static_cast<int>((u >> shift) & 0xFFu);
+                                }
+                                const unsigned act = __activemask();
+                                const unsigned same = __match_any_sync(act, bin);
+                                if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(hist + bin, __popc(same));
+                            };
+                            sweep_row(count, [&](const float4 q, int v0) {
+                                count(v0, q.x);
+                                count(v0 + 1, q.y);
+                                count(v0 + 2, q.z);
+                                count(v0 + 3, q.w);
+                            });
+                            __syncthreads();
+                            if (wid == 0) {
+                                int loc[8];
+                                int tot = 0;
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                loc[j] = hist[lane * 8 + j];
-                                tot += loc[j];
-                            }
-                            int incl = tot;
+                                for (int j = 0; j < 8; ++j) {
+                                    loc[j] = hist[lane * 8 + j];
+                                    tot += loc[j];
+                                }
+                                int incl = tot;
 #pragma unroll
-                            for (int o = 1; o < 32; o <<= 1) {
-                                const int v = __shfl_down_sync(FULL, incl, o);
-                                if (lane + o < 32) incl += v;
-                            }
-                            const int excl = incl - tot;
-                            if (lane == 0 && incl < need_r) sh_sel[0] = -1;   // fewer than N allowed entries
-                            if (excl < need_r && need_r <= incl) {
-                                int run = excl;
-                                for (int j = 7; j >= 0; --j) {
-                                    if (run + loc[j] >= need_r) {
-                                        sh_sel[0] = lane * 8 + j;
-                                        sh_sel[1] = run;
-                                        sh_sel[2] = loc[j];
-                                        break;
+                                for (int o = 1; o < 32; o <<= 1) {
+                                    const int v = __shfl_down_sync(FULL, incl, o);
+                                    if (lane + o < 32) incl += v;
+                                }
+                                const int excl = incl - tot;
+                                if (lane == 0 && incl < need_r) sh_sel[0] = -1;   // fewer than N allowed entries
+                                if (excl < need_r && need_r <= incl) {
+                                    int run = excl;
+                                    for (int j = 7; j >= 0; --j) {
+                                        if (run + loc[j] >= need_r) {
+                                            sh_sel[0] = lane * 8 + j;
+                                            sh_sel[1] = run;
+                                            sh_sel[2] = loc[j];
+                                            break;
+                                        }
+                                        run += loc[j];
                                     }
-                                    run += loc[j];
                                 }
                             }
+                            __syncthreads();
+                            const int digit = sh_sel[0];
+                            const int above = sh_sel[1];
+                            const int group = sh_sel[2];
+                            __syncthreads();
+                            if (digit < 0) { enough = false; break; }
+                            prefix |= static_cast<uint32_t>(digit) << shift;
+                            mask |= 0xFFu << shift;
+                            need_r -= above;
+                            // the values at or above the prefix: (N - need_r) + group
+                            if (shift == 0 || (N - need_r) + group <= room) break;
                         }
-                        __syncthreads();
-                        const int digit = sh_sel[0];
-                        const int above = sh_sel[1];
-                        const int group = sh_sel[2];
-                        __syncthreads();
-                        if (digit < 0) { enough = false; break; }
-                        prefix |= static_cast<uint32_t>(digit) << shift;
-                        mask |= 0xFFu << shift;
-                        need_r -= above;
-                        // the values at or above the prefix: (N - need_r) + group
-                        if (shift == 0 || (N - need_r) + group <= room) break;
-                    }
-                    if (enough) {
-                        const float edge = unord_f32(prefix);   // the least value with the prefix
-                        nth_floor = isfinite(edge) ? nextafterf(edge, -INFINITY) : -INFINITY;
-                    }
-                }
-                // one sweep against the G of the row's start, no barrier inside
-                {
-                    const uint64_t gh = sh[N - 1], gl = sl[N - 1];
-                    const float floor_lp = gh == 0 ? nth_floor : floor_of(gh);
-                    if (tid == 0) { sh_n = 0; sh_over = 0; }
-                    __syncthreads();
-                    auto stage = [&](int v, float lp) {
-                        uint64_t l = 0;
-                        const uint64_t h = winner(v, lp, floor_lp, gh, gl, l);
-                        if (!h) return;
-                        const int pos = atomicAdd(&sh_n, 1);
-                        if (pos < room) {
-                            sh[N + pos] = h;
-                            sl[N + pos] = l;
-                        } else {
-                            sh_over = 1;
+                        if (enough) {
+                            const float edge = unord_f32(prefix);   // the least value with the prefix
+                            nth_floor = isfinite(edge) ? nextafterf(edge, -INFINITY) : -INFINITY;
                         }
-                    };
-                    sweep_row(stage, [&](const float4 q, int v0) {
-                        // a vector whose largest value is at or below the floor is skipped
-                        const float m4 = fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w));
-                        if (!(m4 > floor_lp)) return;   // (NaN is not finite: never a candidate)
-                        stage(v0, q.x);
-                        stage(v0 + 1, q.y);
-                        stage(v0 + 2, q.z);
-                        stage(v0 + 3, q.w);
-                    });
+                    }
+                    // one sweep against the G of the row's start, no barrier inside
+                    {
+                        const uint64_t gh = sh[N - 1], gl = sl[N - 1];
+                        const float floor_lp = gh == 0 ? nth_floor : fmaxf(floor_of(gh), nth_floor);
+                        if (tid == 0) { sh_n = 0; sh_over = 0; }
+                        __syncthreads();
+                        auto stage = [&](int v, float lp) {
+                            uint64_t l = 0;
+                            const uint64_t h = winner(v, lp, floor_lp, gh, gl, l);
+                            if (!h) return;
+                            const int pos = atomicAdd(&sh_n, 1);
+                            if (pos < room) {
+                                sh[N + pos] = h;
+                                sl[N + pos] = l;
+                            } else {
+                                sh_over = 1;
+                            }
+                        };
+                        sweep_row(stage, [&](const float4 q, int v0) {
+                            // a vector whose largest value is at or below the floor is skipped
+                            const float m4 = fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w));
+                            if (!(m4 > floor_lp)) return;   // (NaN is not finite: never a candidate)
+                            stage(v0, q.x);
+                            stage(v0 + 1, q.y);
+                            stage(v0 + 2, q.z);
+                            stage(v0 + 3, q.w);
+                        });
+                        __syncthreads();
+                    }
+                    const int staged = sh_n;
+                    over = sh_over != 0;
+                    __syncthreads();
+                    if (!over) {
+                        if (staged > 0) merge_stage(staged);
+                        break;
+                    }
+                    for (int i = N + tid; i < sort_n2; i += NT) { sh[i] = 0; sl[i] = 0; }
                     __syncthreads();
                 }
-                const int staged = sh_n;
-                const int over = sh_over;
-                __syncthreads();
-                if (!over) {
-                    if (staged > 0) merge_stage(staged);
-                    continue;
-                }
+                if (!over) continue;
                 // More winners than the staging room: drop the stage and sweep
                 // the row again in chunks of at most `room` values, merging the
                 // stage after each chunk (G only improves; each value is seen
