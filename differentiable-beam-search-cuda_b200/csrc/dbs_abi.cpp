@@ -421,6 +421,20 @@ std::shared_ptr<ResultStore> run_decode(DBSDecoderHandle* h, const Options& opt,
     auto stage = [&](size_t ci) {   // host -> device copy of chunk ci's log-probs
         const Chunk& c = chunks[ci];
         float* dst = stage_buf[ci & 1]->as<float>();
+        // examples stored back to back without padding beams: one copy
+        bool packed = true;
+        for (int b = c.b0; b < c.b1 && packed; ++b) {
+            const HostExample& e = hx[b];
+            packed = e.k_stride == e.K && (b == c.b0 || e.x_offset == hx[b - 1].x_offset +
+                                                             static_cast<int64_t>(hx[b - 1].T) * hx[b - 1].k_stride * V);
+        }
+        if (packed) {
+            dbs_host::check_cuda(cudaMemcpyAsync(dst, x + hx[c.b0].x_offset, static_cast<size_t>(c.elems) * sizeof(float),
+                                                 cudaMemcpyHostToDevice, copy_cs->s),
+                                 "stage log_probs");
+            dbs_host::check_cuda(cudaEventRecord(staged_ev[ci & 1], copy_cs->s), "cudaEventRecord");
+            return;
+        }
         int64_t off = 0;
         for (int b = c.b0; b < c.b1; ++b) {
             const HostExample& e = hx[b];

@@ -874,13 +874,16 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
     };
 
     // Lists longer than 32 (when each warp scans many rows): the warp starts
-    // a row at a speculative threshold, the (C + 4 sqrt(C))-th largest lp of
+    // a row at a speculative threshold, the (C + 6 sqrt(C))-th largest lp of
     // the last row with the same list length C it scanned (the rank of a
     // row's C-th value varies by about sqrt(C) between rows of one
     // distribution). If fewer than C entries reach it the row is scanned
     // again from global memory, so the list stays exact; otherwise far fewer
     // elements take the slow path than with a threshold that starts at
-    // -FLT_MAX. The guesses are kept per list length (a few slots, by a hash
+    // -FLT_MAX. (Measured at C = 64 on 256 examples of log_softmax(N(0,1))
+    // rows: margins of 3 / 4 / 5 / 6 / 7 / 8 sqrt(C) read 6.4 / 2.4 / 0.8 /
+    // 0.15 / 0.01 / 0 % of the rows twice and scan in 21.3 / 18.8 / 17.7 /
+    // 17.8 / 17.8 / 28.2 ms.) The guesses are kept per list length (a few slots, by a hash
     // of C): consecutive rows of a warp come from different examples, whose
     // beam sizes may differ.
     auto spec_slot = [](int c) { return static_cast<int>((static_cast<uint32_t>(c) * 2654435761u) >> 30); };
@@ -1103,7 +1106,7 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
             }
             __syncwarp();
             drop_disallowed();
-            const int k_spec = C + static_cast<int>(4.0f * sqrtf(static_cast<float>(C)));
+            const int k_spec = C + static_cast<int>(6.0f * sqrtf(static_cast<float>(C)));
             const bool missed = spec_used && cnt < C;
             if (missed) {
                 if (lane == 0 && p.counters) atomicAdd(p.counters, 1ull);   // diagnostics: second passes
