@@ -49,6 +49,8 @@ struct ExampleDesc {
     int32_t P;               // relaxed pool size (output width of the pool)
     int32_t N;               // candidates selected per step (P or K)
     int32_t C;               // row list capacity (at most N; shorter lists are proven per step)
+    int32_t ext0;            // extra entries of beam 0's rows (compact merge only): a step's lists
+                             // are K rows of C entries, then beam 0's entries C .. C + ext0 - 1
     int32_t sel_stride;      // K-dimension stride of [T,K] outputs
     int32_t pool_stride;     // P-dimension stride of [T,P] outputs
     int32_t sel_t_stride;    // T-dimension stride (elements) of selected outputs
@@ -178,7 +180,13 @@ cudaError_t launch_row_scan(const DecodeParams& p, int max_C, int num_sms, cudaS
 // max_threads caps the CTA size of the selection merge (256 lets two merge
 // CTAs share an SM).
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T,
-                              int max_N, bool need_sequences, cudaStream_t stream, int max_threads = 0);
+                              int max_N, bool need_sequences, cudaStream_t stream, int max_threads = 0,
+                              int max_ext = 0);
+// Whether launch_step_merge runs the compact merge for these sizes, with
+// beam 0's lists max_ext entries longer (only the compact merge reads
+// ExampleDesc::ext0, so the engine sets it only when this holds).
+bool compact_merge_applies(int max_K, int max_C, int max_ext, int max_N, bool need_sequences,
+                           bool first_row_apart);
 // Kernel launches made by this library in this process (every launcher
 // counts the launches it queues).
 long long kernel_launch_count();
@@ -189,8 +197,8 @@ cudaError_t launch_weights(const DecodeParams& p, int max_T, int max_K, int max_
 // merge_ctas < B; step_done [B*T] zeroed). cudaErrorNotSupported when the
 // shape or the device does not allow it (the caller then scans and merges
 // in separate launches).
-cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int max_N, int merge_ctas,
-                                unsigned int* step_done, int num_sms, cudaStream_t stream);
+cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int max_ext, int max_N,
+                                int merge_ctas, unsigned int* step_done, int num_sms, cudaStream_t stream);
 cudaError_t launch_backward(const BackwardParams& p, int max_K, int max_P, bool sparse,
                             cudaStream_t stream);
 // blocks_per_sm: 4 fills the GPU; 1 leaves three quarters of every SM's

@@ -721,10 +721,12 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     if constexpr (k16) j.row = p.x16 + elem;
     else j.row = p.x + elem;
     j.r = r;
-    j.list_at = d.list_offset + lr * d.C;
+    // a step's lists: K rows of C entries, then beam 0's extra entries
+    j.list_at = d.list_offset + static_cast<int64_t>(t) * (static_cast<int64_t>(d.K) * d.C + d.ext0) +
+                static_cast<int64_t>(k) * d.C;
     // the live step-0 row of a short-list decode keeps a long list in the
     // list space of step 0's K rows
-    j.C = p.first_rows_only ? min(min(d.N, d.K * d.C), kStep0ListMax) : d.C;
+    j.C = p.first_rows_only ? min(min(d.N, d.K * d.C), kStep0ListMax) : d.C + (k == 0 ? d.ext0 : 0);
     j.forced = d.forced ? d.forced[t] : -1;
     // A decode starts from beam 0 alone (the other beams score -inf), so the
     // rows of the other beams at step 0 can never yield a candidate; like
@@ -746,9 +748,6 @@ __device__ __forceinline__ RowJob make_job(const DecodeParams& p, int64_t r, int
     return j;
 }
 
-// The row-scan loop of one warp (per-warp shared memory at smem_raw + warp
-// index * row_scan_warp_bytes). With step_done, each finished row (its list,
-// count and bound written and fenced) adds one to step_done[e * T + t].
 // Speculative thresholds of long lists left by the warps that last ran out
 // of rows in a row-scan launch on this device, (list length << 32) | lp bits
 // per slot: a launch's warps start from them instead of from nothing (a row
@@ -761,6 +760,9 @@ __device__ __forceinline__ void scan_row_done(unsigned int* step_done, int idx, 
     if (lane == 0) atomicAdd(step_done + idx, 1u);
 }
 
+// The row-scan loop of one warp (per-warp shared memory at smem_raw + warp
+// index * row_scan_warp_bytes). With step_done, each finished row (its list,
+// count and bound written and fenced) adds one to step_done[e * T + t].
 template <bool k16, bool kFused>
 __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, int speculate, unsigned char* smem_raw,
                                               unsigned int* step_done) {
@@ -883,10 +885,18 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
     // -FLT_MAX. (Measured at C = 64 on 256 examples of log_softmax(N(0,1))
     // rows: margins of 3 / 4 / 5 / 6 / 7 / 8 sqrt(C) read 6.4 / 2.4 / 0.8 /
     // 0.15 / 0.01 / 0 % of the rows twice and scan in 21.3 / 18.8 / 17.7 /
-    // 17.8 / 17.8 / 28.2 ms.) The guesses are kept per list length (a few slots, by a hash
-    // of C): consecutive rows of a warp come from different examples, whose
-    // beam sizes may differ.
-    auto spec_slot = [](int c) { return static_cast<int>((static_cast<uint32_t>(c) * 2654435761u) >> 30); };
+    // 17.8 / 17.8 / 28.2 ms.) The guesses are kept per list length in a few
+    // slots (the slot that holds C, else an empty one, else one by a hash of
+    // C): consecutive rows of a warp come from different examples, whose
+    // beam sizes may differ, and beam 0's rows may list more entries; two
+    // lengths that shared a slot would evict each other's guess.
+    auto spec_slot = [&](int c) {
+        for (int s = 0; s < kSpecSlots; ++s)
+            if (spec_len[s] == c) return s;
+        for (int s = 0; s < kSpecSlots; ++s)
+            if (spec_len[s] == 0) return s;
+        return static_cast<int>((static_cast<uint32_t>(c) * 2654435761u) >> 30);
+    };
     while (true) {
         issue_more();
         const RowJob& j = cur;
@@ -1170,7 +1180,10 @@ __device__ __forceinline__ void row_scan_body(const DecodeParams& p, int capw, i
                 __syncwarp();
             }
             const int keep = cnt < C ? cnt : C;
-            for (int i = lane; i < keep; i += 32) out[i] = buf[i];
+            // beam 0's entries past C go behind the step's K row lists
+            const int base_c = p.first_rows_only ? C : p.desc[e_cur].C;
+            const int skip = keep > base_c ? (p.desc[e_cur].K - 1) * base_c : 0;
+            for (int i = lane; i < keep; i += 32) out[i < base_c ? i : i + skip] = buf[i];
             rej = warp_max(rej);
             if (lane == 0) {
                 float b = fmaxf(rej, evict);
@@ -2040,7 +2053,11 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
     }
     int sort_n2 = 1;
     while (sort_n2 < sel_cap) sort_n2 <<= 1;   // sel_cap is a power of two
-    const int M = K * C;
+    // A step's slots: K rows of C entries (slot k * C + i: entry i of row k),
+    // then beam 0's entries C .. C + ext0 - 1 (slot K * C + i - C); at step
+    // 0 of a decode with the first row apart, entry i of row 0 (slot i).
+    const int KC = K * C;
+    const int ext0 = d.ext0;
     // the selection buffer past the top N is the rescans' staging area and
     // is kept zero from here on (the sorts read it; every step leaves it so)
     if (fresh)
@@ -2048,12 +2065,15 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
 
     for (int t = t_first; t < t_stop; ++t) {
         const int64_t row0 = d.row_begin + static_cast<int64_t>(t) * K;
-        const uint64_t* step_lists = p.lists + d.list_offset + (row0 - d.row_begin) * C;
+        const uint64_t* step_lists = p.lists + d.list_offset + static_cast<int64_t>(t) * (KC + ext0);
         const int forced = d.forced ? d.forced[t] : -1;
         const bool eos_blocked = use_eos && (t + 1) < d.min_length;
         __syncthreads();   // the previous step's state update is visible
         if (step_done && !wait_step_rows(p, step_done, e * T + t, static_cast<unsigned int>(K))) return false;
         const bool long0 = p.first_row_apart && t == 0;
+        const int M = long0 ? KC : KC + ext0;
+        auto slot_row = [&](int idx) { return long0 || idx >= KC ? 0 : idx / C; };
+        auto slot_entry = [&](int idx, int k) { return long0 ? idx : (idx >= KC ? C + (idx - KC) : idx - k * C); };
         // The step's list entries (its M slots of the lists) are loaded
         // together with the counts and bounds, one round trip; entries past
         // a row's count are dropped after the barrier.
@@ -2083,8 +2103,8 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
             for (int u = 0; u < kLmPer; ++u) {
                 const int idx = tid + u * NT;
                 if (idx < M) {
-                    const int k = long0 ? 0 : idx / C;
-                    const int i = idx - k * C;
+                    const int k = slot_row(idx);
+                    const int i = slot_entry(idx, k);
                     if (i == row_cnt[k] - 1) {
                         next_raw[k] = list_lp(raw_e[u]);
                         next_len[k] = list_token(raw_e[u]);
@@ -2098,8 +2118,8 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
                 uint64_t h = 0;
                 int tok = -1;
                 if (idx < M) {
-                    const int k = long0 ? 0 : idx / C;
-                    const int i = idx - k * C;
+                    const int k = slot_row(idx);
+                    const int i = slot_entry(idx, k);
                     const float pr = prev_raw[k];
                     if (isfinite(pr)) {
                         if (use_eos && ended[k]) {
@@ -2122,9 +2142,7 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
             }
         }
         auto cand_lo_of = [&](int u) -> uint64_t {
-            const int idx = tid + u * NT;
-            const int k = long0 ? 0 : idx / C;
-            return cand_lo(k, ctok[u]);
+            return cand_lo(slot_row(tid + u * NT), ctok[u]);
         };
 
         // Radix select: the masked prefix (ph, pl) that the top-N keys reach
@@ -3971,8 +3989,16 @@ static size_t merge_rank_smem(int ring, int max_K, int max_C, int max_N, int tab
 // Shared memory the ranking merge may take; beyond it the sort merge runs.
 constexpr size_t kMergeRankSmemBudget = 200 * 1024;
 
+bool compact_merge_applies(int max_K, int max_C, int max_ext, int max_N, bool need_sequences,
+                           bool first_row_apart) {
+    const int64_t M = static_cast<int64_t>(max_K) * max_C;
+    if (!need_sequences && !first_row_apart && M <= 256) return false;   // the ranking merge
+    return !need_sequences && M + max_ext <= kListMergeMaxCandidates && max_N <= kListMergeThreads &&
+           list_merge_enabled();
+}
+
 cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int max_T, int max_N,
-                              bool need_sequences, cudaStream_t stream, int max_threads) {
+                              bool need_sequences, cudaStream_t stream, int max_threads, int max_ext) {
     // (the ranking merge reads every row as one list of at most C entries)
     if (!need_sequences && !p.first_row_apart && static_cast<int64_t>(max_K) * max_C <= 256) {
         const int tab_n = (p.Lmax + 1 <= 4096) ? p.Lmax + 1 : 0;
@@ -3997,17 +4023,20 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
         }
     }
     const int M = max_K * max_C;
-    if (!need_sequences && M <= kListMergeMaxCandidates && max_N <= kListMergeThreads && list_merge_enabled()) {
-        // compact merge: candidate keys in registers, radix select, one sort
+    if (!need_sequences && M + max_ext <= kListMergeMaxCandidates && max_N <= kListMergeThreads &&
+        list_merge_enabled()) {
+        // compact merge: candidate keys in registers, radix select, ranking by counting
         constexpr int nt = kListMergeThreads;
         const int sel_cap = list_merge_sel_cap(max_N, nt);
         const size_t smem = list_merge_smem(nt, sel_cap, max_K);
-        const bool small = M <= nt * 4;
-        const void* fn = small ? reinterpret_cast<const void*>(list_merge_kernel<nt, 4>)
-                               : reinterpret_cast<const void*>(list_merge_kernel<nt, 8>);
+        const int per = M + max_ext <= nt * 4 ? 4 : (M + max_ext <= nt * 5 ? 5 : 8);
+        const void* fn = per == 4 ? reinterpret_cast<const void*>(list_merge_kernel<nt, 4>)
+                                  : (per == 5 ? reinterpret_cast<const void*>(list_merge_kernel<nt, 5>)
+                                              : reinterpret_cast<const void*>(list_merge_kernel<nt, 8>));
         cudaError_t err = ensure_dynamic_smem(fn, smem);
         if (err != cudaSuccess) return err;
-        if (small) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
+        if (per == 4) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
+        else if (per == 5) list_merge_kernel<nt, 5><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
         else list_merge_kernel<nt, 8><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
         return counted(cudaGetLastError());
     }
@@ -4049,11 +4078,11 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
     return counted(cudaGetLastError());
 }
 
-cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int max_N, int merge_ctas,
-                                unsigned int* step_done, int num_sms, cudaStream_t stream) {
-    const int M = max_K * max_C;
-    if (M > 8 * kFusedThreads || max_N > kFusedThreads || merge_ctas < 1 || max_C > 128) return cudaErrorNotSupported;
-    const int capw = row_scan_capw(max_C);
+cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int max_ext, int max_N,
+                                int merge_ctas, unsigned int* step_done, int num_sms, cudaStream_t stream) {
+    const int M = max_K * max_C + max_ext;
+    if (M > 8 * kFusedThreads || max_N > kFusedThreads || merge_ctas < 1) return cudaErrorNotSupported;
+    const int capw = row_scan_capw(max_C + max_ext);
     const int sel_cap = list_merge_sel_cap(max_N, kFusedThreads);
     size_t smem = static_cast<size_t>(kFusedThreads / 32) * row_scan_warp_bytes(capw, false);
     // a merge CTA with several examples keeps their beams after its arrays
@@ -4062,9 +4091,10 @@ cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int
                          (per_cta > 1 ? static_cast<size_t>(per_cta) * 3 * max_K * sizeof(float) : 0);
     if (msmem > smem) smem = msmem;
     if (smem > static_cast<size_t>(227) * 1024) return cudaErrorNotSupported;
-    const bool small = M <= kFusedThreads * 4;
-    const void* fn = small ? reinterpret_cast<const void*>(fused_decode_kernel<4>)
-                           : reinterpret_cast<const void*>(fused_decode_kernel<8>);
+    const int per = M <= kFusedThreads * 4 ? 4 : (M <= kFusedThreads * 5 ? 5 : 8);
+    const void* fn = per == 4 ? reinterpret_cast<const void*>(fused_decode_kernel<4>)
+                              : (per == 5 ? reinterpret_cast<const void*>(fused_decode_kernel<5>)
+                                          : reinterpret_cast<const void*>(fused_decode_kernel<8>));
     cudaError_t err = ensure_dynamic_smem(fn, smem);
     if (err != cudaSuccess) return err;
     int per_sm = 0;

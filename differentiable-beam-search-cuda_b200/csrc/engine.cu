@@ -459,11 +459,11 @@ int list_capacity(const Options& opt, int K, bool pool, bool dynamic) {
 // K = 16 with 32 examples, 32K rows, 2.73 -> 2.88 ms).
 constexpr int kFusedMaxExamples = 64;
 // Fused decode: DBS_FUSED=0 turns it off; DBS_FUSED_MERGE_CTAS=<n> sets how
-// many CTAs merge (default: one per example up to 32 examples, 24 above; a
-// CTA with several examples merges them one step at a time in turn).
-// Measured with T = 64, K = 32, V = 50257 (ms per decode + backward):
-// 32 examples 3.59 / 3.75 / 3.98 with 32 / 24 / 16 merge CTAs, 64 examples
-// 6.87 / 6.53 / 7.51 with 32 / 24 / 16.
+// many CTAs merge (default: one per example up to 16 examples, 16 above; a
+// CTA with several examples merges them one step at a time in turn, and
+// every SM it leaves runs the scan). Measured with T = 64, K = 32,
+// V = 50257 (ms per decode + backward): 32 examples 3.36 / 3.20 / 3.18 with
+// 32 / 24 / 16 merge CTAs, 64 examples 6.30 / 5.90 / 5.64.
 bool fused_enabled() {
     static const bool on = [] {
         const char* v = std::getenv("DBS_FUSED");
@@ -477,9 +477,10 @@ int fused_merge_ctas(int B) {
         return v ? std::max(1, std::atoi(v)) : 0;
     }();
     if (n > 0) return std::min(B, n);
-    return B <= 32 ? B : 24;
+    return std::min(B, 16);
 }
 constexpr int kShortListEntries = 64;
+constexpr int kBeam0Extra = 128;
 constexpr int kShortListMinExamples = 32;
 constexpr int64_t kShortListMinRows = 65536;
 
@@ -552,7 +553,6 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         dbs_dev::ExampleDesc& d = desc[b];
         d.x_offset = e.x_offset;
         d.row_begin = rows;
-        d.list_offset = list_entries;
         d.sel_offset = layout.sel_offset[b];
         d.pool_offset = layout.pool_offset[b];
         d.final_offset = layout.final_offset[b];
@@ -564,6 +564,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         d.P = P;
         d.N = N;
         d.C = C;
+        d.ext0 = 0;
         d.sel_stride = e.K;
         d.pool_stride = P;
         d.sel_t_stride = e.K;
@@ -573,7 +574,6 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         d.banned = e.banned;
         d.forced = e.forced;
         rows += static_cast<int64_t>(e.T) * e.K;
-        list_entries += static_cast<int64_t>(e.T) * e.K * C;
         row_prefix[b + 1] = rows;
         max_T = std::max(max_T, e.T);
         max_K = std::max(max_K, e.K);
@@ -584,6 +584,24 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
     }
     if (pool && out.relaxed_weights && max_P > 1024) {
         throw LengthError("relaxed pool above 1024 entries is not supported by the device decoder");
+    }
+    // Beam 0's rows list up to kBeam0Extra more entries when the merge is the
+    // compact merge (the only one that reads them): the best parent's row
+    // holds most of a step's pool, and without them it is the row the
+    // merge rescans (91 % of the rescans at K = 32, N = 256, C = 64).
+    int max_ext = 0;
+    if (pool && !dynamic && !ext_lists && ctl.scan && ctl.merge && !ctl.row_allow &&
+        (fused || dbs_dev::compact_merge_applies(max_K, max_C, kBeam0Extra, max_N, dynamic, short_lists))) {
+        for (dbs_dev::ExampleDesc& d : desc) {
+            int ext = std::min(kBeam0Extra, d.N - d.C);
+            ext = std::min(ext, dbs_dev::kListMergeMaxCandidates - d.K * d.C);
+            d.ext0 = std::max(0, ext);
+            max_ext = std::max(max_ext, d.ext0);
+        }
+    }
+    for (dbs_dev::ExampleDesc& d : desc) {
+        d.list_offset = list_entries;
+        list_entries += static_cast<int64_t>(d.T) * (static_cast<int64_t>(d.K) * d.C + d.ext0);
     }
     const int lmax = max_T + 1;
     std::vector<float> pen, inv;
@@ -772,7 +790,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
                     ProfileScope ps(kRowScan, hp.side);
                     dbs_dev::DecodeParams ps_p = p;
                     ps_p.total_rows = r1;
-                    check_cuda(dbs_dev::launch_row_scan(ps_p, max_C, device_sm_count(), hp.side, r1 - r0),
+                    check_cuda(dbs_dev::launch_row_scan(ps_p, max_C + max_ext, device_sm_count(), hp.side, r1 - r0),
                                "row scan kernel");
                 }
                 check_cuda(cudaEventRecord(seg_done[i], hp.side), "cudaEventRecord");
@@ -805,13 +823,13 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
             mp.t_end = std::min(max_T, (i + 1) * seg_steps);
             mp.merge_state = d_state;
             ProfileScope ps(kStepMerge, stream);
-            check_cuda(dbs_dev::launch_step_merge(mp, max_K, max_C, max_T, max_N, dynamic, stream),
+            check_cuda(dbs_dev::launch_step_merge(mp, max_K, max_C, max_T, max_N, dynamic, stream, 0, max_ext),
                        "step merge kernel");
         }
         trace.mark("merge queued");
         check_cuda(cudaStreamWaitEvent(stream, seg_done[n_seg], 0), "cudaStreamWaitEvent");
     } else if (fused) {
-        // merge CTAs: one per example up to 32 examples, else examples in turn
+        // merge CTAs: one per example up to 16 examples, else examples in turn
         const int merge_ctas = fused_merge_ctas(B);
         check_cuda(cudaMemsetAsync(d_done, 0, sizeof(unsigned int) * static_cast<size_t>(B) * max_T, stream),
                    "zero step counters");
@@ -822,14 +840,15 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         cudaError_t ferr;
         {
             ProfileScope ps(kRowScan, stream);   // the whole fused launch
-            ferr = dbs_dev::launch_fused_decode(fp, max_K, max_C, max_N, merge_ctas, d_done, device_sm_count(), stream);
+            ferr = dbs_dev::launch_fused_decode(fp, max_K, max_C, max_ext, max_N, merge_ctas, d_done, device_sm_count(),
+                                                stream);
         }
         if (ferr == cudaErrorNotSupported) {
             cudaGetLastError();
             // separate launches on the same lists (the merge's rescans list step 0)
             {
                 ProfileScope ps(kRowScan, stream);
-                check_cuda(dbs_dev::launch_row_scan(p, max_C, device_sm_count(), stream, rows), "row scan kernel");
+                check_cuda(dbs_dev::launch_row_scan(p, max_C + max_ext, device_sm_count(), stream, rows), "row scan kernel");
             }
             if (validate) {
                 check_cuda(cudaEventSynchronize(lease.s->validated), "validate");
@@ -837,7 +856,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
                     if (h_status[b]) throw InvalidArgument("log_probs contains NaN or +Inf");
             }
             ProfileScope ps(kStepMerge, stream);
-            check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream), "step merge kernel");
+            check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream, 0, max_ext), "step merge kernel");
         } else {
             check_cuda(ferr, "fused decode kernel");
             trace.mark("fused queued");
@@ -855,7 +874,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
             ProfileScope ps(kRowScan, stream);
             dbs_dev::DecodeParams ps_p = p;
             ps_p.total_rows = scan_end;   // rows are claimed from scan_begin up to here
-            check_cuda(dbs_dev::launch_row_scan(ps_p, max_C, device_sm_count(), stream, scan_end - scan_begin),
+            check_cuda(dbs_dev::launch_row_scan(ps_p, max_C + max_ext, device_sm_count(), stream, scan_end - scan_begin),
                        "row scan kernel");
             if (short_lists) {
                 // the live step-0 row of every example, with its long list
@@ -892,7 +911,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
             check_cuda(cudaEventRecord(hp.before, stream), "cudaEventRecord");
             {
                 ProfileScope ps(kStepMerge, stream);
-                check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream),
+                check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream, 0, max_ext),
                            "step merge kernel");
             }
             trace.mark("merge queued");
@@ -907,7 +926,7 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
             check_cuda(cudaStreamWaitEvent(stream, hp.after, 0), "cudaStreamWaitEvent");
         } else {
             ProfileScope ps(kStepMerge, stream);
-            check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream), "step merge kernel");
+            check_cuda(dbs_dev::launch_step_merge(p, max_K, max_C, max_T, max_N, dynamic, stream, 0, max_ext), "step merge kernel");
         }
     }
     const bool want_w = (p.weights && p.scores) || (p.relaxed_weights && p.pool_scores);
