@@ -1965,6 +1965,23 @@ __device__ __forceinline__ void lm_sort(uint64_t* hi, uint64_t* lo, int n2) {
     }
 }
 
+// Prefetch block of one example in list_merge_body: a flag (set when the
+// next step's lists are on their way), then room for pf_cap list entries and
+// the next step's K counts and K bounds. 16-byte copies that bypass L1
+// (cp.async.cg), so that lines of steps the scan has not listed yet are
+// never cached on the SM.
+__host__ __device__ constexpr size_t merge_prefetch_bytes(int pf_cap, int max_K) {
+    return 16 + static_cast<size_t>(pf_cap) * sizeof(uint64_t) +
+           ((static_cast<size_t>(max_K) * 2 * sizeof(int) + 15) & ~static_cast<size_t>(15));
+}
+__host__ __device__ constexpr size_t align16(size_t n) { return (n + 15) & ~static_cast<size_t>(15); }
+__device__ __forceinline__ void cp_async_16_cg(void* smem_dst, const void* gsrc) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_all() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Bounded wait of a merge CTA for the K rows of step t of example e
 // (step_done[e * T + t] == K, counted by the row-scan warps of the same
 // launch after their lists are written). Returns false, after setting the
@@ -2004,7 +2021,8 @@ template <int NT, int PER>
 __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, int t_first, int t_stop, float* state,
                                                 int seq_K, int sel_cap, unsigned char* smem,
                                                 const unsigned int* step_done, float* beams = nullptr,
-                                                bool fresh = true) {
+                                                bool fresh = true, unsigned char* pfb = nullptr,
+                                                int pf_cap = 0) {
     constexpr int NW = NT / 32;
     constexpr unsigned FULL = 0xFFFFFFFFu;
     constexpr int kLmPer = PER;
@@ -2062,38 +2080,92 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
     // is kept zero from here on (the sorts read it; every step leaves it so)
     if (fresh)
         for (int i = tid; i < sort_n2; i += NT) { sh[i] = 0; sl[i] = 0; }
+    // the 1 / penalty table in shared memory, so that a step's set-up reads
+    // no global memory once its lists are prefetched (published by the step
+    // loop's first barrier; every call of a block shares one table)
+    constexpr int kInvCache = 512;
+    __shared__ float sh_inv[kInvCache];
+    const bool inv_cached = p.Lmax + 1 <= kInvCache;
+    if (fresh && inv_cached)
+        for (int i = tid; i <= p.Lmax; i += NT) sh_inv[i] = p.inv_pen[i];
 
     for (int t = t_first; t < t_stop; ++t) {
         const int64_t row0 = d.row_begin + static_cast<int64_t>(t) * K;
         const uint64_t* step_lists = p.lists + d.list_offset + static_cast<int64_t>(t) * (KC + ext0);
         const int forced = d.forced ? d.forced[t] : -1;
         const bool eos_blocked = use_eos && (t + 1) < d.min_length;
-        __syncthreads();   // the previous step's state update is visible
-        if (step_done && !wait_step_rows(p, step_done, e * T + t, static_cast<unsigned int>(K))) return false;
+        // lists, counts and bounds prefetched during the example's previous
+        // step (flag 1: entries only, 2: counts and bounds too)
+        int* pf_flag = reinterpret_cast<int*>(pfb);
+        uint64_t* pf_e = pfb ? reinterpret_cast<uint64_t*>(pfb + 16) : nullptr;
+        int* pf_cnt = pfb ? reinterpret_cast<int*>(pf_e + pf_cap) : nullptr;
+        float* pf_bnd = pfb ? reinterpret_cast<float*>(pf_cnt + K) : nullptr;
+        const int pf_have = pfb ? *pf_flag : 0;   // (read before thread 0 rewrites it below)
+        cp_async_wait_all();   // (this thread's copies of any prefetch)
+        __syncthreads();   // the previous step's state update and the prefetched lists are visible
+        if (step_done && !pf_have && !wait_step_rows(p, step_done, e * T + t, static_cast<unsigned int>(K)))
+            return false;
         const bool long0 = p.first_row_apart && t == 0;
         const int M = long0 ? KC : KC + ext0;
         auto slot_row = [&](int idx) { return long0 || idx >= KC ? 0 : idx / C; };
         auto slot_entry = [&](int idx, int k) { return long0 ? idx : (idx >= KC ? C + (idx - KC) : idx - k * C); };
         // The step's list entries (its M slots of the lists) are loaded
-        // together with the counts and bounds, one round trip; entries past
-        // a row's count are dropped after the barrier.
+        // together with the counts and bounds, one round trip (or read from
+        // the prefetch); entries past a row's count are dropped after the
+        // barrier.
         uint64_t raw_e[kLmPer];
 #pragma unroll
         for (int u = 0; u < kLmPer; ++u) {
             const int idx = tid + u * NT;
-            raw_e[u] = idx < M ? __ldcg(reinterpret_cast<const unsigned long long*>(step_lists) + idx) : 0ull;
+            raw_e[u] = idx >= M ? 0ull
+                                : (pf_have ? pf_e[idx]
+                                           : __ldcg(reinterpret_cast<const unsigned long long*>(step_lists) + idx));
         }
         for (int k = tid; k < K; k += NT) {
-            row_cnt[k] = __ldcg(p.list_count + row0 + k);
-            row_bound[k] = __ldcg(p.list_bound + row0 + k);
-            row_inv[k] = p.inv_pen[prev_len[k] + 1];
+            row_cnt[k] = pf_have == 2 ? pf_cnt[k] : __ldcg(p.list_count + row0 + k);
+            row_bound[k] = pf_have == 2 ? pf_bnd[k] : __ldcg(p.list_bound + row0 + k);
+            row_inv[k] = inv_cached ? sh_inv[prev_len[k] + 1] : p.inv_pen[prev_len[k] + 1];
             unsafe[k] = 0;
             next_raw[k] = INFINITY;   // the lp and token of the row's last listed entry (rescans)
             next_len[k] = -1;
         }
         if (tid == 0) { sh_n = 0; sh_g = 0; sh_any = 0; }
         for (int i = tid; i < 256; i += NT) hist[i] = 0;   // the first radix pass
+        const int MN = KC + ext0;   // the next step's slots
+        const uint64_t* next_lists = step_lists + MN;
+        if (pfb && tid == 0) {
+            // prefetch the next step's lists while this step runs, when they
+            // are listed (always, without step_done) and fit 16-byte copies
+            // (the next step of this example comes in this call, or, with the
+            // beams kept by the caller, in its next call)
+            int ok = t + 1 < (beams ? T : t_stop) && MN <= pf_cap && (MN & 1) == 0 &&
+                     (reinterpret_cast<uintptr_t>(next_lists) & 15u) == 0;
+            if (ok && step_done) {
+                unsigned int v;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];"
+                             : "=r"(v)
+                             : "l"(step_done + e * T + t + 1)
+                             : "memory");
+                ok = v >= static_cast<unsigned int>(K);
+            }
+            if (ok && (K & 3) == 0 && (reinterpret_cast<uintptr_t>(p.list_count + row0 + K) & 15u) == 0 &&
+                (reinterpret_cast<uintptr_t>(p.list_bound + row0 + K) & 15u) == 0)
+                ok = 2;
+            *pf_flag = ok;
+        }
         __syncthreads();
+        if (pfb) {
+            const int pf_next = *pf_flag;
+            if (pf_next) {
+                for (int c = tid; c < (MN >> 1); c += NT) cp_async_16_cg(pf_e + 2 * c, next_lists + 2 * c);
+                if (pf_next == 2)
+                    for (int c = tid; c < (K >> 2); c += NT) {
+                        cp_async_16_cg(pf_cnt + 4 * c, p.list_count + row0 + K + 4 * c);
+                        cp_async_16_cg(pf_bnd + 4 * c, p.list_bound + row0 + K + 4 * c);
+                    }
+                cp_async_commit_all();
+            }
+        }
 
         // candidate keys of this thread's slots
         uint64_t ch[kLmPer];
@@ -2783,11 +2855,14 @@ __device__ __forceinline__ bool list_merge_body(const DecodeParams& p, int e, in
 }
 
 template <int NT, int PER>
-__global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int seq_K, int sel_cap) {
+__global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int seq_K, int sel_cap, int pf_cap) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int e = blockIdx.x;
     float* state = p.merge_state ? p.merge_state + static_cast<int64_t>(e) * 4 * seq_K : nullptr;
-    list_merge_body<NT, PER>(p, e, p.t_begin > 0 ? p.t_begin : 0, p.t_end, state, seq_K, sel_cap, smem, nullptr);
+    unsigned char* pfb = pf_cap > 0 ? smem + align16(list_merge_smem(NT, sel_cap, seq_K)) : nullptr;
+    if (pfb && threadIdx.x == 0) *reinterpret_cast<int*>(pfb) = 0;   // (published by the body's first barrier)
+    list_merge_body<NT, PER>(p, e, p.t_begin > 0 ? p.t_begin : 0, p.t_end, state, seq_K, sel_cap, smem, nullptr,
+                             nullptr, true, pfb, pf_cap);
 }
 
 // ---------------------------------------------------------------------------
@@ -2808,7 +2883,7 @@ __global__ void __launch_bounds__(NT, 1) list_merge_kernel(DecodeParams p, int s
 template <int PER>
 __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodeParams p, int capw, int seq_K,
                                                                       int sel_cap, int merge_ctas,
-                                                                      unsigned int* step_done) {
+                                                                      unsigned int* step_done, int pf_cap) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     if (static_cast<int>(blockIdx.x) >= merge_ctas) {
         row_scan_body<false, true>(p, capw, 1, smem_raw, step_done);
@@ -2824,18 +2899,28 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(DecodePa
     __syncthreads();
     if (sh_bad) return;
     const int T = p.desc[0].T;
+    // after the merge arrays: each example's beams (examples in turn), then
+    // each example's prefetch block
+    const int per_cta = (p.B + merge_ctas - 1) / merge_ctas;
+    const size_t beams_at = align16(list_merge_smem(kFusedThreads, sel_cap, seq_K));
+    const size_t pf_at = beams_at + align16(static_cast<size_t>(per_cta > 1 ? per_cta : 0) * 3 * seq_K * sizeof(float));
+    const size_t pf_stride = merge_prefetch_bytes(pf_cap, seq_K);
+    if (pf_cap > 0 && threadIdx.x == 0)
+        for (int j = 0; j < per_cta; ++j) *reinterpret_cast<int*>(smem_raw + pf_at + j * pf_stride) = 0;
+    auto pfb_of = [&](int j) { return pf_cap > 0 ? smem_raw + pf_at + j * pf_stride : nullptr; };
     if (merge_ctas >= p.B) {
-        list_merge_body<kFusedThreads, PER>(p, blockIdx.x, 0, T, nullptr, seq_K, sel_cap, smem_raw, step_done);
+        list_merge_body<kFusedThreads, PER>(p, blockIdx.x, 0, T, nullptr, seq_K, sel_cap, smem_raw, step_done,
+                                            nullptr, true, pfb_of(0), pf_cap);
         return;
     }
     // examples in turn, one step at a time, each one's beams in shared memory
-    float* beams_area = reinterpret_cast<float*>(smem_raw + list_merge_smem(kFusedThreads, sel_cap, seq_K));
+    float* beams_area = reinterpret_cast<float*>(smem_raw + beams_at);
     for (int t = 0; t < T; ++t) {
         int j = 0;
         for (int e = blockIdx.x; e < p.B; e += merge_ctas, ++j) {
             float* beams = beams_area + static_cast<size_t>(j) * 3 * seq_K;
             if (!list_merge_body<kFusedThreads, PER>(p, e, t, t + 1, nullptr, seq_K, sel_cap, smem_raw, step_done, beams,
-                                                     t == 0 && j == 0))
+                                                     t == 0 && j == 0, pfb_of(j), pf_cap))
                 return;
         }
     }
@@ -4028,16 +4113,18 @@ cudaError_t launch_step_merge(const DecodeParams& p, int max_K, int max_C, int m
         // compact merge: candidate keys in registers, radix select, ranking by counting
         constexpr int nt = kListMergeThreads;
         const int sel_cap = list_merge_sel_cap(max_N, nt);
-        const size_t smem = list_merge_smem(nt, sel_cap, max_K);
+        // the next step's lists are prefetched into shared memory
+        const int pf_cap = (M + max_ext + 1) & ~1;
+        const size_t smem = align16(list_merge_smem(nt, sel_cap, max_K)) + merge_prefetch_bytes(pf_cap, max_K);
         const int per = M + max_ext <= nt * 4 ? 4 : (M + max_ext <= nt * 5 ? 5 : 8);
         const void* fn = per == 4 ? reinterpret_cast<const void*>(list_merge_kernel<nt, 4>)
                                   : (per == 5 ? reinterpret_cast<const void*>(list_merge_kernel<nt, 5>)
                                               : reinterpret_cast<const void*>(list_merge_kernel<nt, 8>));
         cudaError_t err = ensure_dynamic_smem(fn, smem);
         if (err != cudaSuccess) return err;
-        if (per == 4) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
-        else if (per == 5) list_merge_kernel<nt, 5><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
-        else list_merge_kernel<nt, 8><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap);
+        if (per == 4) list_merge_kernel<nt, 4><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap, pf_cap);
+        else if (per == 5) list_merge_kernel<nt, 5><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap, pf_cap);
+        else list_merge_kernel<nt, 8><<<p.B, nt, smem, stream>>>(p, max_K, sel_cap, pf_cap);
         return counted(cudaGetLastError());
     }
     int cand_cap = M;
@@ -4085,13 +4172,31 @@ cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int
     const int capw = row_scan_capw(max_C + max_ext);
     const int sel_cap = list_merge_sel_cap(max_N, kFusedThreads);
     size_t smem = static_cast<size_t>(kFusedThreads / 32) * row_scan_warp_bytes(capw, false);
-    // a merge CTA with several examples keeps their beams after its arrays
-    const int per_cta = (p.B + merge_ctas - 1) / merge_ctas;
-    const size_t msmem = list_merge_smem(kFusedThreads, sel_cap, max_K) +
-                         (per_cta > 1 ? static_cast<size_t>(per_cta) * 3 * max_K * sizeof(float) : 0);
-    if (msmem > smem) smem = msmem;
-    if (smem > static_cast<size_t>(227) * 1024) return cudaErrorNotSupported;
     const int per = M <= kFusedThreads * 4 ? 4 : (M <= kFusedThreads * 5 ? 5 : 8);
+    // the dynamic shared memory a CTA can have beside the kernel's static arrays
+    size_t smem_max = 0;
+    {
+        const void* f = per == 4 ? reinterpret_cast<const void*>(fused_decode_kernel<4>)
+                                 : (per == 5 ? reinterpret_cast<const void*>(fused_decode_kernel<5>)
+                                             : reinterpret_cast<const void*>(fused_decode_kernel<8>));
+        cudaFuncAttributes fa{};
+        int dev = 0, optin = 0;
+        cudaError_t e = cudaFuncGetAttributes(&fa, f);
+        if (e == cudaSuccess) e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return e;
+        smem_max = static_cast<size_t>(optin) > fa.sharedSizeBytes ? static_cast<size_t>(optin) - fa.sharedSizeBytes : 0;
+    }
+    // a merge CTA with several examples keeps their beams after its arrays,
+    // then each example's prefetch block (left out when it does not fit)
+    const int per_cta = (p.B + merge_ctas - 1) / merge_ctas;
+    const size_t mbase = align16(list_merge_smem(kFusedThreads, sel_cap, max_K)) +
+                         align16(static_cast<size_t>(per_cta > 1 ? per_cta : 0) * 3 * max_K * sizeof(float));
+    int pf_cap = (M + 1) & ~1;
+    if (mbase + static_cast<size_t>(per_cta) * merge_prefetch_bytes(pf_cap, max_K) > smem_max) pf_cap = 0;
+    const size_t msmem = mbase + (pf_cap ? static_cast<size_t>(per_cta) * merge_prefetch_bytes(pf_cap, max_K) : 0);
+    if (msmem > smem) smem = msmem;
+    if (smem > smem_max) return cudaErrorNotSupported;
     const void* fn = per == 4 ? reinterpret_cast<const void*>(fused_decode_kernel<4>)
                               : (per == 5 ? reinterpret_cast<const void*>(fused_decode_kernel<5>)
                                           : reinterpret_cast<const void*>(fused_decode_kernel<8>));
@@ -4103,9 +4208,9 @@ cudaError_t launch_fused_decode(const DecodeParams& p, int max_K, int max_C, int
     const int grid = per_sm * num_sms;
     if (per_sm < 1 || grid <= merge_ctas) return cudaErrorNotSupported;
     DecodeParams pp = p;
-    int a_capw = capw, a_seq = max_K, a_sel = sel_cap, a_m = merge_ctas;
+    int a_capw = capw, a_seq = max_K, a_sel = sel_cap, a_m = merge_ctas, a_pf = pf_cap;
     unsigned int* a_done = step_done;
-    void* args[] = {&pp, &a_capw, &a_seq, &a_sel, &a_m, &a_done};
+    void* args[] = {&pp, &a_capw, &a_seq, &a_sel, &a_m, &a_done, &a_pf};
     err = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kFusedThreads), args, smem, stream);
     return counted(err);
 }

@@ -595,6 +595,8 @@ void decode(const Options& opt, const float* d_x, int V, const std::vector<Examp
         for (dbs_dev::ExampleDesc& d : desc) {
             int ext = std::min(kBeam0Extra, d.N - d.C);
             ext = std::min(ext, dbs_dev::kListMergeMaxCandidates - d.K * d.C);
+            // (the fused launch's scan warps hold lists of up to 192 in shared memory)
+            if (fused) ext = std::min(ext, 192 - d.C);
             d.ext0 = std::max(0, ext);
             max_ext = std::max(max_ext, d.ext0);
         }
