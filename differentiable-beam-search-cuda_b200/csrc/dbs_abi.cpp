@@ -109,6 +109,42 @@ struct CallStream {
     }
 };
 
+// A calling thread's stream and pinned staging buffer on the current device,
+// kept for the thread's later calls: the per-example host-buffer backward
+// moves a few small arrays each way, and a stream created per call or a
+// pageable copy per array cost more than the kernel. Never freed (the
+// process may outlive the CUDA runtime's own teardown order).
+struct ThreadStaging {
+    int device = -1;
+    cudaStream_t s = nullptr;
+    char* pinned = nullptr;
+    size_t bytes = 0;
+};
+ThreadStaging& thread_staging(size_t need) {
+    thread_local std::vector<ThreadStaging> per_device;
+    int dev = 0;
+    dbs_host::check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    ThreadStaging* t = nullptr;
+    for (ThreadStaging& c : per_device)
+        if (c.device == dev) t = &c;
+    if (!t) {
+        per_device.push_back(ThreadStaging{});
+        t = &per_device.back();
+        t->device = dev;
+        dbs_host::check_cuda(cudaStreamCreateWithFlags(&t->s, cudaStreamNonBlocking), "cudaStreamCreate");
+    }
+    if (t->bytes < need) {
+        if (t->pinned) dbs_host::check_cuda(cudaFreeHost(t->pinned), "cudaFreeHost(staging)");
+        t->pinned = nullptr;
+        t->bytes = 0;
+        const size_t n = std::max(need + need / 4, static_cast<size_t>(64) << 10);
+        dbs_host::check_cuda(cudaHostAlloc(reinterpret_cast<void**>(&t->pinned), n, cudaHostAllocDefault),
+                             "cudaHostAlloc(staging)");
+        t->bytes = n;
+    }
+    return *t;
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -593,18 +629,22 @@ std::unique_ptr<DBSBackwardHandle> run_backward(DBSDecoderHandle* h, const DBSRe
     auto out = std::make_unique<DBSBackwardHandle>();
     out->sparse = sparse;
     const size_t pool = static_cast<size_t>(e.T) * e.P;
-    CallStream cs(nullptr);
-    cudaStream_t s = cs.s;
     const size_t nsp = static_cast<size_t>(e.T) * (e.K + e.P);
-    DeviceBuffer tb(sel * (4 * 3 + 1 + 4 + 4) + pool * (4 * 4 + 1 + 4) + e.K * 8 + 32 * 16, s);
-    char* cur = tb.as<char>();
+    // inputs packed at their device offsets in pinned memory, one copy up;
+    // results read back through the same buffer
+    const size_t in_bytes = sel * (4 * 3 + 1 + 4 + 4) + pool * (4 * 4 + 1 + 4) + e.K * 8 + 32 * 16;
+    ThreadStaging& ts = thread_staging(std::max(in_bytes, nsp * 12 + 64));
+    cudaStream_t s = ts.s;
+    DeviceBuffer tb(in_bytes, s);
+    char* base = tb.as<char>();
+    char* cur = base;
     auto take = [&](size_t n) {
         char* p = cur;
         cur += (n + 15) & ~static_cast<size_t>(15);
         return p;
     };
     auto h2d = [&](void* dst, const void* src, size_t n) {
-        if (n) dbs_host::check_cuda(cudaMemcpyAsync(dst, src, n, cudaMemcpyHostToDevice, s), "stage trace");
+        if (n) std::memcpy(ts.pinned + (static_cast<char*>(dst) - base), src, n);
     };
     dbs_host::BackwardInputs in;
     auto* d_par = reinterpret_cast<int32_t*>(take(sel * 4));
@@ -653,6 +693,8 @@ std::unique_ptr<DBSBackwardHandle> run_backward(DBSDecoderHandle* h, const DBSRe
         in.grad_final = d_gf;
     }
     auto* d_gi = reinterpret_cast<float*>(take(static_cast<size_t>(e.K) * 4));
+    const size_t staged = static_cast<size_t>(reinterpret_cast<char*>(d_gi) - base);
+    dbs_host::check_cuda(cudaMemcpyAsync(base, ts.pinned, staged, cudaMemcpyHostToDevice, s), "stage trace");
     std::vector<ExampleSpec> spec(1);
     spec[0].T = e.T;
     spec[0].K = e.K;
@@ -673,21 +715,25 @@ std::unique_ptr<DBSBackwardHandle> run_backward(DBSDecoderHandle* h, const DBSRe
     }
     dbs_host::backward(bopt, e.V, spec, L, in, bo, s, true);
     host_alloc(out->grad_initial, static_cast<size_t>(e.K), 0.0f);
-    dbs_host::check_cuda(cudaMemcpyAsync(out->grad_initial.data(), d_gi, static_cast<size_t>(e.K) * 4,
-                                         cudaMemcpyDeviceToHost, s),
-                         "read grad_initial");
+    // grad_initial and the count (adjacent on the device) in one copy
+    const size_t gi_bytes = static_cast<size_t>(reinterpret_cast<char*>(sparse ? reinterpret_cast<char*>(bo.sparse_counts) + 8
+                                                                                : reinterpret_cast<char*>(d_gi) + e.K * 4) -
+                                                reinterpret_cast<char*>(d_gi));
+    dbs_host::check_cuda(cudaMemcpyAsync(ts.pinned, d_gi, gi_bytes, cudaMemcpyDeviceToHost, s), "read grad_initial");
+    dbs_host::check_cuda(cudaStreamSynchronize(s), "backward");
+    std::memcpy(out->grad_initial.data(), ts.pinned, static_cast<size_t>(e.K) * 4);
     if (sparse) {
-        dbs_host::check_cuda(cudaMemcpyAsync(&nnz, bo.sparse_counts, 8, cudaMemcpyDeviceToHost, s), "read nnz");
-        dbs_host::check_cuda(cudaStreamSynchronize(s), "backward");
+        std::memcpy(&nnz, ts.pinned + (reinterpret_cast<char*>(bo.sparse_counts) - reinterpret_cast<char*>(d_gi)), 8);
         host_alloc(out->indices, static_cast<size_t>(nnz), int64_t{0});
         host_alloc(out->values, static_cast<size_t>(nnz), 0.0f);
         if (nnz) {
-            dbs_host::check_cuda(cudaMemcpyAsync(out->indices.data(), bo.sparse_indices, nnz * 8,
+            // indices and values are adjacent on the device: one copy
+            dbs_host::check_cuda(cudaMemcpyAsync(ts.pinned, bo.sparse_indices, nsp * 8 + nnz * 4,
                                                  cudaMemcpyDeviceToHost, s),
-                                 "read sparse indices");
-            dbs_host::check_cuda(cudaMemcpyAsync(out->values.data(), bo.sparse_values, nnz * 4,
-                                                 cudaMemcpyDeviceToHost, s),
-                                 "read sparse values");
+                                 "read sparse entries");
+            dbs_host::check_cuda(cudaStreamSynchronize(s), "backward");
+            std::memcpy(out->indices.data(), ts.pinned, static_cast<size_t>(nnz) * 8);
+            std::memcpy(out->values.data(), ts.pinned + nsp * 8, static_cast<size_t>(nnz) * 4);
         }
     } else {
         host_alloc(out->grad_log_probs, dense_count, 0.0f);
