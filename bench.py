@@ -236,6 +236,41 @@ def constrained_loop(args):
 # ---------------------------------------------------------------------------
 # shared measurement helpers
 # ---------------------------------------------------------------------------
+def warm_up(step, args, world, device, sync_every, sync=None):
+    """Run the warm-up steps: at least max(3, --warmup), then as many more as
+    --warmup-seconds asks for, estimated from the first ones. Every rank runs
+    the same number of steps (a step may hold a collective, so the ranks
+    agree on the count, by one all-reduce after the fixed steps, before any
+    rank runs more). `sync` waits for the device (default: CUDA). Returns
+    the number of steps run."""
+    import torch
+    import torch.distributed as dist
+    if sync is None:
+        sync = torch.cuda.synchronize
+    n_min = max(3, args.warmup)
+    t0 = time.perf_counter()
+    for i in range(n_min):
+        step()
+        if (i + 1) % sync_every == 0:
+            sync()
+    sync()
+    elapsed = time.perf_counter() - t0
+    extra = 0
+    if elapsed < args.warmup_seconds:
+        per_step = max(elapsed / n_min, 1e-6)
+        extra = min(100000, int((args.warmup_seconds - elapsed) / per_step) + 1)
+    if world > 1:
+        t = torch.tensor([extra], dtype=torch.int64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        extra = int(t.item())
+    for i in range(extra):
+        step()
+        if (i + 1) % sync_every == 0:
+            sync()
+    sync()
+    return n_min + extra
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -714,21 +749,7 @@ def run_config3(args, rank, world, local):
             pk_val.copy_(sp_val[:, :SK])
             dist.all_gather_into_tensor(gathered, packet)
 
-    warm_steps = 0
-    t_warm = time.perf_counter()
-    while warm_steps < max(3, args.warmup) or time.perf_counter() - t_warm < args.warmup_seconds:
-        step()
-        warm_steps += 1
-        if warm_steps % 20 == 0:
-            torch.cuda.synchronize()
-    torch.cuda.synchronize()
-    if world > 1:   # every rank ran the same number of steps before the timed region
-        wt = torch.tensor([warm_steps], dtype=torch.int64, device=device)
-        dist.all_reduce(wt, op=dist.ReduceOp.MAX)
-        for _ in range(int(wt.item()) - warm_steps):
-            step()
-        warm_steps = int(wt.item())
-        torch.cuda.synchronize()
+    warm_steps = warm_up(step, args, world, device, 20)
     # the gathered counts bound the gathered entries (grad_final only)
     if world > 1:
         gc = torch.stack([gathered[r * off + offs["sparse_counts"][0]:
@@ -969,21 +990,7 @@ def run_config2(args, rank, world, local):
         y = ext.final_scores(x, opts)
         y.sum().backward()
 
-    warm_steps = 0
-    t_warm = time.perf_counter()
-    while warm_steps < max(3, args.warmup) or time.perf_counter() - t_warm < args.warmup_seconds:
-        step()
-        warm_steps += 1
-        if warm_steps % 50 == 0:
-            torch.cuda.synchronize()
-    torch.cuda.synchronize()
-    if world > 1:
-        wt = torch.tensor([warm_steps], dtype=torch.int64, device=device)
-        dist.all_reduce(wt, op=dist.ReduceOp.MAX)
-        for _ in range(int(wt.item()) - warm_steps):
-            step()
-        warm_steps = int(wt.item())
-        torch.cuda.synchronize()
+    warm_steps = warm_up(step, args, world, device, 50)
 
     uuid = str(torch.cuda.get_device_properties(device).uuid)
     sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)

@@ -108,3 +108,47 @@ def test_compare_with_reference_flags_a_difference():
     assert "tokens" in bench.compare_with_reference(bad, ref, "ex")
     bad = dict(ours, sparse_values=np.array([1.0, 1.001], np.float32))
     assert "sparse values" in bench.compare_with_reference(bad, ref, "ex")
+
+
+def _warm_up_worker(rank, world, port, path):
+    # ranks whose steps take different times must still run the same number
+    # of warm-up steps: each step holds a collective, so a rank that stopped
+    # early would leave the others waiting in it
+    import time
+    import types
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        sys.path.insert(0, ROOT)
+        import bench
+        count = [0]
+        buf = torch.zeros(4)
+        out = torch.zeros(4 * world)
+
+        def step():
+            time.sleep(0.002 if rank == 0 else 0.02)
+            dist.all_gather_into_tensor(out, buf)
+            count[0] += 1
+
+        args = types.SimpleNamespace(warmup=3, warmup_seconds=0.3)
+        if rank == 1:
+            time.sleep(0.2)   # its warm-up clock starts later than rank 0's
+        n = bench.warm_up(step, args, world, torch.device("cpu"), 5, sync=lambda: None)
+        counts = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(counts, torch.tensor([count[0]], dtype=torch.int64))
+        if rank == 0:
+            with open(path, "w") as f:
+                f.write(json.dumps({"n": n, "counts": [int(c.item()) for c in counts]}))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_warm_up_runs_the_same_steps_on_every_rank(tmp_path):
+    import torch.multiprocessing as mp
+    path = tmp_path / "warm.json"
+    mp.start_processes(_warm_up_worker, args=(2, 29637, str(path)), nprocs=2, start_method="spawn")
+    got = json.loads(path.read_text())
+    assert got["counts"][0] == got["counts"][1] == got["n"] >= 3
