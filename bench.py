@@ -44,6 +44,12 @@ Warm-up: at least --warmup steps and at least --warmup-seconds of steps,
 since a freshly started GPU runs the first seconds measurably slower; the
 line's "warmup" is the number of warm-up steps run.
 
+`--config 4`: the 512-example constrained variable batch (V=128256, all
+sequence constraints) on one GPU, decoded in eight 64-example slices whose
+decodes are timed with the slice resident; its CPU arm is the reference
+library's dbs_decode_constrained_ex on a 16-example sample (see
+run_config4).
+
 `--impl reference` times only the reference CPU arm (rank 0 prints; other
 ranks exit without work).
 """
@@ -83,7 +89,7 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=3, choices=(2, 3, 5),
+    ap.add_argument("--config", type=int, default=3, choices=(2, 3, 4, 5),
                     help="3: the large-beam batch (default, the bench line); 2: the torch final_scores batch; "
                          "5: the single B=1 T=256 K=16 V=256000 example (one GPU)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -172,6 +178,223 @@ def pool_decode_loop(args):
         ext.device_decode(x, opts, with_pool=True, with_weights=True)
     torch.cuda.synchronize()
     print(f"pool decode x{args.steps} done")
+
+
+def constrained_batch4():
+    """Config 4: steps, beams and the banned row of the 512-example
+    constrained variable batch (seeded)."""
+    import numpy as np
+    rng = np.random.default_rng(4)
+    B, maxT, V = 512, 128, 128256
+    steps_all = rng.integers(8, maxT + 1, B).astype(np.int32)
+    beams_all = rng.choice(np.array([1, 2, 4, 8, 16], np.int32), B).astype(np.int32)
+    banned_row = np.zeros(V, np.uint8)
+    banned_row[rng.choice(V, 256, replace=False)] = 1
+    return steps_all, beams_all, banned_row
+
+
+def run_config4(args, rank, world, local):
+    """Config 4: the 512-example constrained variable batch (T_b in [8, 128],
+    K_b in {1, 2, 4, 8, 16}, V = 128256; 256 banned ids, forced token 1 at
+    step 0, minimum length 8 before EOS 2, repetition penalty 1.2, no
+    repeated 3-gram) through dbs_device_decode_batch_variable_ex, in eight
+    64-example slices of the padded [64, 128, 16, 128256] layout (67 GB
+    each; the whole padded batch would be 538 GB). Each slice's log-probs
+    are generated on the device, then its decode is timed --steps times
+    with CUDA events; a step is one decode of every slice, so ms_per_step is
+    the sum of the slices' mean times. The CPU arm is the reference
+    library's dbs_decode_constrained_ex on a sample of slice 0's examples,
+    16 at a time on host threads; its outputs are compared with this run's."""
+    import numpy as np
+    import torch
+    import dbs_ctypes as dc
+    import torch_dbs_extension as ext
+    if world > 1:
+        raise SystemExit("--config 4 runs on one GPU (its slices would split by examples like config 3)")
+    steps_all, beams_all, banned_row = constrained_batch4()
+    B, maxT, maxK, V, SL = 512, 128, 16, 128256, 64
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lib = ext._library()
+    opts = ext.DBSOptions(beam_size=maxK, eos_token=2, min_length=8)
+    h = ext._handle(opts)
+    n_ref = 0 if args.no_cpu_baseline else min(args.ref_sample, SL)
+    elems = int((steps_all.astype(np.int64) * beams_all).sum()) * V
+    alg = int(((steps_all.astype(np.int64) * beams_all) - (beams_all - 1)).sum()) * V * 4
+    slice_ms, scan_ms, launches, t_gen = [], [], 0, 0.0
+    sample = None
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    for s0 in range(0, B, SL):
+        steps = np.ascontiguousarray(steps_all[s0:s0 + SL])
+        beams = np.ascontiguousarray(beams_all[s0:s0 + SL])
+        nb = len(steps)
+        t0 = time.perf_counter()
+        x = torch.zeros((nb, maxT, maxK, V), dtype=torch.float32, device=dev)
+        g = torch.Generator(device=dev)
+        for b in range(nb):
+            g.manual_seed(4 * 1_000_003 + s0 + b)
+            T, K = int(steps[b]), int(beams[b])
+            z = torch.empty((T, K, V), device=dev)
+            z.normal_(generator=g)
+            x[b, :T, :K] = torch.log_softmax(1.5 * z, dim=-1)
+            del z
+        eos = np.full(nb, 2, np.int32)
+        minl = np.full(nb, 8, np.int32)
+        banned = torch.tensor(np.tile(banned_row, (nb, 1)), device=dev)
+        forced_np = np.full((nb, maxT), -1, np.int32)
+        forced_np[:, 0] = 1
+        forced = torch.tensor(forced_np, device=dev)
+        torch.cuda.synchronize()
+        t_gen += time.perf_counter() - t0
+        sel = int((steps.astype(np.int64) * beams).sum())
+        fin = int(beams.sum())
+        sel_names = ("parents", "tokens", "lengths", "from_logprob", "raw_scores", "scores", "weights")
+        out = {}
+        so = dc.DBSDeviceDecodeOutputs()
+        for name, _ in dc.DBSDeviceDecodeOutputs._fields_:
+            n = sel if name in sel_names else (fin if name.startswith("final") else 8 * sel)
+            dt = torch.uint8 if "from_logprob" in name else (
+                torch.int32 if name.split("_")[-1] in ("parents", "tokens", "lengths") else torch.float32)
+            out[name] = torch.empty(n, dtype=dt, device=dev)
+            setattr(so, name, out[name].data_ptr())
+
+        def step():
+            rc = lib.dbs_device_decode_batch_variable_ex(
+                h, ext._vp(x), nb, maxT, maxK, V, steps.ctypes.data_as(ctypes.c_void_p),
+                beams.ctypes.data_as(ctypes.c_void_p), eos.ctypes.data_as(ctypes.c_void_p),
+                minl.ctypes.data_as(ctypes.c_void_p), ext._vp(banned), ext._vp(forced), ctypes.c_float(1.2), 3,
+                ctypes.byref(so), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+            if rc != 0:
+                raise RuntimeError("dbs_device_decode_batch_variable_ex: " + lib.dbs_last_error(h).decode())
+
+        for _ in range(max(3, args.warmup) if s0 == 0 else 1):
+            step()
+        torch.cuda.synchronize()
+        if s0 == 0:
+            sampler.start()
+            time.sleep(0.3)
+        lib.dbs_device_profile(-1)
+        lib.dbs_device_profile_kernels(1 << dbs_ctypes_index(dc, "row_scan"))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        n0 = kernel_launches(lib)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        launches += kernel_launches(lib) - n0
+        lib.dbs_device_profile(0)
+        slice_ms.append(e0.elapsed_time(e1) / args.steps)
+        scan_ms.append(read_profile(lib, dc)["row_scan"]["total_ms"] / args.steps)
+        if s0 == 0 and n_ref:
+            # this run's results for the CPU arm's sample
+            sel_off = np.concatenate([[0], np.cumsum(steps.astype(np.int64) * beams)])
+            fin_off = np.concatenate([[0], np.cumsum(beams.astype(np.int64))])
+            tok = out["tokens"].cpu().numpy()
+            fs = out["final_scores"].cpu().numpy()
+            sample = []
+            for b in range(n_ref):
+                T, K = int(steps[b]), int(beams[b])
+                sample.append({"x": np.ascontiguousarray(x[b, :T, :K].cpu().numpy()), "T": T, "K": K,
+                               "tokens": tok[sel_off[b]:sel_off[b + 1]].copy(),
+                               "final": fs[fin_off[b]:fin_off[b + 1]].copy()})
+        del x, banned, forced, out
+        torch.cuda.empty_cache()
+    clocks = sampler.stop()
+    ms = float(sum(slice_ms))
+    rs = float(sum(scan_ms))
+    peak, peak_kind = measured_peaks()
+    achieved = alg / (rs / 1e3) / 1e9 if rs > 0 else None
+    cpu, parity = None, "not run: no CPU baseline requested" if not n_ref else None
+    if n_ref:
+        r = reference_run4(sample, banned_row, V)
+        if r is None:
+            parity = "not run: the reference library is not built"
+        else:
+            cpu = {"value": r[0], "unit": "elem/s", "cores": r[1], "kind": "reference", "sample": r[2]}
+            bad = [b for b, (want, got) in enumerate(zip(r[3], sample))
+                   if not (np.array_equal(want["tokens"], got["tokens"]) and
+                           np.array_equal(want["final"], got["final"]))]
+            parity = (f"ok: {n_ref} examples identical to the reference library (tokens, final scores)" if not bad
+                      else f"MISMATCH in examples {bad}")
+    line = {
+        "metric": "log-prob elems/s (sum of T_b*K_b*V) constrained variable batch", "value": elems / (ms / 1e3),
+        "unit": "elem/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "none (one GPU)", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic: log_softmax(1.5 N(0,1)) over V per live row, generated on the device (seeded)",
+        "config": {"workload": "dbs_device_decode_batch_variable_ex, B=512 T_b in [8,128] K_b in {1,2,4,8,16} "
+                               "V=128256, 256 banned ids, forced token 1 at step 0, min length 8 before EOS 2, "
+                               "repetition penalty 1.2, no repeated 3-gram", "global_batch": 512, "seq_len": 128,
+                   "vocab": V, "slices": "8 x 64 examples, padded [64,128,16,128256] (67 GB each), decodes timed "
+                                          "per slice with the slice resident",
+                   "l2": "inputs larger than L2; no flush needed"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": (achieved / peak) if achieved else None, "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "row_scan_kernel", "algorithmic_bytes_per_launch": alg,
+                     "unit_of_launch": "all eight slices' row scans", "avg_launch_ms": rs},
+        "cpu_baseline": cpu, "parity": parity,
+        "e2e": {"value": None, "unit": "elem/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+                "note": "not measured: the padded host layout of the batch is 538 GB"},
+        "gpu_launches": launches, "slice_ms": slice_ms, "clocks": clocks, "input_generation_s": t_gen,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def dbs_ctypes_index(dc, name):
+    return dc.PROFILED_KERNELS.index(name)
+
+
+def reference_run4(sample, banned_row, V, budget_s=10.0):
+    """Config 4's CPU arm: the reference library's dbs_decode_constrained_ex
+    per example (src/differentiable_beam.cpp:3438-3482), the sample's
+    examples 16 at a time on host threads (the call takes one example).
+    Returns (elems/s, threads, sample text, outputs) or None when the
+    reference library is not built."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import dbs_ctypes as dc
+    from oracle import reference_library_path
+    path = reference_library_path()
+    if not path or not os.path.exists(path):
+        return None
+    lib = dc.load_library(path, device_api=False)
+    threads = min(16, os.cpu_count() or 1)
+    decs = {}
+    for ex in sample:
+        if ex["K"] not in decs:
+            decs[ex["K"]] = [dc.Decoder(lib, dc.Options(beam_size=ex["K"], eos_token=2, min_length=8))
+                             for _ in range(threads)]
+
+    def one(i):
+        ex = sample[i]
+        dec = decs[ex["K"]][i % threads]
+        forced = np.full(ex["T"], -1, np.int32)
+        forced[0] = 1
+        r = dec.decode_constrained_ex(ex["x"], ex["T"], V, banned=banned_row, forced=forced, min_length=8,
+                                      repetition_penalty=1.2, no_repeat_ngram_size=3)
+        res = dc.read_result(lib, r)
+        lib.dbs_free_result(r)
+        return {"tokens": res["tokens"].ravel(), "final": res["final_scores"].ravel()}
+
+    outs = None
+    reps = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        while True:
+            outs = list(pool.map(one, range(len(sample))))
+            reps += 1
+            if time.perf_counter() - t0 >= budget_s or reps >= 20:
+                break
+    dt = time.perf_counter() - t0
+    el = sum(ex["T"] * ex["K"] for ex in sample) * V * reps
+    for ds in decs.values():
+        for d in ds:
+            d.close()
+    return (el / dt, threads, f"{reps} x {len(sample)} examples of slice 0 via dbs_decode_constrained_ex "
+                             f"({threads} host threads, one example per call)", outs)
 
 
 def constrained_loop(args):
@@ -1146,6 +1369,8 @@ def main():
         return
     if args.config == 2:
         run_config2(args, rank, world, local)
+    elif args.config == 4:
+        run_config4(args, rank, world, local)
     else:
         if args.config == 5 and world > 1:
             raise SystemExit("--config 5 runs on one GPU (its one example does not split by examples)")
