@@ -71,6 +71,7 @@ PKG = os.path.join(ROOT, "differentiable-beam-search-cuda_b200")
 sys.path.insert(0, os.path.join(PKG, "python"))
 
 METRIC = "log-prob elems/s (B·T·K·V) fwd+sparse bwd; % B200 HBM BW; 1/2/4/8 GPU"
+METRIC4 = "log-prob elems/s (sum of T_b*K_b*V) constrained variable batch"
 SEED = 0
 # config 2 (torch final_scores, per GPU)
 WORKLOAD = dict(B=64, T=32, K=8, V=32000)
@@ -320,7 +321,7 @@ def run_config4(args, rank, world, local):
             parity = (f"ok: {n_ref} examples identical to the reference library (tokens, final scores)" if not bad
                       else f"MISMATCH in examples {bad}")
     line = {
-        "metric": "log-prob elems/s (sum of T_b*K_b*V) constrained variable batch", "value": elems / (ms / 1e3),
+        "metric": METRIC4, "value": elems / (ms / 1e3),
         "unit": "elem/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
         "ms_per_step": ms, "higher_is_better": True, "scaling": "none (one GPU)", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic: log_softmax(1.5 N(0,1)) over V per live row, generated on the device (seeded)",
@@ -788,7 +789,10 @@ def run_reference_arm(args, rank, world):
     Config 3: one step = the reference library on a seeded sample of
     --ref-sample examples (dbs_decode_batch with all host threads + per-example
     dbs_backward). Config 2: one full batch (decode + sparse backward + dense
-    scatter, all host threads). Rank 0 alone runs and prints."""
+    scatter, all host threads). Config 4: dbs_decode_constrained_ex on a
+    sample of the constrained batch's first examples (16 host threads).
+    Config 5: the one example, decode + sparse backward. Rank 0 alone runs
+    and prints."""
     if rank != 0:
         return
     import torch
@@ -811,6 +815,51 @@ def run_reference_arm(args, rank, world):
         config = bench_config2(B, T, K, V, 1)
         data = "synthetic: 2*N(0,1) logits + Zipf bias -1.1*ln(v+1), log_softmax over V (CPU generator)"
         scaling = "weak"
+    elif args.config == 4:
+        steps_all, beams_all, banned_row = constrained_batch4()
+        V = 128256
+        n = max(1, min(64, args.ref_sample))
+        g = torch.Generator()
+        sample = []
+        for b in range(n):
+            g.manual_seed(4 * 1_000_003 + b)
+            T, K = int(steps_all[b]), int(beams_all[b])
+            z = torch.empty((T, K, V)).normal_(generator=g)
+            sample.append({"x": torch.log_softmax(1.5 * z, dim=-1).numpy(), "T": T, "K": K})
+        vals, res = [], None
+        for i in range(max(3, args.warmup) + args.steps):
+            r = reference_run4(sample, banned_row, V, budget_s=0.0)
+            if r is None:
+                print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdbs_ref.so was not built"}))
+                return
+            res = (r[0], r[1], "reference", r[2])
+            if i >= max(3, args.warmup):
+                vals.append(r[0])
+        value = statistics.median(vals)
+        elems = int(sum(ex["T"] * ex["K"] for ex in sample)) * V
+        config = {"workload": "dbs_decode_constrained_ex per example, constrained variable batch (B=512, "
+                              "T_b in [8,128], K_b in {1,2,4,8,16}, V=128256)", "global_batch": 512, "seq_len": 128,
+                  "vocab": V, "sample": f"the first {n} examples"}
+        data = "synthetic: log_softmax(1.5 N(0,1)) over V (CPU generator), seeded per example"
+        scaling = "none (one GPU)"
+    elif args.config == 5:
+        T, K, V = (WORKLOAD5[k] for k in "TKV")
+        x = make_inputs5(torch, T, K, V, "cpu").numpy()
+        vals, res = [], None
+        for i in range(max(3, args.warmup) + args.steps):
+            res = reference_run3(x, reps_min=1, budget_s=0.0, options=OPTIONS5)
+            if res is None:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "neither oracle/_ref/libdbs_ref.so nor the oracle port was built"}))
+                return
+            if i >= max(3, args.warmup):
+                vals.append(res[0])
+        value = statistics.median(vals)
+        elems = T * K * V
+        config = {"workload": "one example, decode (pool) + sparse backward", "global_batch": 1, "seq_len": T,
+                  "beam_size": K, "vocab": V}
+        data = "synthetic: log_softmax(N(0,1)) + 8 on 64 seeded ids per step (CPU generator)"
+        scaling = "none (one GPU)"
     else:
         B, T, K, V = (WORKLOAD3[k] for k in "BTKV")
         n = max(1, min(B, args.ref_sample))
@@ -831,7 +880,8 @@ def run_reference_arm(args, rank, world):
         scaling = "strong"
     kind = res[2]
     line = {
-        "impl": "reference", "kind": kind, "metric": METRIC, "value": value, "unit": "elem/s", "n_gpus": world,
+        "impl": "reference", "kind": kind, "metric": METRIC4 if args.config == 4 else METRIC, "value": value,
+        "unit": "elem/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * elems / value, "higher_is_better": True,
         "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": data, "config": config,
         "cpu_baseline": {"value": value, "unit": "elem/s", "cores": res[1], "kind": kind,
