@@ -462,8 +462,10 @@ constexpr int kFusedMaxExamples = 64;
 // many CTAs merge (default: one per example up to 16 examples, 16 above; a
 // CTA with several examples merges them one step at a time in turn, and
 // every SM it leaves runs the scan). Measured with T = 64, K = 32,
-// V = 50257 (ms per decode + backward): 32 examples 3.36 / 3.20 / 3.18 with
-// 32 / 24 / 16 merge CTAs, 64 examples 6.30 / 5.90 / 5.64.
+// V = 50257 (ms per decode + backward, with the merge's prefetch): 32
+// examples 3.2-3.3 / 3.14-3.19 / 3.07-3.09 / 3.71-3.73 with 24 / 20 / 16 /
+// 14 merge CTAs (14: three examples on some CTAs), 64 examples 5.95 /
+// 5.78 / 5.64 / 6.18.
 bool fused_enabled() {
     static const bool on = [] {
         const char* v = std::getenv("DBS_FUSED");
