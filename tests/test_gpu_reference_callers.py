@@ -10,6 +10,13 @@ lib/libdbs.so (nothing of the reference's library is linked in):
   its CSV row;
 * its ctypes torch binding (python/torch_dbs.py, byte-compiled), loaded with
   DBS_LIBRARY pointing at lib/libdbs.so, whose forward and backward must
+  match the oracle;
+* its JAX binding (python/jax_dbs.py, byte-compiled): host callbacks that
+  call dbs_create / dbs_decode / dbs_backward and the sparse accessors
+  through ctypes, wrapped in jax.custom_vjp and jax.pure_callback. jax is
+  not installed, so an eager stand-in for those two (and for the
+  ShapeDtypeStruct / float32 names the module reads) lets the module load;
+  its forward and backward callbacks then run on lib/libdbs.so and must
   match the oracle.
 
 They are built on a host with the reference's source tree and carried to the
@@ -20,6 +27,7 @@ import importlib.util
 import os
 import subprocess
 import sys
+import types
 
 import numpy as np
 import pytest
@@ -82,3 +90,70 @@ def test_reference_torch_binding_on_the_dropin(oracle_lib, monkeypatch):
     g = np.zeros(T * K * V, dtype=np.float32)
     np.add.at(g, sp["indices"], sp["values"])
     assert_close_rel(xt.grad.numpy().ravel(), g, 1e-5, "reference binding gradient")
+
+
+def _eager_jax():
+    """The few names python/jax_dbs.py uses from jax, run eagerly: a
+    custom_vjp whose forward is the wrapped function and whose registered
+    (fwd, bwd) pair is kept for the test, and a pure_callback that calls the
+    host function on numpy arrays."""
+    jax = types.ModuleType("jax")
+    jnp = types.ModuleType("jax.numpy")
+    jnp.float32 = np.float32
+    jax.numpy = jnp
+    jax.rules = []
+
+    class _CustomVJP:
+        def __init__(self, fn):
+            self.fn = fn
+
+        def defvjp(self, fwd, bwd):
+            jax.rules.append((fwd, bwd))
+
+        def __call__(self, *args):
+            return self.fn(*args)
+
+    def pure_callback(callback, result_shape_dtype, *args):
+        out = np.asarray(callback(*(np.asarray(a) for a in args)))
+        assert out.shape == tuple(result_shape_dtype.shape) and out.dtype == result_shape_dtype.dtype
+        return out
+
+    jax.custom_vjp = _CustomVJP
+    jax.pure_callback = pure_callback
+    jax.ShapeDtypeStruct = lambda shape, dtype: types.SimpleNamespace(shape=shape, dtype=np.dtype(dtype))
+    return jax, jnp
+
+
+@pytest.mark.parametrize("kw", [
+    dict(beam_size=4),
+    dict(beam_size=5, eos_token=7, length_penalty_alpha=0.6, selected_temperature=0.7, min_length=2),
+])
+def test_reference_jax_binding_on_the_dropin(oracle_lib, monkeypatch, kw):
+    pyc = _need("jax_dbs.bytecode")
+    jax, jnp = _eager_jax()
+    monkeypatch.setitem(sys.modules, "jax", jax)
+    monkeypatch.setitem(sys.modules, "jax.numpy", jnp)
+    loader = importlib.machinery.SourcelessFileLoader("reference_jax_dbs", pyc)
+    spec = importlib.util.spec_from_loader("reference_jax_dbs", loader)
+    mod = importlib.util.module_from_spec(spec)
+    monkeypatch.setitem(sys.modules, spec.name, mod)   # its dataclasses look their module up
+    loader.exec_module(mod)
+    rng = np.random.default_rng(31 + kw["beam_size"])
+    T, K, V = 7, kw["beam_size"], 900
+    x = log_softmax_np(1.3 * rng.standard_normal((T, K, V)).astype(np.float32))
+    gout = rng.standard_normal(K).astype(np.float32)
+    opts = mod.DBSOptions(**kw)
+
+    y = mod.final_scores(x, opts, LIBDBS)            # forward: pure_callback -> dbs_decode
+    fwd, bwd = jax.rules[-1]
+    y2, saved = fwd(x)
+    (grad,) = bwd(saved, gout)                       # backward: pure_callback -> dbs_backward
+
+    want = oracle_lib.decode(oracle_lib.options(**kw), x, T, V)
+    assert np.array_equal(y, want["final_scores"])
+    assert np.array_equal(y2, want["final_scores"])
+    sp = oracle_lib.backward_sparse(want, None, None, gout)
+    g = np.zeros(T * K * V, dtype=np.float32)
+    np.add.at(g, sp["indices"], sp["values"])
+    assert grad.shape == (T, K, V)
+    assert_close_rel(grad.ravel(), g, 1e-5, "reference JAX binding gradient")
