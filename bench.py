@@ -497,10 +497,16 @@ def warm_up(step, args, world, device, sync_every, sync=None):
 
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(p):
+    try:
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
+        v = d.get("hbm_gbs")
+        if v is None:   # a nested layout: the first "hbm_gbs" one level down
+            v = next((x["hbm_gbs"] for x in d.values() if isinstance(x, dict) and "hbm_gbs" in x), None)
+        if v is not None and float(v) > 0:
+            return float(v), "measured"
+    except (OSError, ValueError, TypeError, AttributeError):
+        pass
     return 6650.0, "fallback"
 
 

@@ -88,6 +88,25 @@ def test_scatter_add_keeps_duplicate_indices():
     assert g.tolist() == [0.0, 0.75, 0.0, 1.0]
 
 
+@pytest.mark.parametrize("content,want", [
+    ('{"hbm_gbs": 6538.9, "bf16_tflops": 1500.0}', (6538.9, "measured")),
+    ('{"b200": {"hbm_gbs": 6500}}', (6500.0, "measured")),
+    ('{"bf16_tflops": 1500.0}', (6650.0, "fallback")),
+    ("not json", (6650.0, "fallback")),
+    (None, (6650.0, "fallback")),
+])
+def test_roofline_peak_from_the_measured_peaks_file(tmp_path, monkeypatch, content, want):
+    """The roofline's denominator: the measured copy bandwidth when the peaks
+    file holds one, the fallback figure (and says so) when it is absent or
+    unreadable, never an exception that would lose the bench line."""
+    sys.path.insert(0, ROOT)
+    import bench
+    if content is not None:
+        (tmp_path / "MEASURED_PEAKS.json").write_text(content)
+    monkeypatch.setattr(bench, "ROOT", str(tmp_path))
+    assert bench.measured_peaks() == want
+
+
 def test_compare_with_reference_flags_a_difference():
     """The bench's parity check of its sample against the reference's outputs."""
     sys.path.insert(0, ROOT)
