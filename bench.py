@@ -73,6 +73,9 @@ sys.path.insert(0, os.path.join(PKG, "python"))
 METRIC = "log-prob elems/s (B·T·K·V) fwd+sparse bwd; % B200 HBM BW; 1/2/4/8 GPU"
 METRIC4 = "log-prob elems/s (sum of T_b*K_b*V) constrained variable batch"
 SEED = 0
+# config 1 (the reference's own small case: four examples, launch-bound; one GPU)
+WORKLOAD1 = dict(B=4, T=4, K=4, V=32000)
+OPTIONS1 = dict(beam_size=4)
 # config 2 (torch final_scores, per GPU)
 WORKLOAD = dict(B=64, T=32, K=8, V=32000)
 OPTIONS = dict(beam_size=8, eos_token=2, length_penalty_alpha=0.2, selected_temperature=0.7)
@@ -90,9 +93,10 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=3, choices=(2, 3, 4, 5),
-                    help="3: the large-beam batch (default, the bench line); 2: the torch final_scores batch; "
-                         "5: the single B=1 T=256 K=16 V=256000 example (one GPU)")
+    ap.add_argument("--config", type=int, default=3, choices=(1, 2, 3, 4, 5),
+                    help="3: the large-beam batch (default, the bench line); 1: the B=4 T=4 K=4 V=32000 case "
+                         "(one GPU, L2 flushed between steps); 2: the torch final_scores batch; 4: the constrained "
+                         "variable batch; 5: the single B=1 T=256 K=16 V=256000 example (one GPU)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=None,
                     help="end-to-end steps (default 20 for config 2, 2 for config 3)")
@@ -144,6 +148,15 @@ def make_inputs3(torch, B, T, K, V, first_example, device):
         x[b].normal_(generator=g)
         x[b] = torch.log_softmax(x[b], dim=-1)
     return x
+
+
+def make_inputs1(torch, device):
+    """Config 1: log_softmax over V of 1.5*N(0,1) logits, [4,4,4,32000], from
+    the CPU generator seeded 0 (the same tensor on every host)."""
+    B, T, K, V = (WORKLOAD1[k] for k in "BTKV")
+    g = torch.Generator().manual_seed(SEED)
+    x = torch.log_softmax(1.5 * torch.randn((B, T, K, V), generator=g), dim=-1)
+    return x.to(device)
 
 
 def make_inputs5(torch, T, K, V, device):
@@ -682,7 +695,7 @@ def _oracle_port_run(x, steps_budget_s):
     return elems / dt, 1, "port", sample
 
 
-def reference_run3(x_host, reps_min=1, budget_s=10.0, keep_outputs=False, options=None):
+def reference_run3(x_host, reps_min=1, budget_s=10.0, keep_outputs=False, options=None, threads=None):
     """Config 3: time the reference CPU library on a sample of examples.
 
     One repetition = dbs_decode_batch over the sample (all host threads) and
@@ -691,7 +704,8 @@ def reference_run3(x_host, reps_min=1, budget_s=10.0, keep_outputs=False, option
     (src/differentiable_beam.cpp:3588-3673, :3782-3798). Returns
     (elems/s, cores, kind, sample, outputs) where outputs (keep_outputs) holds
     the last repetition's decode and backward results per example; None when
-    neither the reference library nor the oracle port is built."""
+    neither the reference library nor the oracle port is built. `threads`:
+    dbs_decode_batch's thread count (default: every host core)."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import dbs_ctypes as dc
@@ -705,7 +719,7 @@ def reference_run3(x_host, reps_min=1, budget_s=10.0, keep_outputs=False, option
     reps = 0
     t0 = time.perf_counter()
     if path is not None:
-        cores = os.cpu_count() or 1
+        cores = threads or os.cpu_count() or 1
         lib = dc.load_library(path, device_api=False)
         dec = dc.Decoder(lib, dc.Options(**(options or OPTIONS3)))
         while True:
@@ -773,6 +787,15 @@ def bench_config3(B, T, K, V, world, per_rank):
             "l2": f"inputs larger than L2 ({4 * per_rank * T * K * V / 1e9:.1f} GB per GPU); no flush needed"}
 
 
+def bench_config1(B, T, K, V):
+    return {"workload": f"C ABI device decode (pool P={8 * K} + weights) + sparse backward (grad_final=e_0), "
+                        f"B={B} T={T} K={K} V={V}, log_softmax(1.5 N(0,1)) (CPU generator, seed 0), default options",
+            "global_batch": B, "seq_len": T, "beam_size": K, "vocab": V, "examples_per_gpu": B,
+            "parallelism": "one GPU",
+            "l2": (f"inputs smaller than L2 ({4 * B * T * K * V / 1e6:.1f} MB): a 256 MB buffer is written "
+                   "between timed steps, outside each step's event pair")}
+
+
 def bench_config5(T, K, V):
     return {"workload": f"C ABI device decode (pool P={8 * K} + weights) + sparse backward (grad_final=e_0), "
                         f"B=1 T={T} K={K} V={V}, log_softmax(N(0,1) + 8 on 64 ids per step), default options",
@@ -797,8 +820,9 @@ def run_reference_arm(args, rank, world):
     dbs_backward). Config 2: one full batch (decode + sparse backward + dense
     scatter, all host threads). Config 4: dbs_decode_constrained_ex on a
     sample of the constrained batch's first examples (16 host threads).
-    Config 5: the one example, decode + sparse backward. Rank 0 alone runs
-    and prints."""
+    Config 5: the one example, decode + sparse backward. Config 1: twenty
+    repetitions of its four examples per step (dbs_decode_batch with all
+    host threads + per-example dbs_backward). Rank 0 alone runs and prints."""
     if rank != 0:
         return
     import torch
@@ -847,6 +871,24 @@ def run_reference_arm(args, rank, world):
                               "T_b in [8,128], K_b in {1,2,4,8,16}, V=128256)", "global_batch": 512, "seq_len": 128,
                   "vocab": V, "sample": f"the first {n} examples"}
         data = "synthetic: log_softmax(1.5 N(0,1)) over V (CPU generator), seeded per example"
+        scaling = "none (one GPU)"
+    elif args.config == 1:
+        B, T, K, V = (WORKLOAD1[k] for k in "BTKV")
+        x = make_inputs1(torch, "cpu").numpy()
+        reps = 20
+        vals, res = [], None
+        for i in range(max(3, args.warmup) + args.steps):
+            res = reference_run3(x, reps_min=reps, budget_s=0.0, options=OPTIONS1)
+            if res is None:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "neither oracle/_ref/libdbs_ref.so nor the oracle port was built"}))
+                return
+            if i >= max(3, args.warmup):
+                vals.append(res[0])
+        value = statistics.median(vals)
+        elems = reps * B * T * K * V
+        config = bench_config1(B, T, K, V)
+        data = "synthetic: log_softmax(1.5 N(0,1)) over V (CPU generator, seed 0)"
         scaling = "none (one GPU)"
     elif args.config == 5:
         T, K, V = (WORKLOAD5[k] for k in "TKV")
@@ -932,9 +974,10 @@ def compare_with_reference(ours, ref, label):
 
 
 def run_config3(args, rank, world, local):
-    """Configs 3 and 5: device decode (pool + weights) + sparse backward of
+    """Configs 3, 5 and 1: device decode (pool + weights) + sparse backward of
     grad_final = e_0 through the C ABI's device entry points; config 3's
-    batch is split over the ranks with an all-gather of the results."""
+    batch is split over the ranks with an all-gather of the results. Config
+    1's inputs fit in L2, so L2 is flushed before each timed step."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -948,7 +991,8 @@ def run_config3(args, rank, world, local):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     five = args.config == 5
-    W, O = (WORKLOAD5, OPTIONS5) if five else (WORKLOAD3, OPTIONS3)
+    one = args.config == 1
+    W, O = (WORKLOAD5, OPTIONS5) if five else (WORKLOAD1, OPTIONS1) if one else (WORKLOAD3, OPTIONS3)
     Bg, T, K, V = (W[k] for k in "BTKV")
     if Bg % world:
         raise SystemExit(f"the {Bg}-example batch does not split over {world} ranks")
@@ -961,7 +1005,12 @@ def run_config3(args, rank, world, local):
     h = ext._handle(opts)
 
     t_gen = time.perf_counter()
-    x = make_inputs5(torch, T, K, V, device) if five else make_inputs3(torch, Bl, T, K, V, first, device)
+    if five:
+        x = make_inputs5(torch, T, K, V, device)
+    elif one:
+        x = make_inputs1(torch, device)
+    else:
+        x = make_inputs3(torch, Bl, T, K, V, first, device)
     torch.cuda.synchronize()
     t_gen = time.perf_counter() - t_gen
 
@@ -1048,20 +1097,35 @@ def run_config3(args, rank, world, local):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
     n_launch0 = kernel_launches(lib)
-    start.record()
-    for _ in range(args.steps):
-        step()
-    end.record()
-    torch.cuda.synchronize()
+    if not one:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    else:
+        # inputs smaller than L2: a 256 MB write before each step evicts them,
+        # and each step is timed by its own event pair (the write is outside)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+        pairs = []
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            step()
+            b.record()
+            pairs.append((a, b))
+        torch.cuda.synchronize()
     launches = kernel_launches(lib) - n_launch0
     if world > 1:
         dist.barrier()
     lib.dbs_device_profile(0)
     clocks = sampler.stop()
-    ms = start.elapsed_time(end)
+    ms = start.elapsed_time(end) if not one else sum(a.elapsed_time(b) for a, b in pairs)
     rs = read_profile(lib, dbs_ctypes)["row_scan"]
 
     # per-kernel breakdown from a short separate pass with every kernel timed
@@ -1087,7 +1151,7 @@ def run_config3(args, rank, world, local):
     rs_ms = rs["total_ms"] / max(1, rs["launches"])
     alg_bytes = bench_bytes_bound(Bl, T, K, V)
     achieved = alg_bytes / (rs_ms / 1e3) / 1e9 if rs_ms > 0 else None
-    traffic = ncu_traffic_per_launch(3) if not five else None
+    traffic = ncu_traffic_per_launch(3) if not (five or one) else None
     if traffic is not None and args.batch is None:
         traffic = traffic * Bl / 32.0   # the committed capture covers 32 examples
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -1130,7 +1194,7 @@ def run_config3(args, rank, world, local):
     # end to end through the C ABI with host buffers: dbs_decode_batch on
     # pinned host log-probs (the library stages them to the device inside the
     # call), dbs_backward per example, every result read on the host
-    e2e_steps = args.e2e_steps if args.e2e_steps is not None else 2
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else (20 if one else 2)
     x_host = torch.empty((Bl if e2e_steps > 0 else 1, T, K, V), dtype=torch.float32, pin_memory=True)
     if e2e_steps > 0:
         for b0 in range(0, Bl, 16):
@@ -1202,6 +1266,9 @@ def run_config3(args, rank, world, local):
             parity = "not run: neither the reference library nor the oracle is built"
         else:
             cpu = {"value": r[0], "unit": "elem/s", "cores": r[1], "kind": r[2], "sample": r[3]}
+            if one and r[2] == "reference":   # the small case also on one host thread
+                r1 = reference_run3(x_sample, reps_min=1, budget_s=5.0, options=O, threads=1)
+                cpu["one_thread"] = {"value": r1[0], "unit": "elem/s", "cores": 1, "sample": r1[3]}
             bad = None
             for b in range(n_ref):
                 bad = compare_with_reference(ours[b], r[4][b], f"example {first + b}")
@@ -1221,8 +1288,10 @@ def run_config3(args, rank, world, local):
         "warmup": warm_steps, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32",
         "data": ("synthetic: log_softmax(N(0,1) + 8 on 64 seeded ids per step) over V, generated on the device"
-                 if five else "synthetic: log_softmax(N(0,1)) over V, generated on the device per example (seeded)"),
-        "config": bench_config5(T, K, V) if five else bench_config3(Bg, T, K, V, world, Bl),
+                 if five else "synthetic: log_softmax(1.5 N(0,1)) over V (CPU generator, seed 0), copied to the device"
+                 if one else "synthetic: log_softmax(N(0,1)) over V, generated on the device per example (seeded)"),
+        "config": (bench_config5(T, K, V) if five else bench_config1(Bg, T, K, V) if one
+                   else bench_config3(Bg, T, K, V, world, Bl)),
         "roofline": roofline,
         "step_hbm": whole,
         "cpu_baseline": cpu,
@@ -1430,6 +1499,8 @@ def main():
     else:
         if args.config == 5 and world > 1:
             raise SystemExit("--config 5 runs on one GPU (its one example does not split by examples)")
+        if args.config == 1 and world > 1:
+            raise SystemExit("--config 1 runs on one GPU (four examples: a launch-bound parity case)")
         run_config3(args, rank, world, local)
 
 

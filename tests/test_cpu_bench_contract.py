@@ -62,6 +62,26 @@ def test_reference_arm_config2():
     assert (cfg["global_batch"], cfg["seq_len"], cfg["beam_size"], cfg["vocab"]) == (64, 32, 8, 32000)
 
 
+@pytest.mark.skipif(not os.path.exists(REF_LIB), reason="reference library not built (oracle/Makefile)")
+def test_reference_arm_config1():
+    line = _check_line(_run({"RANK": "0", "WORLD_SIZE": "1"}, "--config", "1"))
+    cfg = line["config"]
+    assert (cfg["global_batch"], cfg["seq_len"], cfg["beam_size"], cfg["vocab"]) == (4, 4, 4, 32000)
+    assert "20 x 4 examples" in line["cpu_baseline"]["sample"]
+
+
+def test_config1_inputs_are_the_seeded_cpu_tensor():
+    """Config 1's log-probs come from the CPU generator seeded 0, so the GPU
+    arm and the reference arm decode the same tensor on any host."""
+    sys.path.insert(0, ROOT)
+    import torch
+    import bench
+    a = bench.make_inputs1(torch, "cpu")
+    g = torch.Generator().manual_seed(0)
+    want = torch.log_softmax(1.5 * torch.randn((4, 4, 4, 32000), generator=g), dim=-1)
+    assert a.shape == (4, 4, 4, 32000) and torch.equal(a, want)
+
+
 def test_reference_arm_other_ranks_exit_without_work():
     out = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert out.returncode == 0, out.stderr[-2000:]
