@@ -120,6 +120,9 @@ def parse_args(argv=None):
     ap.add_argument("--rows", choices=("zipf", "normal"), default="zipf",
                     help="profiling only (--pool-decode): the Zipf-biased rows of config 2, or "
                          "log_softmax(N(0,1)) rows as in config 3")
+    ap.add_argument("--default-options", action="store_true",
+                    help="profiling only (--pool-decode): the default options (beam_size K, eos -1, no length "
+                         "penalty) as in config 3, instead of config 2's")
     return ap.parse_args(argv)
 
 
@@ -187,7 +190,8 @@ def pool_decode_loop(args):
         x = make_inputs(torch, B, T, K, V, 0, device)
     else:
         x = make_inputs3(torch, B, T, K, V, 0, device)
-    opts = ext.DBSOptions(**dict(OPTIONS, beam_size=K, relaxed_pool_multiplier=args.pool_decode))
+    base = {} if args.default_options else OPTIONS
+    opts = ext.DBSOptions(**dict(base, beam_size=K, relaxed_pool_multiplier=args.pool_decode))
     for _ in range(args.steps):
         ext.device_decode(x, opts, with_pool=True, with_weights=True)
     torch.cuda.synchronize()
