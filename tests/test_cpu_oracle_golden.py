@@ -74,6 +74,55 @@ def test_oracle_live_against_reference_random(oracle_lib):
         assert_decode_equal(got, want, f"random {i}")
 
 
+def test_oracle_backward_live_against_reference_random(oracle_lib):
+    """The surrogate backward on seeded random cases beyond the fixtures,
+    against oracle/_ref directly: with grad_final alone bit-exact (indices,
+    values, grad_initial, and the dense form); with selected and relaxed
+    weight gradients too, within the reference's weight tolerance (its
+    weights use a SIMD exp)."""
+    import dbs_ctypes as dc
+    from oracle import reference_library_path
+    from parity import random_case
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+    ref = dc.load_library(path, device_api=False)
+    rng = np.random.default_rng(123)
+    for i in range(80):
+        opts, x, T, V, cons = random_case(rng)
+        x = np.ascontiguousarray(x)
+        dec = dc.Decoder(ref, dc.Options(**opts))
+        r = dec.decode_constrained_ex(x, T, V, **cons) if cons else dec.decode(x, T, V)
+        try:
+            fwd = oracle_lib.decode(oracle_lib.options(**opts), x, T, V, **cons)
+            K, P = fwd["K"], fwd["P"]
+            gfin = rng.standard_normal(K).astype(np.float32)
+            gsel = rng.standard_normal(T * K).astype(np.float32)
+            grel = rng.standard_normal(T * P).astype(np.float32)
+            b = dec.backward(r, None, None, gfin, mode="sparse")
+            want = dc.read_backward(ref, b, K=K)
+            ref.dbs_free_backward(b)
+            got = oracle_lib.backward_sparse(fwd, None, None, gfin)
+            for k in ("indices", "values", "grad_initial"):
+                assert np.array_equal(got[k], want[k]), f"random {i}: grad_final-only {k}"
+            b = dec.backward(r, gsel, grel, gfin, mode="sparse")
+            want = dc.read_backward(ref, b, K=K)
+            ref.dbs_free_backward(b)
+            got = oracle_lib.backward_sparse(fwd, gsel, grel, gfin)
+            assert_sparse_close(got, want, 8e-3, f"random {i}")
+            # the dense form (dbs_backward_dense), grad_final alone
+            b = dec.backward(r, None, None, gfin, mode="dense")
+            want = dc.read_backward(ref, b, dense_count=T * K * V, K=K)
+            ref.dbs_free_backward(b)
+            got = oracle_lib.backward_dense(fwd, None, None, gfin)
+            assert not want["sparse"]
+            for k in ("grad_log_probs", "grad_initial"):
+                assert np.array_equal(got[k], want[k]), f"random {i}: dense {k}"
+        finally:
+            ref.dbs_free_result(r)
+            dec.close()
+
+
 def test_oracle_token_filter_matches_reference(oracle_lib):
     """The token filter: same results and the same sequence of filter calls
     (batch index, step, parent, prefix, token) as the reference library."""
