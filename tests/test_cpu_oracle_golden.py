@@ -123,6 +123,46 @@ def test_oracle_backward_live_against_reference_random(oracle_lib):
             dec.close()
 
 
+@pytest.mark.parametrize("seed", range(4))
+def test_variable_batch_restatement_matches_reference(oracle_lib, seed):
+    """dbs_decode_batch_variable restated per example as the GPU tests check
+    it (the example's beam size, steps, EOS and minimum length as its
+    options, its banned row and forced prefix as constraints, its [T_b,K_b]
+    corner of the padded input), against the reference library's own
+    variable batch on the same padded input."""
+    import dbs_ctypes as dc
+    from oracle import reference_library_path
+    from parity import log_softmax_np
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+    ref = dc.load_library(path, device_api=False)
+    rng = np.random.default_rng(700 + seed)
+    B, maxT, maxK, V = 6, 7, 5, 97
+    x = log_softmax_np(rng.standard_normal((B, maxT, maxK, V)).astype(np.float32) * 1.5)
+    steps = rng.integers(1, maxT + 1, B).astype(np.int32)
+    beams = rng.integers(1, maxK + 1, B).astype(np.int32)
+    eos = rng.integers(-1, 6, B).astype(np.int32)
+    minlen = rng.integers(-1, 4, B).astype(np.int32)
+    banned = (rng.random((B, V)) < 0.1).astype(np.uint8)
+    forced = np.where(rng.random((B, maxT)) < 0.2, rng.integers(0, V, (B, maxT)), -1).astype(np.int32)
+    base = dict(beam_size=3, relaxed_pool_multiplier=4, length_penalty_alpha=0.35)
+    dec = dc.Decoder(ref, dc.Options(**base))
+    br = dec.decode_batch_variable(np.ascontiguousarray(x), B, maxT, maxK, V, steps, beams, eos, minlen, banned,
+                                   forced, threads=1)
+    try:
+        for b in range(B):
+            T, K = int(steps[b]), int(beams[b])
+            opts = dict(base, beam_size=K, eos_token=int(eos[b]), min_length=max(0, int(minlen[b])))
+            cons = dict(banned=banned[b], forced=forced[b, :T].copy(), min_length=int(minlen[b]))
+            got = oracle_lib.decode(oracle_lib.options(**opts), np.ascontiguousarray(x[b, :T, :K]), T, V, **cons)
+            want = dc.read_result(ref, ref.dbs_batch_result_at(br, b))
+            assert_decode_equal(got, want, f"seed {seed} example {b}")
+    finally:
+        ref.dbs_free_batch_result(br)
+        dec.close()
+
+
 def test_oracle_token_filter_matches_reference(oracle_lib):
     """The token filter: same results and the same sequence of filter calls
     (batch index, step, parent, prefix, token) as the reference library."""
