@@ -163,6 +163,48 @@ def test_variable_batch_restatement_matches_reference(oracle_lib, seed):
         dec.close()
 
 
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_typed_widening_matches_reference(oracle_lib, dtype):
+    """dbs_decode_typed restated as the oracle's fp32 decode of the exactly
+    widened values (as the GPU tests check it), against the reference
+    library's own typed decode of the same 16-bit words: near-zero log-probs
+    that are subnormal in fp16, -inf entries and signed zeros included."""
+    import ctypes
+    import dbs_ctypes as dc
+    from oracle import reference_library_path
+    from parity import log_softmax_np
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+    ref = dc.load_library(path, device_api=False)
+    rng = np.random.default_rng(17)
+    for i in range(12):
+        T, K, V = int(rng.integers(1, 6)), int(rng.integers(1, 6)), int(rng.integers(2, 300))
+        x = log_softmax_np(rng.standard_normal((T, K, V)).astype(np.float32) * float(rng.choice([0.5, 3.0])))
+        x[rng.random(x.shape) < 0.05] = -np.inf
+        x[rng.random(x.shape) < 0.02] = -1e-6
+        x[rng.random(x.shape) < 0.02] = -0.0
+        if dtype == "f16":
+            h = x.astype(np.float16)
+            bits = np.ascontiguousarray(h.view(np.uint16))
+            wide = h.astype(np.float32)
+            code = dc.DBS_DTYPE_F16
+        else:
+            bits = np.ascontiguousarray((x.view(np.uint32) >> 16).astype(np.uint16))
+            wide = (bits.astype(np.uint32) << 16).view(np.float32)
+            code = dc.DBS_DTYPE_BF16
+        opts = dict(beam_size=K, eos_token=int(rng.integers(-1, V)), length_penalty_alpha=0.4)
+        got = oracle_lib.decode(oracle_lib.options(**opts), np.ascontiguousarray(wide), T, V)
+        dec = dc.Decoder(ref, dc.Options(**opts))
+        r = ctypes.c_void_p()
+        rc = ref.dbs_decode_typed(dec.h, bits.ctypes.data_as(ctypes.c_void_p), code, T, V, ctypes.byref(r))
+        assert rc == 0, ref.dbs_last_error(dec.h)
+        want = dc.read_result(ref, r)
+        ref.dbs_free_result(r)
+        dec.close()
+        assert_decode_equal(got, want, f"{dtype} case {i}")
+
+
 def test_oracle_token_filter_matches_reference(oracle_lib):
     """The token filter: same results and the same sequence of filter calls
     (batch index, step, parent, prefix, token) as the reference library."""
