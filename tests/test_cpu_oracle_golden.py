@@ -205,6 +205,70 @@ def test_typed_widening_matches_reference(oracle_lib, dtype):
         assert_decode_equal(got, want, f"{dtype} case {i}")
 
 
+@pytest.mark.parametrize("K,V,T,alpha", [(4, 300, 7, 0.0), (8, 2000, 12, 0.6), (3, 50, 9, 0.3)])
+def test_model_step_restatement_matches_reference(oracle_lib, K, V, T, alpha):
+    """dbs_decode_model_steps restated as the GPU tests check it: step t is
+    filled from the tokens of step t-1 and the final scores of an oracle
+    decode of steps 0..t-1, then the whole trace decoded. Against the
+    reference library's own model-step decode with the same callback: the
+    callbacks' arguments and the results must match."""
+    import ctypes
+    import dbs_ctypes as dc
+    from oracle import reference_library_path
+    from parity import log_softmax_np
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+    ref = dc.load_library(path, device_api=False)
+    rng = np.random.default_rng(K * V + T)
+    base = rng.standard_normal((T, K, V)).astype(np.float32)
+
+    def make_step(log):
+        @dc.MODEL_STEP_FN
+        def step(user, batch, t, prev_tokens, prev_scores, k_, v_, out):
+            toks = [prev_tokens[k] for k in range(K)]
+            scs = [prev_scores[k] for k in range(K)]
+            log.append((t, tuple(toks), tuple(np.float32(v) for v in scs)))
+            row = base[t].copy()
+            for k in range(K):
+                if toks[k] >= 0:
+                    row[k, (toks[k] * 7 + 3) % V] += 3.0
+                row[k] += np.float32(0.01) * np.float32(scs[k])
+            row = log_softmax_np(row)
+            ctypes.memmove(out, row.ctypes.data, row.nbytes)
+            return 0
+        return step
+
+    opts = dict(beam_size=K, eos_token=2, length_penalty_alpha=alpha, relaxed_pool_multiplier=2)
+    log_ref = []
+    cb = make_step(log_ref)
+    dec = dc.Decoder(ref, dc.Options(**opts))
+    r = ctypes.c_void_p()
+    assert ref.dbs_decode_model_steps(dec.h, cb, None, 0, T, V, ctypes.byref(r)) == 0, ref.dbs_last_error(dec.h)
+    want = dc.read_result(ref, r)
+    ref.dbs_free_result(r)
+    dec.close()
+
+    log_orc = []
+    fill = make_step(log_orc)
+    x = np.zeros((T, K, V), dtype=np.float32)
+    toks = np.full(K, -1, np.int32)
+    scs = np.zeros(K, np.float32)
+    o = oracle_lib.options(**opts)
+    for t in range(T):
+        buf = (ctypes.c_float * (K * V))()
+        fill(None, 0, t, toks.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+             scs.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), K, V, buf)
+        x[t] = np.frombuffer(buf, dtype=np.float32).reshape(K, V)
+        if t + 1 < T:
+            part = oracle_lib.decode(o, np.ascontiguousarray(x[:t + 1]), t + 1, V)
+            toks = part["tokens"][t * K:(t + 1) * K].astype(np.int32).copy()
+            scs = part["final_scores"].astype(np.float32).copy()
+    got = oracle_lib.decode(o, x, T, V)
+    assert log_orc == log_ref
+    assert_decode_equal(got, want, "model steps")
+
+
 def test_oracle_token_filter_matches_reference(oracle_lib):
     """The token filter: same results and the same sequence of filter calls
     (batch index, step, parent, prefix, token) as the reference library."""
