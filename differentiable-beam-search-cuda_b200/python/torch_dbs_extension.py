@@ -287,6 +287,107 @@ def decode_row_sharded(x4: torch.Tensor, options: DBSOptions, with_pool: bool = 
     return trace
 
 
+def gather_examples(arrays: Dict[str, torch.Tensor], group=None) -> Dict[str, torch.Tensor]:
+    """Every rank's per-example arrays, in rank order, on every rank of `group`.
+
+    The first dimension of each tensor is this rank's examples (the same
+    count for every tensor; the other dimensions and the dtypes equal on every
+    rank). Two collectives whatever the number of arrays: an all-gather of
+    the example counts, then one all_gather_into_tensor of a packed byte
+    buffer in which each rank's share is padded to the largest share. Works
+    on NCCL (CUDA tensors) and on gloo (CPU tensors)."""
+    import torch.distributed as dist
+    if not arrays:
+        return {}
+    world = dist.get_world_size(group)
+    names = list(arrays)
+    n = int(arrays[names[0]].shape[0])
+    dev = arrays[names[0]].device
+    for name in names:
+        t = arrays[name]
+        if t.dim() < 1 or int(t.shape[0]) != n or t.device != dev:
+            raise ValueError(f"gather_examples: '{name}' must have {n} examples on {dev}")
+    counts = torch.empty(world, dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(counts, torch.tensor([n], dtype=torch.int64, device=dev), group=group)
+    counts = [int(c) for c in counts.tolist()]
+    per = max(counts)
+    layout, off = [], 0
+    for name in names:
+        t = arrays[name]
+        tail = tuple(int(s) for s in t.shape[1:])
+        ex_bytes = math.prod(tail) * t.element_size()
+        off = (off + 15) & ~15   # every array starts 16-byte aligned, so the views below hold
+        layout.append((name, off, ex_bytes, t.dtype, tail))
+        off += per * ex_bytes
+    size = (off + 15) & ~15
+    packet = torch.zeros(size, dtype=torch.uint8, device=dev)
+    for name, o, ex_bytes, _, _ in layout:
+        if n and ex_bytes:
+            packet[o:o + n * ex_bytes].copy_(arrays[name].contiguous().reshape(-1).view(torch.uint8))
+    gathered = torch.empty(world * size, dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(gathered, packet, group=group)
+    out = {}
+    for name, o, ex_bytes, dtype, tail in layout:
+        parts = [gathered[r * size + o:r * size + o + counts[r] * ex_bytes].view(dtype).view(counts[r], *tail)
+                 for r in range(world)]
+        out[name] = torch.cat(parts)
+    return out
+
+
+def decode_batch_sharded(x_local: torch.Tensor, options: DBSOptions, grad_final: Optional[torch.Tensor] = None,
+                         with_pool: bool = False, with_weights: bool = False, group=None):
+    """Batch-sharded decode: each rank decodes its own share of a global
+    batch of examples on its own GPU, then every rank holds every example's
+    results.
+
+    `x_local` is this rank's contiguous share [B_r,T,K,V] of the examples
+    (fp32 on this rank's GPU; shares follow rank order and may differ in
+    size). The share is decoded with dbs_device_decode_batch and, with
+    `grad_final` ([B_r,K]), its sparse surrogate backward runs with
+    dbs_device_backward_batch; gather_examples then gives every rank of
+    `group` the whole batch's final_scores [B,K], tokens and parents [B,T,K]
+    and, with grad_final, each example's sparse gradient: sparse_counts [B],
+    sparse_indices / sparse_values [B,T*K] (grad_final alone gives at most K
+    entries per step; entries beyond an example's count are unspecified;
+    indices are local to the example's [T*K*V]) and grad_initial [B,K].
+    Returns (the gathered dict, this rank's DeviceTrace)."""
+    B, T, K, V = (int(s) for s in x_local.shape)
+    trace = device_decode(x_local, options, with_pool=with_pool, with_weights=with_weights)
+    arrays = {"final_scores": trace.final_scores, "tokens": trace.tokens, "parents": trace.parents}
+    if grad_final is not None:
+        sp = device_backward_sparse(trace, grad_final, options, V)
+        arrays["sparse_counts"] = sp["counts"]
+        arrays["sparse_indices"] = sp["indices"][:, :T * K]
+        arrays["sparse_values"] = sp["values"][:, :T * K]
+        arrays["grad_initial"] = sp["grad_initial"]
+    return gather_examples(arrays, group), trace
+
+
+def device_backward_sparse(trace: DeviceTrace, grad_final: torch.Tensor, options: DBSOptions,
+                           V: int) -> Dict[str, torch.Tensor]:
+    """Sparse surrogate gradient of the final scores, per example, on the
+    device: counts [B] (int64), indices [B,T*(K+P)] (int64, local to the
+    example's [T*K*V], ascending) and values [B,T*(K+P)] (fp32), entries
+    beyond an example's count unspecified, and grad_initial [B,K]."""
+    B, T, K = (int(s) for s in trace.parents.shape)
+    P = max(K, K * options.relaxed_pool_multiplier)
+    cap = T * (K + P)
+    device = trace.parents.device
+    indices = torch.empty((B, cap), dtype=torch.int64, device=device)
+    values = torch.empty((B, cap), dtype=torch.float32, device=device)
+    counts = torch.empty((B,), dtype=torch.int64, device=device)
+    grad_initial = torch.empty((B, K), dtype=torch.float32, device=device)
+    g = grad_final.detach().to(device=device, dtype=torch.float32).contiguous()
+    lib = _library()
+    h = _handle(options)
+    tr = trace.struct()
+    with torch.cuda.device(device):
+        rc = lib.dbs_device_backward_batch(h, B, T, V, ctypes.byref(tr), None, None, _vp(g), None, _vp(indices),
+                                           _vp(values), _vp(counts), _vp(grad_initial), _stream_ptr(device))
+    _check(rc, h, "dbs_backward")
+    return {"counts": counts, "indices": indices, "values": values, "grad_initial": grad_initial}
+
+
 def device_backward_dense(trace: DeviceTrace, grad_final: torch.Tensor, options: DBSOptions, V: int,
                           out: Optional[torch.Tensor] = None, prezeroed: bool = False) -> torch.Tensor:
     """Dense surrogate gradient [B,T,K,V] of the final scores, on the device.
