@@ -142,3 +142,88 @@ def test_null_handles_are_safe(libdbs):
     libdbs.dbs_free_batch_result(None)
     libdbs.dbs_free_backward(None)
     libdbs.dbs_destroy(None)
+
+
+def _reference_lib():
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import reference_library_path
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+    return dc.load_library(path, device_api=False)
+
+
+def _null_out():
+    return ctypes.byref(ctypes.c_void_p())
+
+
+_X = (ctypes.c_float * 64)()
+_REJECTED_CALLS = [
+    ("null log_probs", lambda L, h: L.dbs_decode(h, None, 1, 4, _null_out())),
+    ("zero steps", lambda L, h: L.dbs_decode(h, _X, 0, 4, _null_out())),
+    ("zero vocab", lambda L, h: L.dbs_decode(h, _X, 1, 0, _null_out())),
+    ("eos outside vocab", lambda L, h: L.dbs_decode(h, _X, 2, 4, _null_out())),
+    ("null result out", lambda L, h: L.dbs_decode(h, _X, 2, 16, None)),
+    ("empty batch", lambda L, h: L.dbs_decode_batch(h, _X, 0, 1, 16, 1, _null_out())),
+    ("null batch out", lambda L, h: L.dbs_decode_batch(h, _X, 1, 1, 16, 1, None)),
+    ("backward of null result", lambda L, h: L.dbs_backward(h, None, None, None, None, _null_out())),
+    ("backward null out", lambda L, h: L.dbs_backward(h, None, None, None, None, None)),
+    ("stats to null", lambda L, h: L.dbs_get_stats(h, None)),
+    ("stats json too small", lambda L, h: L.dbs_get_stats_json(h, ctypes.create_string_buffer(4), 4)),
+    ("stats json to null", lambda L, h: L.dbs_get_stats_json(h, None, 0)),
+]
+
+
+@pytest.mark.parametrize("name,call", _REJECTED_CALLS, ids=[c[0] for c in _REJECTED_CALLS])
+def test_rejected_calls_match_the_reference(libdbs, name, call):
+    """Calls the library rejects before any device work: the same return
+    code, per-handle message and stats error category as the reference
+    library on the same call."""
+    ref = _reference_lib()
+    seen = []
+    for lib in (libdbs, ref):
+        h = ctypes.c_void_p()
+        assert lib.dbs_create_ex(dc.Options(beam_size=2, eos_token=9).to_c(), ctypes.byref(h)) == 0
+        rc = call(lib, h)
+        st = dc.DBSStatsC()
+        lib.dbs_get_stats(h, ctypes.byref(st))
+        seen.append((rc, lib.dbs_last_error(h), st.last_error_category))
+        lib.dbs_destroy(h)
+    assert seen[0] == seen[1], f"{name}: {seen[0]} here, {seen[1]} in the reference"
+
+
+@pytest.mark.parametrize("opts", [dict(beam_size=0), dict(beam_size=-3), dict(relaxed_pool_multiplier=0),
+                                  dict(selected_temperature=0.0), dict(soft_topk_temperature=-1.0),
+                                  dict(length_penalty_alpha=float("nan")), dict(soft_topk_max_iters=0),
+                                  dict(vocab_block=0), dict(max_dense_gradient_elements=0)])
+def test_option_substitution_matches_the_reference(libdbs, opts):
+    """Out-of-range options: created or refused as the reference does, with
+    its global message."""
+    ref = _reference_lib()
+    seen = []
+    for lib in (libdbs, ref):
+        h = ctypes.c_void_p()
+        rc = lib.dbs_create_ex(dc.Options(**opts).to_c(), ctypes.byref(h))
+        seen.append((rc, lib.dbs_last_global_error()))
+        if rc == 0:
+            lib.dbs_destroy(h)
+    assert seen[0] == seen[1]
+
+
+def test_stats_json_matches_the_reference_format(libdbs):
+    """dbs_get_stats_json of a fresh handle: the reference's keys, order and
+    values, the kernel name aside ("cuda" here, the reference's SIMD level
+    there)."""
+    ref = _reference_lib()
+    texts = []
+    for lib in (libdbs, ref):
+        h = ctypes.c_void_p()
+        assert lib.dbs_create_ex(dc.Options(beam_size=3, eos_token=2, length_penalty_alpha=0.4).to_c(),
+                                 ctypes.byref(h)) == 0
+        js = ctypes.create_string_buffer(4096)
+        assert lib.dbs_get_stats_json(h, js, 4096) == 0
+        texts.append(re.sub(rb'"kernel":"[a-z0-9_]+"', b'"kernel":"-"', js.value))
+        lib.dbs_destroy(h)
+    assert b'"kernel":"-"' in texts[0]
+    assert texts[0] == texts[1]
