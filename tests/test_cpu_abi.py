@@ -227,3 +227,41 @@ def test_stats_json_matches_the_reference_format(libdbs):
         lib.dbs_destroy(h)
     assert b'"kernel":"-"' in texts[0]
     assert texts[0] == texts[1]
+
+
+def _host_only_calls(L):
+    """The host-only entry points, exercised in one fixed sequence."""
+    out = [L.dbs_abi_version(), L.dbs_version_string(), L.dbs_is_deterministic(),
+           (L.dbs_has_avx512(), L.dbs_has_avx2(), L.dbs_has_sse42(), L.dbs_has_neon())]
+    w = ctypes.c_void_p()
+    out += [L.dbs_workspace_create(ctypes.byref(w)), L.dbs_workspace_allocated_bytes(w),
+            L.dbs_workspace_reserve(w, 1000, 10), L.dbs_workspace_allocated_bytes(w),
+            L.dbs_workspace_reserve(w, -1, 10), L.dbs_workspace_reserve(None, 1, 1),
+            L.dbs_workspace_allocated_bytes(None), L.dbs_workspace_create(None), L.dbs_last_global_error()]
+    L.dbs_workspace_destroy(w)
+    L.dbs_workspace_destroy(None)
+    h = ctypes.c_void_p()
+    L.dbs_create_ex(dc.Options(beam_size=2).to_c(), ctypes.byref(h))
+    out += [L.dbs_get_deterministic_seed(h), L.dbs_set_deterministic_seed(h, 42), L.dbs_get_deterministic_seed(h),
+            L.dbs_set_deterministic_seed(None, 1), L.dbs_get_deterministic_seed(None), L.dbs_last_error(None)]
+    L.dbs_reset_stats(h)
+    L.dbs_reset_stats(None)
+    L.dbs_destroy(h)
+    L.dbs_destroy(None)
+    L.dbs_allocator_counters_reset()
+    out += [L.dbs_allocator_call_count(), L.dbs_allocator_byte_count()]
+    buf = ctypes.create_string_buffer(256)
+    out += [L.dbs_validate_production_gate_manifest(b"{}", buf, 256), buf.value,
+            L.dbs_validate_production_gate_manifest(None, None, 0)]
+    old = L.dbs_create(dc.Options(beam_size=3).to_c())
+    out.append(bool(old))
+    L.dbs_destroy(old)
+    return out
+
+
+def test_host_only_entry_points_match_the_reference(libdbs):
+    """Version, capability queries, workspaces, seeds, allocator counters,
+    the deprecated manifest stub and dbs_create: the same results, codes and
+    messages as the reference library."""
+    ref = _reference_lib()
+    assert _host_only_calls(libdbs) == _host_only_calls(ref)
