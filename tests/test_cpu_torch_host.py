@@ -146,3 +146,16 @@ def test_options_match_the_reference_module(monkeypatch):
         [(f.name, f.default) for f in ref.fields(ref.DBSOptions)]
     o = dict(beam_size=5, eos_token=3, selected_temperature=0.7, relaxed_pool_multiplier=3, min_length=2)
     assert ext.DBSOptions(**o).args() == ref.DBSOptions(**o).args()
+
+
+def test_op_schemas_equal_the_reference_text():
+    """torch.ops.dbs schemas, as registered here, against the reference's
+    TORCH_LIBRARY(dbs, m) strings (tests/golden/op_schemas.json, extracted
+    by tests/golden/make_op_schemas.py)."""
+    import json
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "op_schemas.json")
+    want = json.load(open(path))["schemas"]
+    got = [str(torch.ops.dbs.final_scores_forward.default._schema),
+           str(torch.ops.dbs.final_scores_backward.default._schema)]
+    assert got == ["dbs::" + s for s in want]
