@@ -265,3 +265,20 @@ def test_host_only_entry_points_match_the_reference(libdbs):
     messages as the reference library."""
     ref = _reference_lib()
     assert _host_only_calls(libdbs) == _host_only_calls(ref)
+
+
+def test_struct_layouts_equal_the_reference_header():
+    """Every public struct's size and every field's offset and size, the
+    data-type enum, the callback pointers and the version macros, as
+    include/dbs.h declares them and as the reference's header does
+    (oracle/abi_layout.c compiled against each by oracle/Makefile)."""
+    ours = os.path.join(ROOT, "oracle", "_build", "abi_layout")
+    ref = os.path.join(ROOT, "oracle", "_ref", "abi_layout")
+    if not os.path.exists(ours):
+        pytest.skip("oracle/_build/abi_layout not built (make -C oracle)")
+    if not os.path.exists(ref):
+        pytest.skip("oracle/_ref/abi_layout not built (needs the reference source tree)")
+    a = subprocess.run([ours], capture_output=True, text=True, check=True).stdout
+    b = subprocess.run([ref], capture_output=True, text=True, check=True).stdout
+    assert "DBSOptionsC size 64" in a and a.count("\n") > 40
+    assert a == b
