@@ -282,3 +282,25 @@ def test_struct_layouts_equal_the_reference_header():
     b = subprocess.run([ref], capture_output=True, text=True, check=True).stdout
     assert "DBSOptionsC size 64" in a and a.count("\n") > 40
     assert a == b
+
+
+def test_versioned_symbols_equal_the_reference_library(libdbs):
+    """The names exported under DBS_0.6: every name the reference library
+    exports there (oracle/_ref/libdbs_ref.so, built from its source with its
+    version script), and besides them only the device extension's
+    dbs_device_* names."""
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import reference_library_path
+    path = reference_library_path()
+    if path is None:
+        pytest.skip("oracle/_ref not built")
+
+    def versioned(lib_path):
+        out = subprocess.run(["objdump", "-T", lib_path], capture_output=True, text=True, check=True).stdout
+        return {m.group(1) for m in re.finditer(r"DBS_0\.6\s+(dbs_\w+)", out)}
+
+    ours, ref = versioned(libdbs._name), versioned(path)
+    assert len(ref) == 76
+    assert ref <= ours, sorted(ref - ours)
+    assert all(n.startswith("dbs_device_") for n in ours - ref), sorted(ours - ref)
