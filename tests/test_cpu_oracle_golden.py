@@ -56,6 +56,20 @@ def test_reference_debug_unit_tests_pass():
     assert out.returncode == 0 and "dbs_tests passed" in out.stdout
 
 
+def test_reference_scalar_and_simd_paths_agree():
+    """The reference's own scalar-vs-SIMD harness (tests/simd_internal_tests.cpp):
+    the scalar path the oracle restates agrees with the SIMD kernels the
+    reference library dispatches to (the CPU baseline's kernel)."""
+    import os
+    import subprocess
+    exe = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                       "dbs_simd_parity")
+    if not os.path.exists(exe):
+        pytest.skip("reference harness not built here (no reference tree)")
+    out = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and "dbs_simd_internal_tests passed" in out.stdout, out.stdout[-2000:]
+
+
 def test_oracle_live_against_reference_random(oracle_lib):
     """Seeded random cases beyond the fixtures, against oracle/_ref directly."""
     import dbs_ctypes as dc
