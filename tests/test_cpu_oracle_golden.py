@@ -283,6 +283,69 @@ def test_model_step_restatement_matches_reference(oracle_lib, K, V, T, alpha):
     assert_decode_equal(got, want, "model steps")
 
 
+def _reference_scalar_lib():
+    """oracle/_ref/libdbs_ref_scalar.so (the reference library with a switch
+    to its scalar kernels, oracle/ref_scalar.cpp), pinned to the scalar path
+    for this thread."""
+    import ctypes
+    import os
+    import dbs_ctypes as dc
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
+                        "libdbs_ref_scalar.so")
+    if not os.path.exists(path):
+        pytest.skip("oracle/_ref/libdbs_ref_scalar.so not built (needs the reference source tree)")
+    lib = dc.load_library(path, device_api=False)
+    lib.dbs_ref_force_scalar.argtypes = [ctypes.c_int]
+    lib.dbs_ref_force_scalar.restype = None
+    lib.dbs_ref_force_scalar(1)
+    assert lib.dbs_selected_kernel_name() == b"scalar"
+    return lib
+
+
+def _assert_all_equal(got, want, label):
+    for k, v in want.items():
+        if isinstance(v, np.ndarray) and k in got:
+            assert np.array_equal(np.asarray(got[k]), v, equal_nan=v.dtype.kind == "f"), f"{label}: {k}"
+
+
+def test_oracle_bit_exact_against_the_reference_scalar_path(oracle_lib):
+    """With the reference pinned to its scalar kernels (the path the oracle
+    restates), every output is bit-exact, the selected and relaxed weights
+    included, and so is the sparse and dense backward with selected,
+    relaxed and final gradients: seeded random cases and the degenerate
+    cases. (Against the SIMD kernels the reference picks by default, weights
+    differ in the last bits; see the tolerance-based checks above.)"""
+    import dbs_ctypes as dc
+    from parity import degenerate_cases, random_case
+    ref = _reference_scalar_lib()
+    rng = np.random.default_rng(5)
+    cases = [random_case(rng) for _ in range(120)]
+    cases += [(o, x, x.shape[0], x.shape[2], c) for o, x, c in degenerate_cases()]
+    for i, (opts, x, T, V, cons) in enumerate(cases):
+        x = np.ascontiguousarray(x)
+        dec = dc.Decoder(ref, dc.Options(**opts))
+        r = dec.decode_constrained_ex(x, T, V, **cons) if cons else dec.decode(x, T, V)
+        try:
+            want = dc.read_result(ref, r)
+            fwd = oracle_lib.decode(oracle_lib.options(**opts), x, T, V, **cons)
+            _assert_all_equal(fwd, want, f"case {i}")
+            K, P = fwd["K"], fwd["P"]
+            gf = rng.standard_normal(K).astype(np.float32)
+            gs = rng.standard_normal(T * K).astype(np.float32)
+            gr = rng.standard_normal(T * P).astype(np.float32)
+            b = dec.backward(r, gs, gr, gf, mode="sparse")
+            wb = dc.read_backward(ref, b, K=K)
+            ref.dbs_free_backward(b)
+            _assert_all_equal(oracle_lib.backward_sparse(fwd, gs, gr, gf), wb, f"case {i} sparse backward")
+            b = dec.backward(r, gs, gr, gf, mode="dense")
+            wd = dc.read_backward(ref, b, dense_count=T * K * V, K=K)
+            ref.dbs_free_backward(b)
+            _assert_all_equal(oracle_lib.backward_dense(fwd, gs, gr, gf), wd, f"case {i} dense backward")
+        finally:
+            ref.dbs_free_result(r)
+            dec.close()
+
+
 def test_oracle_token_filter_matches_reference(oracle_lib):
     """The token filter: same results and the same sequence of filter calls
     (batch index, step, parent, prefix, token) as the reference library."""
